@@ -1,0 +1,510 @@
+"""Benchmark: Sinkhorn fwd+bwd throughput (cost-element-iterations per second).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg1|cfg2|cfg3|cfg4|cfg5]
+
+One step = one pass of the hot path over one batch of synthetic input of the
+chosen BASELINE configuration: for Sinkhorn, ``dot.sinkhorn(C, reg, n_iters,
+tol=0)`` followed by ``result.cost.sum().backward()``; for bidirectional
+softmax, forward + backward with an N(0,1) upstream gradient.  The default
+workload is configs[1] (cfg2: B=256, 512x512, reg 0.05, 200 iterations), the
+configuration the headline metric is quoted on.
+
+Units: one cost-element-iteration = one element of the B x n x m cost for one
+Sinkhorn iteration (fwd+bwd counted once, backward_iters = n_iters); for
+bidirectional softmax one element fwd+bwd.
+
+Timing: W untimed warm-up steps, then K steps between a barrier +
+torch.cuda.synchronize() on both sides, timed with CUDA events on the
+launching stream; the job time is the max over ranks.  Under torchrun each rank
+runs its own batch of the workload (independent problems, no collective on the
+data path): weak scaling.  ``value`` is the whole-job throughput with inputs
+resident in HBM; ``e2e`` re-times the same step from pinned host memory
+(host->device copy of the inputs and device->host read of the loss inside the
+timed region).
+
+``--impl reference`` times the reference's own CPU implementation of the path
+(its kernels_cpu.cpp compiled from source into oracle/_ref by oracle/Makefile;
+the C restatement in oracle/ if that library is absent) on all host threads,
+one bounded sample of the workload per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "Sinkhorn fwd+bwd cost-elem-iters/s per GPU; achieved HBM GB/s vs peak"
+
+CONFIGS = {
+    "cfg1": dict(kind="sinkhorn", B=8, n=64, m=64, reg=1.0, iters=100, cost="uniform", marg="uniform",
+                 desc="configs[0]: Sinkhorn fwd+bwd B=8 64x64 U[0,1) cost, reg 1.0, 100 it, uniform marginals"),
+    "cfg2": dict(kind="sinkhorn", B=256, n=512, m=512, reg=0.05, iters=200, cost="sqdist64", marg="uniform",
+                 desc="configs[1]: Sinkhorn fwd+bwd B=256 512x512 normalised sq-dist of N(0,1) 64-D clouds, "
+                      "reg 0.05, 200 it, uniform marginals"),
+    "cfg3": dict(kind="bidir", B=64, n=1024, m=1024, tau=0.1, dtype="f32",
+                 desc="configs[2]: bidirectional softmax fwd+bwd B=64 1024x1024 N(0,1) scores, tau 0.1"),
+    "cfg4": dict(kind="sinkhorn", B=4096, n=128, m=128, reg=0.1, iters=100, cost="uniform", marg="dirichlet",
+                 desc="configs[3]: Sinkhorn fwd+bwd B=4096 128x128 U[0,1) cost, Dirichlet(1) marginals, "
+                      "reg 0.1, 100 it"),
+    "cfg5": dict(kind="sinkhorn_fwd", B=1, n=32768, m=32768, reg=0.01, iters=500, cost="sqdist3u",
+                 marg="uniform", desc="configs[4]: Sinkhorn fwd B=1 32768x32768 sq-dist of U[0,1)^3 clouds, "
+                                      "reg 0.01, 500 it"),
+}
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# inputs
+# ---------------------------------------------------------------------------
+
+def make_inputs(cfg: dict, seed: int):
+    import torch
+
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    B, n, m = cfg["B"], cfg["n"], cfg["m"]
+    if cfg["kind"] == "bidir":
+        S = torch.randn(B, n, m, generator=g)
+        if cfg.get("dtype") == "bf16":
+            S = S.bfloat16()
+        return {"S": S, "G": torch.randn(B, n, m, generator=g)}
+    if cfg["cost"] == "uniform":
+        C = torch.rand(B, n, m, generator=g)
+    elif cfg["cost"] == "sqdist64":
+        x = torch.randn(B, n, 64, generator=g)
+        y = torch.randn(B, m, 64, generator=g)
+        C = torch.cdist(x, y).square()
+        C = C / C.amax(dim=(1, 2), keepdim=True)
+    elif cfg["cost"] == "sqdist3u":
+        x = torch.rand(B, n, 3, generator=g)
+        y = torch.rand(B, m, 3, generator=g)
+        C = torch.cdist(x, y).square()
+    else:
+        raise ValueError(cfg["cost"])
+    out = {"C": C.float().contiguous()}
+    if cfg["marg"] == "dirichlet":
+        torch.manual_seed(seed)
+        d = torch.distributions.Dirichlet(torch.ones(n))
+        out["a"] = d.sample((B,)).float()
+        out["b"] = torch.distributions.Dirichlet(torch.ones(m)).sample((B,)).float()
+    return out
+
+
+def units_per_step(cfg: dict) -> int:
+    if cfg["kind"] == "bidir":
+        return cfg["B"] * cfg["n"] * cfg["m"]
+    return cfg["B"] * cfg["n"] * cfg["m"] * cfg["iters"]
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 9:
+                    rows.append(p)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, cfg: dict) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import dot
+    from dot_b200 import _lib
+
+    rank, local_rank, world = env_rank()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    inputs = make_inputs(cfg, seed=1234 + rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    if cfg["kind"] == "bidir":
+        S_host = inputs["S"].pin_memory()
+        G_host = inputs["G"].pin_memory()
+        S_dev = S_host.to(dev)
+        G_dev = G_host.to(dev)
+
+        def step(S, G):
+            s = S.detach().requires_grad_(True)
+            out = dot.bidirectional_softmax(s, tau=cfg["tau"])
+            out.backward(G)
+            return out
+
+        def step_e2e():
+            S = S_host.to(dev, non_blocking=True)
+            G = G_host.to(dev, non_blocking=True)
+            out = step(S, G)
+            return out.sum()
+
+        step_dev = lambda: step(S_dev, G_dev)  # noqa: E731
+        h2d = S_host.numel() * S_host.element_size() + G_host.numel() * 4
+    else:
+        C_host = inputs["C"].pin_memory()
+        C_dev = C_host.to(dev)
+        a = inputs.get("a")
+        b = inputs.get("b")
+        a_dev = None if a is None else a.to(dev)
+        b_dev = None if b is None else b.to(dev)
+        fwd_only = cfg["kind"] == "sinkhorn_fwd"
+
+        def step(C):
+            Cg = C if fwd_only else C.detach().requires_grad_(True)
+            res = dot.sinkhorn(Cg, reg=cfg["reg"], n_iters=cfg["iters"], a=a_dev, b=b_dev, tol=0)
+            loss = res.cost.sum()
+            if not fwd_only:
+                loss.backward()
+            return loss
+
+        def step_e2e():
+            C = C_host.to(dev, non_blocking=True)
+            return step(C)
+
+        step_dev = lambda: step(C_dev)  # noqa: E731
+        h2d = C_host.numel() * 4
+
+    for _ in range(args.warmup):
+        step_dev()
+    torch.cuda.synchronize()
+
+    # ---- timed region (device-resident inputs) ----
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    _lib.prof_begin(time_events=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step_dev()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    prof = _lib.prof_end()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    t_local = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    ms_max = float(t_local.item())
+
+    # ---- timed region (end to end from pinned host memory) ----
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        loss = step_e2e()
+        loss.item()  # device -> host read of the step's result
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t_e2e = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t_e2e.item())
+
+    units = units_per_step(cfg)
+    value = units * world * args.steps / (ms_max / 1e3)
+    e2e_value = units * world * args.steps / (ms_e2e / 1e3)
+    launches = sum(v["launches"] for v in prof.values())
+
+    if rank == 0:
+        peaks = measured_peaks()
+        roof = roofline(cfg, prof, peaks)
+        line = {
+            "metric": METRIC if cfg["kind"] != "bidir" else "bidirectional softmax fwd+bwd elements/s",
+            "value": value,
+            "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32" if cfg.get("dtype", "f32") == "f32" else "bf16-in/f32",
+            "data": "synthetic (seeded; shapes and distributions of the BASELINE config)",
+            "config": {"workload": cfg["desc"], **{k: cfg[k] for k in ("B", "n", "m") if k in cfg},
+                       **({"reg": cfg["reg"], "n_iters": cfg["iters"], "backward_iters": cfg["iters"],
+                           "tol": 0} if cfg["kind"] != "bidir" else {"tau": cfg["tau"]}),
+                       "per_rank_batch": cfg["B"],
+                       "l2": "inputs larger than L2 (126 MB)" if units_per_step(cfg) // max(cfg.get("iters", 1), 1) * 4
+                       > 126e6 else "small working set: L2-resident by design (on-chip solver)",
+                       "parallelism": f"batch-independent x{world} (no collective)"},
+            "e2e": {"value": e2e_value, "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
+                    "ms_per_step": ms_e2e / args.steps},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "kernels": {k: v for k, v in prof.items() if v["launches"]},
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, sample_seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def roofline(cfg: dict, prof: dict, peaks: dict) -> dict:
+    """Dominant kernel class: algorithmic bytes per launch / measured launch time.
+
+    Sinkhorn sweep kernels (row pass, column pass, adjoint row/column mat-vecs)
+    each stream the B x n x m fp32 matrix once: 4 B per element per launch;
+    forward + backward = 4 launches per iteration = 16 B per cost-element-
+    iteration (the survey's sweep model: 8 B/unit forward + 8 B/unit backward).
+    """
+    B, n, m = cfg["B"], cfg["n"], cfg["m"]
+    elems = B * n * m
+    cands = []
+    for k, v in prof.items():
+        if v["launches"] and v["ms"] > 0:
+            cands.append((v["ms"], k, v))
+    if not cands:
+        return {"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": None,
+                "traffic": None}
+    cands.sort(reverse=True)
+    ms, k, v = cands[0]
+    avg_ms = v["ms"] / v["launches"]
+    if k in ("sk_fwd_iter", "sk_bwd_iter"):
+        # per iteration: row launch + column launch (+ a merge launch, which moves
+        # no matrix bytes, when n spans several 512-row column chunks)
+        per_iter = 3 if n > 1024 else 2
+        sweeps = v["launches"] * 2 // per_iter
+        total_bytes = 4 * elems * sweeps
+    elif k in ("bs_fwd", "bs_bwd"):
+        per = 4 if cfg.get("dtype", "f32") == "f32" else 2
+        total_bytes = ((per + 4) if k == "bs_fwd" else (per + 4 + 4)) * elems
+    else:
+        total_bytes = 8 * elems * v["launches"]
+    achieved = total_bytes / (v["ms"] / 1e3) / 1e9
+    peak = peaks["hbm_gbs"]
+    return {"bound": "hbm", "kernel_class": k, "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
+            "launches": v["launches"], "traffic": traffic_from_profiles(k)}
+
+
+def traffic_from_profiles(kclass: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            p = line.split()
+            if len(p) >= 2 and p[0] == kclass:
+                return float(p[1])
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm
+# ---------------------------------------------------------------------------
+
+def cpu_sample(cfg: dict, problems: int, threads: int, kind: str, seed: int = 99):
+    """Time the reference CPU implementation on ``problems`` problems of the
+    workload, ``threads`` at a time.  Returns (units/s, seconds, units)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    sub = dict(cfg)
+    sub["B"] = problems
+    inp = make_inputs(sub, seed)
+    if cfg["kind"] == "bidir":
+        S = inp["S"].float().numpy()
+        G = inp["G"].numpy()
+        lengths = np.tile(np.array([[cfg["n"], cfg["m"]]], np.int32), (problems, 1))
+        from concurrent.futures import ThreadPoolExecutor
+
+        def work(i):
+            out, rs, cs = O.bidir_forward(S[i:i + 1], cfg["tau"], lengths[i:i + 1], kind=kind)
+            O.bidir_backward(S[i:i + 1], out, G[i:i + 1], rs, cs, cfg["tau"], lengths[i:i + 1], kind=kind)
+
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(work, range(problems)))
+        dt = time.perf_counter() - t0
+        units = problems * cfg["n"] * cfg["m"]
+        return units / dt, dt, units
+    C = inp["C"].numpy()
+    a = None if "a" not in inp else inp["a"].numpy()
+    b = None if "b" not in inp else inp["b"].numpy()
+    t0 = time.perf_counter()
+    O.sinkhorn_fwd_bwd_threaded(C, cfg["reg"], cfg["iters"], a, b, threads=threads, kind=kind)
+    dt = time.perf_counter() - t0
+    units = problems * cfg["n"] * cfg["m"] * cfg["iters"]
+    return units / dt, dt, units
+
+
+def cpu_kind() -> str:
+    from oracle import oracle as O
+
+    return "reference" if O.available("reference") else "restated"
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def sample_problems(cfg: dict, threads: int, seconds: float) -> int:
+    """Problems per CPU sample: about `seconds` of CPU work, at least one per thread."""
+    per_problem = {"cfg1": 0.011, "cfg2": 1.7, "cfg3": 0.12, "cfg4": 0.046, "cfg5": 1e9}
+    est = per_problem.get(cfg.get("name", ""), 1.0)
+    p = max(threads, int(seconds / est))
+    p = (p // threads) * threads if p >= threads else threads
+    return max(1, min(p, cfg["B"]))
+
+
+def cpu_baseline(cfg: dict, sample_seconds: float = 15.0) -> dict:
+    if cfg["kind"] == "sinkhorn_fwd":
+        return {"value": None, "unit": "cost-elem-iters/s", "cores": 1, "kind": "reference",
+                "sample": "not run: one iteration of the 32768^2 problem takes minutes on one core"}
+    kind = cpu_kind()
+    threads = cpu_threads()
+    problems = sample_problems(cfg, threads, sample_seconds)
+    v, dt, units = cpu_sample(cfg, problems, threads, kind)
+    return {"value": v, "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
+            "cores": threads, "kind": "reference" if kind == "reference" else "port",
+            "sample": f"{problems} of {cfg['B']} problems of the workload, full size and iterations, "
+                      f"{threads} threads (one problem per thread at a time), {dt:.1f} s wall; the reference's "
+                      "CPU fwd op, then its backward op (which re-runs the forward)"}
+
+
+def run_reference(args, cfg: dict) -> None:
+    rank, _, world = env_rank()
+    if rank != 0:
+        return
+    kind = cpu_kind()
+    threads = cpu_threads()
+    if cfg["kind"] == "sinkhorn_fwd":
+        print(json.dumps({"impl": "reference", "unavailable": "cfg5 on the host CPU takes ~16 h per step"}))
+        return
+    problems = sample_problems(cfg, threads, args.cpu_seconds)
+    for _ in range(args.warmup):
+        cpu_sample(cfg, threads, threads, kind)
+    vals, secs = [], []
+    for _ in range(args.steps):
+        v, dt, _ = cpu_sample(cfg, problems, threads, kind)
+        vals.append(v)
+        secs.append(dt)
+    value = statistics.median(vals)
+    unit = "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s"
+    sample = (f"{problems} of {cfg['B']} problems per step at full size and iterations, {threads} host threads, "
+              f"reference CPU kernels ({'oracle/_ref, compiled from the reference sources' if kind == 'reference' else 'oracle restatement'})")
+    line = {
+        "impl": "reference",
+        "metric": METRIC if cfg["kind"] != "bidir" else "bidirectional softmax fwd+bwd elements/s",
+        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * statistics.median(secs), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; shapes of the BASELINE config)",
+        "config": {"workload": cfg["desc"], "B": cfg["B"], "n": cfg["n"], "m": cfg["m"]},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads,
+                         "kind": "reference" if kind == "reference" else "port", "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work per baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    cfg["name"] = args.config
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

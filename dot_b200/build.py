@@ -1,0 +1,61 @@
+"""Build the dot_b200 C-ABI library for sm_100a with nvcc (in-tree).
+
+``python -m dot_b200.build`` compiles every ``csrc/*.cu`` into
+``dot_b200/_lib/libdot_b200.so`` with
+``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3``.  The CUDA runtime is
+linked statically so the library carries no dependency beyond the driver.
+The build is skipped when the library is newer than every source.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_DIR = os.path.join(HERE, "_lib")
+LIB = os.path.join(LIB_DIR, "libdot_b200.so")
+ARCH = "-gencode=arch=compute_100a,code=sm_100a"
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found; set NVCC or put the CUDA toolkit on PATH")
+
+
+def sources() -> list[str]:
+    return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")))
+
+
+def _stale() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    deps = sources() + glob.glob(os.path.join(HERE, "csrc", "*.h")) + glob.glob(
+        os.path.join(HERE, "csrc", "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not _stale():
+        return LIB
+    os.makedirs(LIB_DIR, exist_ok=True)
+    tmp = LIB + ".tmp"
+    cmd = [_nvcc(), ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+           "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", "-cudart", "static",
+           "-I" + os.path.join(ROOT, "include"), "-o", tmp] + sources()
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,112 @@
+// Shared device helpers for the dot_b200 kernels (sm_100a).
+//
+// Arithmetic conventions shared with the reference (caseysm/dot):
+//  * Sinkhorn works in the log domain, in natural-log units, with the
+//    reference's operation order: K = X * (sign/tau) rounded to fp32 (the
+//    reference materialises log_K = log_alpha * inv_tau, src/sinkhorn/
+//    kernels.cu:128-139,1338-1353), then t = K + v rounded, max over the
+//    reduced axis, sum of exp(t - max).  Only the exponential of the
+//    (non-positive) shifted difference goes through base 2: exp(d) =
+//    2^(d*log2 e) on the SFU (ex2.approx); its argument error is |d|*2^-24,
+//    so the terms that dominate a sum (small |d|) are accurate to a few ulp.
+//  * exp clamp: the reference's safe_exp returns 0 below -88 and caps the
+//    argument at +88 (src/sinkhorn/kernels.cu:21-25).
+//  * log floor: log(max(sum, 1e-12)) on every log-sum-exp
+//    (src/sinkhorn/kernels.cu:538,620).
+//  * empty max: -FLT_MAX, as the reference's reductions start from it.
+#pragma once
+
+#include <cfloat>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dotb {
+
+constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
+constexpr float kSumFloor = 1.0e-12f;
+constexpr float kNegBig = -FLT_MAX;
+
+// 2^x on the SFU (ex2.approx, subnormal results flushed to zero).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// exp(d) for a shifted difference d <= 0 inside a log-sum-exp.
+__device__ __forceinline__ float exp_shift(float d) { return ex2(d * kLog2e); }
+
+// The reference's safe_exp (accurate expf, 0 below -88, argument capped at 88),
+// used where a value is written out (the plan).
+__device__ __forceinline__ float safe_expf(float x) {
+    if (x < -88.0f) return 0.0f;
+    return expf(fminf(x, 88.0f));
+}
+
+// log of a log-sum-exp partial (max m, sum s of exp(x - m)) with the 1e-12 floor.
+__device__ __forceinline__ float lse_finish(float m, float s) {
+    return m + logf(fmaxf(s, kSumFloor));
+}
+
+// Merge two (max, sum) log-sum-exp partials.
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+    float mn = fmaxf(m, m2);
+    s = s * exp_shift(m - mn) + s2 * exp_shift(m2 - mn);
+    m = mn;
+}
+
+template <int W>
+__device__ __forceinline__ void warp_lse(float& m, float& s) {
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1) {
+        float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+        float s2 = __shfl_xor_sync(0xffffffffu, s, off);
+        lse_merge(m, s, m2, s2);
+    }
+}
+
+template <int W>
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+template <int W>
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int off = W / 2; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// Online update of a (max, sum) partial with a group of K new values
+// (-INFINITY marks an empty slot).
+template <int K>
+__device__ __forceinline__ void lse_push(float& m, float& s, const float (&t)[K]) {
+    float gm = t[0];
+#pragma unroll
+    for (int k = 1; k < K; ++k) gm = fmaxf(gm, t[k]);
+    if (gm > m) {
+        s *= exp_shift(m - gm);
+        m = gm;
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) s += exp_shift(t[k] - m);
+}
+
+// K_ij + w: the scaled kernel entry (rounded, as the reference stores log_K)
+// plus a potential, without FMA contraction.
+__device__ __forceinline__ float kplus(float x, float kinv, float w) {
+    return __fadd_rn(__fmul_rn(x, kinv), w);
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// float <-> order-preserving uint for atomicMax on non-negative floats.
+__device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
+    atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+}  // namespace dotb

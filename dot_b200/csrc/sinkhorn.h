@@ -1,0 +1,61 @@
+// Internal interface between the C-ABI layer (capi.cu) and the Sinkhorn
+// kernel families (streaming: sinkhorn_stream.cu, on-chip resident:
+// sinkhorn_resident.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dotb {
+
+struct SkFwdArgs {
+    const float* X;
+    float kinv;        // sign * (1/tau): K = X * kinv
+    float sign;
+    float tau;
+    const float* la;   // natural-log marginals [B,n] / [B,m] or nullptr (uniform)
+    const float* lb;
+    float la_def;      // -log(n), -log(m) in fp32
+    float lb_def;
+    int64_t B, n, m;
+    int n_iters;
+    float tol;
+    int out_mode;      // 0 plan, 1 log-plan
+    float* out;
+    float* cost;       // nullptr = not requested
+    float* u2;         // [B,n] dual potentials u, v (natural log; output)
+    float* v2;         // [B,m]
+    int32_t* status;   // device int32[4]
+};
+
+struct SkBwdArgs {
+    const float* X;
+    float sign;
+    float tau;
+    const float* P;
+    const float* u2;   // may be nullptr
+    const float* v2;
+    const float* gP;   // may be nullptr
+    const float* gcost;
+    int64_t B, n, m;
+    int bwd_iters;
+    float* gX;
+    float* gtau;       // may be nullptr
+};
+
+size_t sk_stream_fwd_ws(int64_t B, int64_t n, int64_t m, int n_iters, float tol, bool want_cost);
+int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
+size_t sk_stream_bwd_ws(int64_t B, int64_t n, int64_t m);
+int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
+
+// On-chip resident solvers (one CTA per problem).  *_supported() tells whether
+// a shape has a resident configuration; the entry points then need the same
+// workspace as reported by *_ws().
+bool sk_resident_supported(int64_t n, int64_t m);
+size_t sk_resident_fwd_ws(int64_t B, int64_t n, int64_t m, bool want_cost);
+int sk_resident_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
+size_t sk_resident_bwd_ws(int64_t B, int64_t n, int64_t m);
+int sk_resident_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
+
+}  // namespace dotb

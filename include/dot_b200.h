@@ -1,0 +1,190 @@
+/*
+ * dot_b200 C-ABI: the drop-in boundary for dot's two operator hot paths on
+ * NVIDIA B200 (sm_100a).
+ *
+ * Every entry point is extern "C", takes plain device pointers, int64 shapes,
+ * float parameters and a cudaStream_t passed as void*, and returns an int
+ * status (DOT_OK = 0, negative on error; dot_last_error() gives the text of
+ * the calling thread's last error).  Kernels are enqueued on the given stream
+ * and the calls return without synchronising.  No entry point allocates device
+ * memory: scratch space is passed in as `workspace`, sized by the matching
+ * *_workspace_bytes() query (callers allocate it, e.g. from torch's caching
+ * allocator).  All tensors are dense, row-major, contiguous.
+ *
+ * Each function names the reference interface it replaces (paths relative to
+ * the caseysm/dot project root).  The reference exposes its ops through
+ * TORCH_LIBRARY schemas; this boundary carries the same arguments as raw
+ * pointers, folds the cost negation (log_alpha = -C) into a sign argument,
+ * and returns the dual potentials so the backward pass need not re-run the
+ * forward (the reference re-runs it, src/sinkhorn/torch_cuda.cpp:842-853).
+ */
+#ifndef DOT_B200_H_
+#define DOT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DOT_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DOT_API __attribute__((visibility("default")))
+#else
+#define DOT_API
+#endif
+
+enum dot_status {
+    DOT_OK = 0,
+    DOT_ERR_INVALID = -1,     /* bad argument (shape, pointer, parameter)      */
+    DOT_ERR_CUDA = -2,        /* a CUDA runtime call or kernel launch failed    */
+    DOT_ERR_WORKSPACE = -3,   /* workspace missing or smaller than required     */
+    DOT_ERR_UNSUPPORTED = -4  /* valid request this build does not implement    */
+};
+
+enum dot_dtype { DOT_F32 = 0, DOT_BF16 = 1, DOT_F16 = 2 };
+
+/* Text of the calling thread's last error ("" if none). */
+DOT_API const char* dot_last_error(void);
+
+/* DOT_B200_ABI_VERSION of the loaded library. */
+DOT_API int dot_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Sinkhorn (log-domain, dual potentials)                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of workspace dot_sinkhorn_fwd needs for this problem. */
+DOT_API size_t dot_sinkhorn_fwd_workspace_bytes(int64_t B, int64_t n, int64_t m, int n_iters,
+                                        float tol, int want_cost);
+
+/*
+ * Sinkhorn forward on X [B,n,m]: K = score_sign * X / tau (score_sign = -1
+ * when X is a cost matrix, +1 when X holds log-scores log_alpha).  Starting
+ * from u = v = 0, each iteration sets
+ *     u_i = log_a_i - LSE_j(K_ij + v_j),   then   v_j = log_b_j - LSE_i(K_ij + u_i),
+ * for n_iters iterations, or, when tol > 0, until the first iteration whose
+ * max_i |u_i - u_i(prev)| over the whole batch is below tol.  Then
+ *     out = exp(K + u_i + v_j)   (out_mode 0, exp clamped as the reference's
+ *                                 safe_exp)   or   K + u_i + v_j  (out_mode 1),
+ * and, if cost != NULL, cost_b = sum_ij out_ij * X_ij (out_mode 0 only).
+ *
+ * log_a [B,n], log_b [B,m]: natural-log marginals; NULL = uniform (-log n,
+ * -log m).  pot_u [B,n], pot_v [B,m]: receive the final dual potentials u, v
+ * (natural log, as the reference's log_u / log_v); pass them to
+ * dot_sinkhorn_bwd.
+ * status (device int32[4]): {n_iters_used, converged, -, -}, written on the
+ * stream.
+ *
+ * Replaces: sinkhorn_dual_forward (src/sinkhorn/registry.cpp:38-45,
+ * CUDA impl src/sinkhorn/torch_cuda.cpp:266-557, vanilla method :147-264),
+ * sinkhorn and sinkhorn_log (registry.cpp:31,34; torch_cuda.cpp:599-715),
+ * plus the Python-side cost reduction (P*C).sum (dot/sinkhorn.py:1703).
+ */
+DOT_API int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_a,
+                     const float* log_b, int64_t B, int64_t n, int64_t m, float tau,
+                     int n_iters, float tol, int out_mode, float* out, float* cost,
+                     float* pot_u, float* pot_v, int32_t* status, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace dot_sinkhorn_bwd needs for this problem. */
+DOT_API size_t dot_sinkhorn_bwd_workspace_bytes(int64_t B, int64_t n, int64_t m, int bwd_iters);
+
+/*
+ * Implicit-function backward of dot_sinkhorn_fwd for the loss
+ *     L = sum_b grad_cost_b * cost_b + sum_ij grad_P_ij * P_ij,
+ * i.e. G = grad_P + grad_cost_b * X.  Runs bwd_iters Gauss-Seidel sweeps of
+ *     lambda_i = (sum_k P_ik G_ik - sum_k P_ik mu_k) / max(sum_k P_ik, 1e-12)
+ *     mu_k     = (sum_i P_ik G_ik - sum_i P_ik lambda_i) / max(sum_i P_ik, 1e-12)
+ * from lambda = mu = 0, then with g = P (G - lambda_i - mu_k) / tau (the
+ * gradient with respect to log_alpha = score_sign * X):
+ *     grad_X   = score_sign * g + grad_cost_b * P
+ *     grad_tau_b = -sum_ij g_ij * log_alpha_ij / tau          (if grad_tau)
+ * P is the forward plan (out_mode 0); pot_u / pot_v are the forward's
+ * potentials (may be NULL).  grad_P [B,n,m] and grad_cost [B] may be NULL
+ * (zero).
+ *
+ * Replaces: sinkhorn_with_grads_implicit (src/sinkhorn/registry.cpp:56; CUDA
+ * impl src/sinkhorn/torch_cuda.cpp:803-871, kernels.cu:965-1098,1682-1726)
+ * together with the autograd terms of the Python cost (dot/sinkhorn.py:1703)
+ * and the negation log_alpha = -C (dot/sinkhorn.py:1346).
+ */
+DOT_API int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P,
+                     const float* pot_u, const float* pot_v, const float* grad_P,
+                     const float* grad_cost, int64_t B, int64_t n, int64_t m, float tau,
+                     int bwd_iters, float* grad_X, float* grad_tau, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Bidirectional softmax                                                     */
+/* ------------------------------------------------------------------------ */
+
+DOT_API size_t dot_bidir_fwd_workspace_bytes(int64_t B, int64_t L1, int64_t L2);
+
+/*
+ * out_ij = sqrt(1e-9 + softmax_j(sim_i. / tau)_ij * softmax_i(sim_.j / tau)_ij)
+ * inside each batch's window i < lengths[b,0], j < lengths[b,1] (softmaxes
+ * taken over the window), and 0 outside.  sim [B,L1,L2] is DOT_F32 or
+ * DOT_BF16 (read natively, computed in fp32); lengths is a device int32
+ * [B,2].  row_stats [B,L1,2] and col_stats [B,L2,2] receive (max, 1/sum) of
+ * the row and column softmaxes; the backward recomputes both softmaxes from
+ * them instead of storing two full-size buffers.
+ *
+ * Replaces: bidirectional_softmax (src/bidirectional_softmax/registry.cpp:31;
+ * CUDA impl torch_cuda.cpp:42-76, kernels.cu:90-242,417-448).
+ */
+DOT_API int dot_bidir_fwd(const void* sim, int sim_dtype, const int32_t* lengths, int64_t B,
+                  int64_t L1, int64_t L2, float tau, float* out, float* row_stats,
+                  float* col_stats, void* workspace, size_t workspace_bytes, void* stream);
+
+DOT_API size_t dot_bidir_bwd_workspace_bytes(int64_t B, int64_t L1, int64_t L2);
+
+/*
+ * Backward of dot_bidir_fwd for upstream grad_out [B,L1,L2] (fp32):
+ *     d = grad_out * 0.5 / out (where out > 1e-9), d_row = d * col, d_col = d * row
+ *     grad_sim = (d_row - sum_j d_row*row) * row / tau + (d_col - sum_i d_col*col) * col / tau
+ * inside the window (0 outside); grad_sim is written as grad_dtype (DOT_F32 or
+ * DOT_BF16, rounded to nearest even).  grad_tau_b = -sum grad_sim * sim / tau
+ * over the window (if grad_tau != NULL).
+ *
+ * Replaces: bidirectional_softmax_backward (src/bidirectional_softmax/
+ * registry.cpp:34; CUDA impl torch_cuda.cpp:78-143, kernels.cu:249-411,450-501).
+ */
+DOT_API int dot_bidir_bwd(const void* sim, int sim_dtype, const int32_t* lengths, int64_t B,
+                  int64_t L1, int64_t L2, float tau, const float* row_stats,
+                  const float* col_stats, const float* grad_out, void* grad_sim,
+                  int grad_dtype, float* grad_tau, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Instrumentation (no counterpart in the reference)                         */
+/* ------------------------------------------------------------------------ */
+
+/* Kernel classes counted and (optionally) timed by the library. */
+enum dot_kclass {
+    DOT_K_SK_FWD_ITER = 0,   /* Sinkhorn forward iteration kernels          */
+    DOT_K_SK_FWD_EPI = 1,    /* plan / cost epilogue                         */
+    DOT_K_SK_BWD_ITER = 2,   /* adjoint iteration kernels                    */
+    DOT_K_SK_BWD_EPI = 3,    /* adjoint setup and gradient epilogue          */
+    DOT_K_SK_RESIDENT = 4,   /* on-chip resident solver kernels              */
+    DOT_K_BS_FWD = 5,        /* bidirectional softmax forward                */
+    DOT_K_BS_BWD = 6,        /* bidirectional softmax backward               */
+    DOT_K_NCLASS = 7
+};
+
+/* Start counting launches per class; with time_events != 0 also bracket each
+ * launch with CUDA events on its stream. */
+DOT_API int dot_prof_begin(int time_events);
+
+/* Stop; per class write launch counts and (if timed) summed kernel time in
+ * milliseconds (arrays of DOT_K_NCLASS entries; either may be NULL).
+ * Synchronises the recorded events. */
+DOT_API int dot_prof_end(int64_t* launches, double* ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DOT_B200_H_ */

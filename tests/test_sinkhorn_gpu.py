@@ -1,0 +1,355 @@
+"""Sinkhorn on the GPU through the public API / C-ABI, checked against the
+reference's golden vectors and the CPU oracle (oracle/), plus size-independent
+properties at the BASELINE configurations' full sizes.
+
+Tolerances (north star): plan normwise rel 1e-5 per batch element, cost rel
+1e-5, gradients normwise rel 1e-4 (tests/util.py).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import dot
+from dot_b200 import ops
+from oracle import oracle as O
+from tests import util as U
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def run_api(C, reg, n_iters, a=None, b=None, backward_iters=None, cost_weight=None, plan_weight=None,
+            reg_tensor=False, tol=0.0):
+    Cg = torch.as_tensor(C).to(DEV).clone().requires_grad_(True)
+    r = torch.tensor(float(reg), device=DEV, requires_grad=True) if reg_tensor else float(reg)
+    kw = {}
+    if backward_iters is not None:
+        kw["backward_iters"] = backward_iters
+    res = dot.sinkhorn(Cg, reg=r, n_iters=n_iters, a=None if a is None else torch.as_tensor(a).to(DEV),
+                       b=None if b is None else torch.as_tensor(b).to(DEV), tol=tol, **kw)
+    cw = torch.ones_like(res.cost) if cost_weight is None else torch.as_tensor(cost_weight).to(DEV)
+    loss = (res.cost * cw).sum()
+    if plan_weight is not None:
+        loss = loss + (res.transport_plan * torch.as_tensor(plan_weight).to(DEV)).sum()
+    loss.backward()
+    out = dict(P=res.transport_plan.detach().cpu().numpy(), cost=res.cost.detach().cpu().numpy(),
+               dC=Cg.grad.cpu().numpy(), res=res)
+    if reg_tensor:
+        out["dreg"] = float(r.grad.item())
+    return out
+
+
+# ---------------------------------------------------------------------------
+# parity: reference golden vectors (produced by the reference's own API)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("path", U.golden_files("sinkhorn_"), ids=lambda p: p.split("/")[-1])
+def test_golden_sinkhorn(path):
+    d = U.load(path)
+    r = run_api(d["C"], float(d["reg"]), int(d["n_iters"]), d.get("a"), d.get("b"),
+                backward_iters=int(d["backward_iters"]) if "backward_iters" in d else None,
+                cost_weight=d["cost_weight"], plan_weight=d.get("plan_weight"), reg_tensor="dreg" in d)
+    U.assert_normwise(r["P"], d["P"], U.PLAN_RTOL, "plan")
+    U.assert_rel(r["cost"], d["cost"], U.COST_RTOL, "cost", atol=1e-9)
+    U.assert_normwise(r["dC"], d["dC"], U.GRAD_RTOL, "dC")
+    if "dreg" in d:
+        assert r["dreg"] == pytest.approx(float(d["dreg"]), rel=U.GRAD_RTOL, abs=1e-7)
+    assert r["res"].n_iters_used == int(d["n_iters"])
+    assert r["res"].converged
+
+
+def test_golden_scores():
+    d = U.load(U.golden_files("scores_")[0])
+    la = torch.from_numpy(d["log_alpha"]).to(DEV).requires_grad_(True)
+    P = dot.sinkhorn_from_scores(la, tau=float(d["tau"]), n_iters=int(d["n_iters"]), tol=0)
+    (P * torch.from_numpy(d["plan_weight"]).to(DEV)).sum().backward()
+    U.assert_normwise(P, d["P"], U.PLAN_RTOL, "plan")
+    U.assert_normwise(la.grad, d["dlog_alpha"], U.GRAD_RTOL, "dlog_alpha")
+    logP = dot.sinkhorn_from_scores(torch.from_numpy(d["log_alpha"]).to(DEV), tau=float(d["tau"]),
+                                    n_iters=int(d["n_iters"]), return_log=True, tol=0)
+    assert logP.grad_fn is None
+    # log-plan: absolute error relative to the spread of log P
+    err = np.abs(U.to_np(logP) - d["logP"]).max()
+    assert err <= 1e-5 * np.abs(d["logP"]).max()
+
+
+# ---------------------------------------------------------------------------
+# parity: CPU oracle on seeded inputs, shapes covering every kernel path
+# ---------------------------------------------------------------------------
+
+SHAPES = [
+    # (B, n, m, reg, T, marginals)
+    (3, 1, 1, 0.5, 3, False),
+    (2, 1, 9, 0.5, 4, False),
+    (2, 9, 1, 0.5, 4, True),
+    (4, 17, 33, 0.2, 30, True),
+    (2, 6, 9, 0.7, 75, True),
+    (2, 64, 64, 1.0, 100, False),       # cfg1 shape
+    (3, 128, 128, 0.1, 40, True),       # cfg4 shape
+    (2, 129, 127, 0.1, 25, False),      # ragged, not a multiple of 4
+    (1, 96, 128, 0.1, 50, False),
+    (1, 300, 1030, 0.2, 10, False),     # wide
+    (1, 1300, 37, 0.1, 12, True),       # tall: column pass spans several row chunks
+    (2, 256, 256, 0.05, 20, False),
+]
+
+
+@pytest.mark.parametrize("B,n,m,reg,T,marg", SHAPES, ids=lambda v: str(v))
+def test_oracle_parity_random(B, n, m, reg, T, marg):
+    g = U.gen(1000 * n + m)
+    C = torch.rand(B, n, m, generator=g)
+    a = b = None
+    if marg:
+        a = U.dirichlet(B, n, 7) + 1e-3
+        a = a / a.sum(-1, keepdim=True)
+        b = U.dirichlet(B, m, 8) + 1e-3
+        b = b / b.sum(-1, keepdim=True)
+    W = torch.randn(B, n, m, generator=g)
+    cw = torch.randn(B, generator=g)
+    ref = O.sinkhorn_api(C.numpy(), reg, T, None if a is None else a.numpy(), None if b is None else b.numpy(),
+                         g_cost=cw.numpy(), grad_P=W.numpy(), bwd_tol=0.0)
+    r = run_api(C, reg, T, a, b, cost_weight=cw, plan_weight=W, reg_tensor=True)
+    U.assert_normwise(r["P"], ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_rel(r["cost"], ref["cost"], U.COST_RTOL, "cost", atol=1e-9)
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
+    assert r["dreg"] == pytest.approx(float(ref["dreg"]), rel=U.GRAD_RTOL, abs=1e-6)
+
+
+def test_return_log_and_low_level_ops_match_oracle():
+    g = U.gen(5)
+    la = torch.randn(2, 20, 30, generator=g)
+    tau, T = 0.3, 40
+    ref_p = O.sinkhorn_forward(la.numpy(), tau, T)
+    ref_lp = O.sinkhorn_forward(la.numpy(), tau, T, return_log=True)
+    P = dot._ops.sinkhorn(la.to(DEV), tau, T)
+    LP = dot._ops.sinkhorn_log(la.to(DEV), tau, T)
+    U.assert_normwise(P, ref_p, U.PLAN_RTOL, "plan")
+    assert np.abs(U.to_np(LP) - ref_lp).max() <= 1e-5 * np.abs(ref_lp).max()
+    out, used, conv = dot._ops.sinkhorn_dual_forward(la.to(DEV), tau, T, 0.0)
+    assert used.item() == T and conv.item() == 0 and used.device.type == "cpu"
+    gP = torch.randn(2, 20, 30, generator=g)
+    P2, gla, gtau = dot._ops.sinkhorn_with_grads_implicit(la.to(DEV), gP.to(DEV), tau, T, T)
+    rg, rt = O.sinkhorn_backward_implicit(la.numpy(), ref_p, gP.numpy(), tau, T)
+    U.assert_normwise(gla, rg, U.GRAD_RTOL, "grad_log_alpha")
+    U.assert_rel(gtau, rt, U.GRAD_RTOL, "grad_tau", atol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# tol > 0: the reference's CUDA early stop (max |du| over the batch)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("B,n,m,reg,tol", [(2, 32, 48, 0.5, 1e-5), (3, 64, 64, 0.2, 1e-4), (1, 200, 150, 1.0, 1e-6)])
+def test_tol_early_stop_matches_oracle(B, n, m, reg, tol):
+    g = U.gen(n + m)
+    C = torch.rand(B, n, m, generator=g)
+    u, v, used_ref, conv_ref = O.sinkhorn_dual(-C.numpy(), reg, 400, tol=tol)
+    res = dot.sinkhorn(C.to(DEV), reg=reg, n_iters=400, tol=tol)
+    assert res.converged == conv_ref
+    assert abs(res.n_iters_used - used_ref) <= 1   # a |du| within an ulp of tol may flip one iteration
+    K = (-C.numpy()) * np.float32(1.0 / reg)
+    P_ref = np.exp(K + u[:, :, None] + v[:, None, :])
+    U.assert_normwise(res.transport_plan, P_ref, 1e-4, "plan at convergence")
+
+
+def test_convergence_reduces_iterations():
+    """tests/test_sinkhorn.py:826-839 of the reference."""
+    torch.manual_seed(0)
+    cost = torch.rand(1, 256, 256, device=DEV)
+    early = dot.sinkhorn(cost, reg=0.1, n_iters=50)
+    fixed = dot.sinkhorn(cost, reg=0.1, n_iters=50, tol=0)
+    assert early.n_iters_used < 50
+    assert fixed.n_iters_used == 50
+    assert torch.allclose(early.transport_plan, fixed.transport_plan, atol=2e-3)
+
+
+def test_dual_false_matches_dual_true():
+    torch.manual_seed(0)
+    cost = torch.rand(1, 96, 128, device=DEV)
+    dual = dot.sinkhorn(cost, reg=0.1, n_iters=50, tol=0, dual=True)
+    full = dot.sinkhorn(cost, reg=0.1, n_iters=50, tol=0, dual=False)
+    assert dual.n_iters_used == 50 and full.n_iters_used == 50
+    assert torch.allclose(dual.transport_plan, full.transport_plan, atol=1e-5)
+
+
+# ---------------------------------------------------------------------------
+# behaviour ported from the reference's tests (tests/test_sinkhorn.py)
+# ---------------------------------------------------------------------------
+
+def _assert_marginals(plan, a, b, atol=1e-3):
+    assert torch.allclose(plan.sum(-1), a.expand_as(plan.sum(-1)), atol=atol)
+    assert torch.allclose(plan.sum(-2), b.expand_as(plan.sum(-2)), atol=atol)
+
+
+def test_uniform_square_and_rectangular():
+    for n, m in [(10, 10), (8, 16)]:
+        cost = torch.rand(2, n, m, device=DEV)
+        res = dot.sinkhorn(cost, reg=1.0)
+        assert res.transport_plan.shape == (2, n, m) and res.cost.shape == (2,)
+        _assert_marginals(res.transport_plan, torch.full((2, n), 1.0 / n, device=DEV),
+                          torch.full((2, m), 1.0 / m, device=DEV))
+
+
+def test_nonuniform_marginals():
+    cost = torch.rand(1, 8, 16, device=DEV)
+    a = torch.tensor([[0.20, 0.10, 0.15, 0.15, 0.10, 0.10, 0.10, 0.10]], device=DEV)
+    b = torch.full((1, 16), 1.0 / 16, device=DEV)
+    res = dot.sinkhorn(cost, reg=1.0, n_iters=100, a=a, b=b)
+    _assert_marginals(res.transport_plan, a, b)
+
+
+def test_unbatched_input_and_module():
+    cost = torch.rand(8, 16, device=DEV)
+    a = torch.softmax(torch.randn(8, device=DEV), -1)
+    b = torch.softmax(torch.randn(16, device=DEV), -1)
+    res = dot.sinkhorn(cost, reg=1.0, a=a, b=b)
+    assert res.transport_plan.shape == (8, 16) and res.cost.shape == ()
+    res2 = dot.Sinkhorn(reg=1.0, max_iter=100)(cost)
+    assert res2.transport_plan.shape == (8, 16)
+    P = dot.SinkhornFromScores(tau=1.0)(torch.randn(2, 8, 16, device=DEV))
+    assert P.shape == (2, 8, 16)
+
+
+def test_large_rectangular_matches_torch_reference():
+    """tests/test_sinkhorn.py:763-773: fp64 torch restatement of the iteration."""
+    torch.manual_seed(0)
+    cost = torch.rand(1, 320, 640, device=DEV)
+    res = dot.sinkhorn(cost, reg=0.1, n_iters=50, tol=0)
+    x = (-cost.double()) / 0.1
+    la, lb = -np.log(320.0), -np.log(640.0)
+    for _ in range(50):
+        x = x - torch.logsumexp(x, -1, keepdim=True) + la
+        x = x - torch.logsumexp(x, -2, keepdim=True) + lb
+    U.assert_normwise(res.transport_plan, x.exp(), 1e-5, "plan vs fp64")
+
+
+def test_very_large_square_preserves_marginals():
+    torch.manual_seed(0)
+    n = 1300
+    cost = torch.rand(1, n, n, device=DEV)
+    res = dot.sinkhorn(cost, reg=0.1, n_iters=50)
+    assert torch.isfinite(res.transport_plan).all()
+    u = torch.full((1, n), 1.0 / n, device=DEV)
+    _assert_marginals(res.transport_plan, u, u, atol=2e-3)
+
+
+def test_differentiable_reg_matches_finite_difference():
+    """tests/test_sinkhorn.py:400-416 (known answer against central differences)."""
+    cost = torch.eye(5, device=DEV).unsqueeze(0)
+    eps = torch.tensor(0.2, device=DEV, requires_grad=True)
+    dot.sinkhorn(cost, reg=eps, n_iters=80).cost.sum().backward()
+    analytic = eps.grad.item()
+    d = 1e-3
+    plus = dot.sinkhorn(cost, reg=0.2 + d, n_iters=80).cost.sum().item()
+    minus = dot.sinkhorn(cost, reg=0.2 - d, n_iters=80).cost.sum().item()
+    assert analytic > 0
+    assert abs(analytic - (plus - minus) / (2 * d)) < 5e-2
+
+
+def test_composed_gradient_through_points_and_reg():
+    source = torch.randn(5, 3, device=DEV, requires_grad=True)
+    target = torch.randn(5, 3, device=DEV)
+    eps = torch.tensor(0.1, device=DEV, requires_grad=True)
+    cost = torch.cdist(source, target).unsqueeze(0)
+    dot.sinkhorn(cost, reg=eps, n_iters=50).cost.sum().backward()
+    assert source.grad is not None and eps.grad is not None
+    assert torch.isfinite(source.grad).all()
+
+
+def test_marginals_without_grad_and_errors():
+    cost = torch.rand(2, 5, 6, device=DEV)
+    a = torch.softmax(torch.randn(2, 5, device=DEV), -1).requires_grad_(True)
+    res = dot.sinkhorn(cost.requires_grad_(True), a=a)
+    res.cost.sum().backward()
+    assert a.grad is None and cost.grad is not None
+    with pytest.raises(ValueError):
+        dot.sinkhorn(cost, reg=0.0)
+    with pytest.raises(ValueError):
+        dot.sinkhorn(cost, a=torch.full((2, 5), 0.3, device=DEV))
+    with pytest.raises(NotImplementedError):
+        dot.sinkhorn(cost, backward_mode="unrolled")
+
+
+def test_bf16_and_fp64_inputs_follow_reference_casts():
+    cost = torch.rand(2, 12, 12, device=DEV)
+    r32 = dot.sinkhorn(cost, reg=0.5, n_iters=30, tol=0)
+    c16 = cost.bfloat16().requires_grad_(True)
+    r16 = dot.sinkhorn(c16, reg=0.5, n_iters=30, tol=0)
+    assert r16.transport_plan.dtype == torch.float32
+    r16.cost.sum().backward()
+    assert c16.grad.dtype == torch.bfloat16
+    c64 = cost.double().requires_grad_(True)
+    r64 = dot.sinkhorn(c64, reg=0.5, n_iters=30, tol=0)
+    r64.cost.sum().backward()
+    assert c64.grad.dtype == torch.float64
+    U.assert_normwise(r64.transport_plan, r32.transport_plan, 1e-6, "fp64 input")
+
+
+# ---------------------------------------------------------------------------
+# full-size properties
+# ---------------------------------------------------------------------------
+
+def test_cfg2_full_size_properties_and_sampled_parity():
+    """B=256, 512x512, reg 0.05, 200 iterations, fwd+bwd."""
+    C = U.sqdist_cost(256, 512, 512, 64, 0).to(DEV).requires_grad_(True)
+    res = dot.sinkhorn(C, reg=0.05, n_iters=200, tol=0)
+    res.cost.sum().backward()
+    P = res.transport_plan.detach()
+    assert torch.isfinite(P).all() and torch.isfinite(C.grad).all()
+    # after the last column update the column marginals hold to fp32 rounding
+    assert torch.allclose(P.sum(-2), torch.full((256, 512), 1 / 512, device=DEV), rtol=1e-4, atol=0)
+    # cost equals sum(P*C) of the returned plan
+    U.assert_rel(res.cost.detach(), (P.double() * C.detach().double()).sum((1, 2)), 1e-5, "cost")
+    # sampled parity with the oracle on two batch elements
+    for bi in (0, 255):
+        ref = O.sinkhorn_api(C.detach()[bi:bi + 1].cpu().numpy(), 0.05, 200, bwd_tol=0.0)
+        U.assert_normwise(P[bi:bi + 1], ref["P"], U.PLAN_RTOL, f"plan[{bi}]")
+        U.assert_rel(res.cost[bi:bi + 1].detach(), ref["cost"], U.COST_RTOL, f"cost[{bi}]")
+        U.assert_normwise(C.grad[bi:bi + 1], ref["dC"], U.GRAD_RTOL, f"dC[{bi}]")
+
+
+def test_backward_is_linear_in_the_upstream_gradient():
+    """For a fixed plan the adjoint solve and epilogue are linear in G."""
+    C = U.sqdist_cost(16, 512, 512, 64, 1).to(DEV)
+    P, _, u, v, _ = ops.sinkhorn_forward_raw(C, -1.0, 0.05, 200)
+    g = U.gen(2)
+    G1 = torch.randn(16, 512, 512, generator=g).to(DEV)
+    G2 = torch.randn(16, 512, 512, generator=g).to(DEV)
+    g1, _ = ops.sinkhorn_backward_raw(C, -1.0, P, u, v, G1, None, 0.05, 200)
+    g2, _ = ops.sinkhorn_backward_raw(C, -1.0, P, u, v, G2, None, 0.05, 200)
+    g12, _ = ops.sinkhorn_backward_raw(C, -1.0, P, u, v, G1 + G2, None, 0.05, 200)
+    U.assert_normwise(g12, g1 + g2, 1e-4, "linearity")
+
+
+def test_deterministic_bitwise():
+    C = U.sqdist_cost(8, 512, 512, 64, 3).to(DEV)
+    outs = []
+    for _ in range(2):
+        Cg = C.clone().requires_grad_(True)
+        r = dot.sinkhorn(Cg, reg=0.05, n_iters=50, tol=0)
+        r.cost.sum().backward()
+        outs.append((r.transport_plan.detach().clone(), r.cost.detach().clone(), Cg.grad.clone()))
+    for x, y in zip(outs[0], outs[1]):
+        assert torch.equal(x, y)
+
+
+def test_cfg4_and_cfg1_full_size_against_oracle_sample():
+    """configs[3] (B=4096, 128x128, Dirichlet marginals, reg 0.1, 100 it) and
+    configs[0] (B=8, 64x64, reg 1, 100 it)."""
+    C = torch.rand(4096, 128, 128, generator=U.gen(0))
+    a = U.dirichlet(4096, 128, 1)
+    b = U.dirichlet(4096, 128, 2)
+    Cd = C.to(DEV).requires_grad_(True)
+    res = dot.sinkhorn(Cd, reg=0.1, n_iters=100, a=a.to(DEV), b=b.to(DEV), tol=0)
+    res.cost.sum().backward()
+    assert torch.isfinite(Cd.grad).all()
+    for bi in (0, 4095):
+        ref = O.sinkhorn_api(C[bi:bi + 1].numpy(), 0.1, 100, a[bi:bi + 1].numpy(), b[bi:bi + 1].numpy(),
+                             bwd_tol=0.0)
+        U.assert_normwise(res.transport_plan[bi:bi + 1], ref["P"], U.PLAN_RTOL, f"plan[{bi}]")
+        U.assert_normwise(Cd.grad[bi:bi + 1], ref["dC"], U.GRAD_RTOL, f"dC[{bi}]")
+    C1 = torch.rand(8, 64, 64, generator=U.gen(0))
+    ref = O.sinkhorn_api(C1.numpy(), 1.0, 100, bwd_tol=0.0)
+    r1 = run_api(C1, 1.0, 100)
+    U.assert_normwise(r1["P"], ref["P"], U.PLAN_RTOL, "cfg1 plan")
+    U.assert_normwise(r1["dC"], ref["dC"], U.GRAD_RTOL, "cfg1 dC")
