@@ -51,13 +51,15 @@ struct Probs {
 };
 
 // row/col softmax values and the output at one element (same expressions in
-// every pass).
+// every pass).  sim/T is rounded before the max is subtracted, as the
+// reference computes it (kernels_cpu.cpp:72-77), so the row/column maximum
+// gives exactly exp(0) = 1 (an FMA-contracted s*invT - max would not).
 __device__ __forceinline__ Probs probs(float s, float invT, float2 rs, float2 cs) {
-    const float val = s * invT;
+    const float val = __fmul_rn(s, invT);
     Probs p;
     p.row = exp88(val - rs.x) * rs.y;
     p.col = exp88(val - cs.x) * cs.y;
-    p.out = sqrtf(1e-9f + p.row * p.col);
+    p.out = sqrtf(__fadd_rn(1e-9f, __fmul_rn(p.row, p.col)));
     return p;
 }
 
@@ -78,10 +80,10 @@ bs_row_stats_kernel(const T* __restrict__ sim, const int32_t* __restrict__ lengt
     }
     const T* sr = sim + row * L2;
     float mx = kNegBig;
-    for (int64_t j = lane; j < l2; j += 32) mx = fmaxf(mx, ld(sr, j) * invT);
+    for (int64_t j = lane; j < l2; j += 32) mx = fmaxf(mx, __fmul_rn(ld(sr, j), invT));
     mx = warp_max<32>(mx);
     float s = 0.0f;
-    for (int64_t j = lane; j < l2; j += 32) s += exp88(ld(sr, j) * invT - mx);
+    for (int64_t j = lane; j < l2; j += 32) s += exp88(__fmul_rn(ld(sr, j), invT) - mx);
     s = warp_sum<32>(s);
     if (lane == 0) rstat[row] = make_float2(mx, s > 0.0f ? 1.0f / s : 0.0f);
 }
@@ -110,7 +112,7 @@ bs_col_stats_kernel(const T* __restrict__ sim, const int32_t* __restrict__ lengt
         for (int k = 0; k < 4; ++k) {
             const int64_t c = cbase + lane + 32 * k;
             if (c < l2) {
-                const float val = ld(sb, r * L2 + c) * invT;
+                const float val = __fmul_rn(ld(sb, r * L2 + c), invT);
                 if (val > M[k]) {
                     S[k] *= exp88(M[k] - val);
                     M[k] = val;
@@ -308,9 +310,9 @@ bs_bwd_grad_kernel(const T* __restrict__ sim, const float* __restrict__ gout,
         if (i < l1 && j < l2) {
             const float s = ld(sim, idx);
             const BwdTerms t = bwd_terms(s, __ldg(gout + idx), invT, rs, cstat[b * L2 + j]);
-            const float a = (t.d_row - rd) * t.row * invT;
-            const float c = (t.d_col - cdot[b * L2 + j]) * t.col * invT;
-            g = a + c;
+            const float a = __fmul_rn(__fmul_rn(t.d_row - rd, t.row), invT);
+            const float c = __fmul_rn(__fmul_rn(t.d_col - cdot[b * L2 + j], t.col), invT);
+            g = __fadd_rn(a, c);
             acc += g * s * invT;
         }
         st_grad<G>(gsim, idx, g);

@@ -44,6 +44,19 @@ struct SkBwdArgs {
     float* gtau;       // may be nullptr
 };
 
+// Fused single-pass iteration kernels (sinkhorn_fused.cu) for m <= 1024,
+// m % 4 == 0, 16-byte aligned data.
+struct FusedPlan {
+    int nseg = 1;          // segments (CTAs) per problem
+    int64_t seg_rows = 0;  // rows per segment
+};
+bool sk_fused_supported(int64_t n, int64_t m, const void* data);
+FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m);
+int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta,
+                      int iter, cudaStream_t st);
+int sk_fused_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv, const float2* cinv,
+                      float* lam, float* mu, float* part, int32_t* cnt, int32_t* err, cudaStream_t st);
+
 size_t sk_stream_fwd_ws(int64_t B, int64_t n, int64_t m, int n_iters, float tol, bool want_cost);
 int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 size_t sk_stream_bwd_ws(int64_t B, int64_t n, int64_t m);

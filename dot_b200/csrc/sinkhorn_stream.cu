@@ -21,6 +21,8 @@
 // column mat-vec P^T lambda.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 #include "sinkhorn.h"
@@ -536,16 +538,21 @@ struct SkFwdWs {
     float2* part;
     float* delta;
     float* cost_row;
+    int32_t* cnt;
 };
 
+// Fused kernels are used when the shape allows it; the workspace covers
+// either path (column partials sized for the larger of the two).
 static SkFwdWs carve_fwd(Carve& c, int64_t B, int64_t n, int64_t m, int n_iters, float tol,
                          bool want_cost) {
     SkFwdWs w{};
-    const int64_t rpc = col_rows_per_chunk(n);
-    const int64_t chunks = ceil_div(n, rpc);
-    w.part = chunks > 1 ? c.take<float2>(size_t(B * chunks * m)) : nullptr;
+    const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
+    const int64_t fseg = (m <= 1024 && m % 4 == 0) ? sk_fused_plan(B, n, m).nseg : 1;
+    const int64_t parts = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
+    w.part = parts > 0 ? c.take<float2>(size_t(B * parts * m)) : nullptr;
     w.delta = tol > 0.0f ? c.take<float>(size_t(n_iters > 0 ? n_iters : 1)) : nullptr;
     w.cost_row = want_cost ? c.take<float>(size_t(B * n)) : nullptr;
+    w.cnt = c.take<int32_t>(size_t(B));
     return w;
 }
 
@@ -571,8 +578,19 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     if (w.delta) cudaMemsetAsync(w.delta, 0, sizeof(float) * size_t(a.n_iters > 0 ? a.n_iters : 1), st);
 
     SkCtl ctl{w.delta, a.status, a.tol, 0};
+    const bool fused = sk_fused_supported(a.n, a.m, a.X);
+    FusedPlan plan;
+    if (fused) {
+        plan = sk_fused_plan(a.B, a.n, a.m);
+        cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
+    }
     for (int it = 0; it < a.n_iters; ++it) {
         ctl.iter = it;
+        if (fused) {
+            ProfScope ps(DOT_K_SK_FWD_ITER, st);
+            sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, st);
+            continue;
+        }
         {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
             sk_row_kernel<<<row_grid, kRowThreads, 0, st>>>(a.X, a.kinv, a.v2, a.la, a.la_def, a.u2,
@@ -613,18 +631,22 @@ struct SkBwdWs {
     float2* part2;
     float* part1;
     float* tau_row;
+    int32_t* cnt;     // [B] arrival counters, then one error word
 };
 
 static SkBwdWs carve_bwd(Carve& c, int64_t B, int64_t n, int64_t m) {
     SkBwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
+    const int64_t fseg = (m <= 1024 && m % 4 == 0) ? sk_fused_plan(B, n, m).nseg : 1;
     w.rinv = c.take<float2>(size_t(B * n));
     w.cinv = c.take<float2>(size_t(B * m));
     w.lam = c.take<float>(size_t(B * n));
     w.mu = c.take<float>(size_t(B * m));
     w.part2 = chunks > 1 ? c.take<float2>(size_t(B * chunks * m)) : nullptr;
-    w.part1 = chunks > 1 ? c.take<float>(size_t(B * chunks * m)) : nullptr;
+    const int64_t p1 = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
+    w.part1 = p1 > 0 ? c.take<float>(size_t(B * p1 * m)) : nullptr;
     w.tau_row = c.take<float>(size_t(B * n));
+    w.cnt = c.take<int32_t>(size_t(B + 1));
     return w;
 }
 
@@ -659,7 +681,18 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
         ProfScope ps(DOT_K_SK_BWD_EPI, st);
         skb_col_prep_merge_kernel<<<merge_grid, 256, 0, st>>>(w.part2, w.cinv, a.B, a.m, chunks);
     }
+    const bool fused = sk_fused_supported(a.n, a.m, a.P);
+    FusedPlan plan;
+    if (fused) {
+        plan = sk_fused_plan(a.B, a.n, a.m);
+        cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B + 1), st);
+    }
     for (int it = 0; it < a.bwd_iters; ++it) {
+        if (fused) {
+            ProfScope ps(DOT_K_SK_BWD_ITER, st);
+            sk_fused_bwd_iter(a, plan, w.rinv, w.cinv, w.lam, w.mu, w.part1, w.cnt, w.cnt + a.B, st);
+            continue;
+        }
         {
             ProfScope ps(DOT_K_SK_BWD_ITER, st);
             skb_row_iter_kernel<<<row_grid, kRowThreads, 0, st>>>(a.P, w.rinv, w.mu, w.lam, rows, a.n, a.m);

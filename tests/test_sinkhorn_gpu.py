@@ -139,7 +139,10 @@ def test_return_log_and_low_level_ops_match_oracle():
 # tol > 0: the reference's CUDA early stop (max |du| over the batch)
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("B,n,m,reg,tol", [(2, 32, 48, 0.5, 1e-5), (3, 64, 64, 0.2, 1e-4), (1, 200, 150, 1.0, 1e-6)])
+# tol is kept well above the fp32 noise floor of u (one ulp of |u| ~ 5 is 4.8e-7):
+# at a tol of a few ulp the first iteration with |du| < tol is decided by rounding
+# noise, in the reference as much as here.
+@pytest.mark.parametrize("B,n,m,reg,tol", [(2, 32, 48, 0.5, 1e-5), (3, 64, 64, 0.2, 1e-4), (1, 200, 150, 1.0, 2e-5)])
 def test_tol_early_stop_matches_oracle(B, n, m, reg, tol):
     g = U.gen(n + m)
     C = torch.rand(B, n, m, generator=g)
