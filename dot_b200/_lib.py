@@ -31,6 +31,8 @@ _SIGS = {
     "dot_sinkhorn_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i, _f, _i]),
     "dot_sinkhorn_fwd": (_i, [_vp, _f, _vp, _vp, _i64, _i64, _i64, _f, _i, _f, _i, _vp, _vp, _vp, _vp, _vp,
                               _vp, _sz, _vp]),
+    "dot_sinkhorn_fwd_noalloc": (_i, [_vp, _f, _vp, _vp, _i64, _i64, _i64, _f, _i, _f, _i, _vp, _vp, _vp, _vp,
+                                      _vp, _vp]),
     "dot_sinkhorn_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "dot_sinkhorn_bwd": (_i, [_vp, _f, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i, _vp, _vp, _vp, _sz,
                               _vp]),
@@ -53,7 +55,7 @@ def load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"dot_b200: native library not found at {LIB_PATH}; build it with "
-            "`python -m dot_b200.build` (there is no CPU fallback)")
+            "`python dot_b200/build.py` (there is no CPU fallback)")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in _SIGS.items():
         fn = getattr(lib, name)

@@ -1,6 +1,6 @@
 """Build the dot_b200 C-ABI library for sm_100a with nvcc (in-tree).
 
-``python -m dot_b200.build`` compiles every ``csrc/*.cu`` into
+``python dot_b200/build.py`` compiles every ``csrc/*.cu`` into
 ``dot_b200/_lib/libdot_b200.so`` with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3``.  The CUDA runtime is
 linked statically so the library carries no dependency beyond the driver.

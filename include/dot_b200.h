@@ -89,6 +89,34 @@ DOT_API int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_
                      float* pot_u, float* pot_v, int32_t* status, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/*
+ * dot_sinkhorn_fwd without a workspace argument: the same computation, with
+ * its scratch space taken from a fixed 16 MiB array in device memory that the
+ * library itself holds (a static __device__ array), so this call never
+ * allocates.  It is for callers that cannot call cudaMalloc: plugins running
+ * inside a host application that owns all device memory and forbids further
+ * allocations, and foreign-language bindings (cgo, JNI, ctypes) that receive
+ * device pointers from elsewhere but have no device allocator of their own.
+ *
+ * Limits and rules:
+ *  * Problems whose scratch need (dot_sinkhorn_fwd_workspace_bytes) exceeds
+ *    16 MiB are rejected with DOT_ERR_WORKSPACE and a message giving the need
+ *    (e.g. B=256 x 512 x 512 and B=4096 x 128 x 128 fit).
+ *  * The first call on a device looks up the array's device address with that
+ *    device current and caches it; make that first call before any stream
+ *    capture begins.
+ *  * All calls share the one array per device, and it keeps the last call's
+ *    contents (the call clears what must start at zero itself).  Calls that
+ *    overlap on the GPU -- on different streams, or from several host threads
+ *    -- race on it; serialise them (one stream, or your own ordering).
+ *  * Every GPU that loads the library holds the 16 MiB until process exit.
+ * This entry point has no counterpart in the reference.
+ */
+DOT_API int dot_sinkhorn_fwd_noalloc(const float* X, float score_sign, const float* log_a,
+                                     const float* log_b, int64_t B, int64_t n, int64_t m, float tau,
+                                     int n_iters, float tol, int out_mode, float* out, float* cost,
+                                     float* pot_u, float* pot_v, int32_t* status, void* stream);
+
 /* Bytes of workspace dot_sinkhorn_bwd needs for this problem. */
 DOT_API size_t dot_sinkhorn_bwd_workspace_bytes(int64_t B, int64_t n, int64_t m, int bwd_iters);
 

@@ -18,9 +18,13 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: test needs a CUDA GPU (B200)")
-    from dot_b200 import build as _b
+    import importlib.util
 
-    _b.build()
+    # load dot_b200/build.py by path: importing the package loads the library
+    spec = importlib.util.spec_from_file_location("_dot_b200_build", os.path.join(ROOT, "dot_b200", "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
     if not os.path.exists(os.path.join(ROOT, "oracle", "_build", "liboracle.so")):
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "oracle"], check=True)
 
