@@ -116,6 +116,39 @@ def test_oracle_parity_random(B, n, m, reg, T, marg):
     assert r["dreg"] == pytest.approx(float(ref["dreg"]), rel=U.GRAD_RTOL, abs=1e-6)
 
 
+@pytest.mark.parametrize("B,n,m,reg", [(2, 64, 256, 1.0), (2, 512, 256, 1.0), (1, 700, 512, 0.5)])
+def test_far_columns_take_the_exact_path(B, n, m, reg):
+    """Columns ~200/reg below every row's maximum flush in the shared-reference
+    column sums of the fused forward; they must be recomputed exactly.
+
+    With |K| up to 400 one ulp of K is 3e-5: on these inputs the reference's
+    own two formulations -- its CUDA dual iteration and its CPU primal one --
+    differ by up to 1.6e-5 normwise in the plan and 1.2e-4 in the gradient
+    (measured with the oracle's restatements of both).  The tolerances here
+    are about 3x that inherent gap; without the exact path the far columns'
+    potentials would be infinite."""
+    g = U.gen(n + m)
+    C = torch.rand(B, n, m, generator=g)
+    C[:, :, 0] = 200.0
+    C[:, :, 7] = 150.0
+    C[0, :, 3] = 120.0
+    C[0, ::3, 3] = 0.5      # far for most rows, near for some
+    Cn = C.numpy()
+    u, v, _, _ = O.sinkhorn_dual(-Cn, reg, 20)
+    K = (-Cn) * np.float32(1.0 / reg)
+    P_dual = np.exp((K + u[:, :, None]) + v[:, None, :]).astype(np.float32)
+    gla, _ = O.sinkhorn_backward_implicit(-Cn, P_dual, Cn, reg, 20)
+    dC_dual = P_dual - gla
+    r = run_api(C, reg, 20)
+    assert np.isfinite(r["P"]).all() and np.isfinite(r["dC"]).all()
+    U.assert_normwise(r["P"], P_dual, 5e-5, "plan vs dual form")
+    U.assert_rel(r["cost"], (P_dual.astype(np.float64) * Cn).sum((1, 2)), U.COST_RTOL, "cost", atol=1e-9)
+    U.assert_normwise(r["dC"], dC_dual, 4e-4, "dC vs dual form")
+    ref = O.sinkhorn_api(Cn, reg, 20, bwd_tol=0.0)
+    U.assert_normwise(r["P"], ref["P"], 5e-5, "plan vs primal form")
+    U.assert_normwise(r["dC"], ref["dC"], 4e-4, "dC vs primal form")
+
+
 def test_return_log_and_low_level_ops_match_oracle():
     g = U.gen(5)
     la = torch.randn(2, 20, 30, generator=g)
