@@ -172,6 +172,7 @@ int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_a, const
 size_t dot_sinkhorn_bwd_workspace_bytes(int64_t B, int64_t n, int64_t m, int bwd_iters) {
     (void)bwd_iters;
     if (B <= 0 || n <= 0 || m <= 0) return 0;
+    // the streaming size covers the resident path and its unaligned fallback
     size_t a = sk_stream_bwd_ws(B, n, m);
     size_t b = sk_resident_supported(n, m) ? sk_resident_bwd_ws(B, n, m) : 0;
     return a > b ? a : b;

@@ -1,14 +1,574 @@
-// On-chip resident Sinkhorn solvers: placeholder until the resident kernels
-// land; every shape currently takes the streaming path.
+// On-chip resident Sinkhorn solvers for small problems: one CTA per problem.
+//
+// The problem's n x m tile is copied into shared memory once with a 1-D bulk
+// copy (cp.async.bulk, the TMA engine) and every iteration runs on it, so HBM
+// is read once per call instead of once per iteration.  Used for tol == 0
+// (the reference's tol > 0 criterion is global over the batch, which
+// independent CTAs cannot evaluate without waiting on one another) when
+// n*m*4 fits the shared-memory budget and m % 4 == 0.
+//
+// Layout: W warps; a warp is split into G = 32/LPR lane groups of LPR lanes,
+// each group owning one row at a time; lane l of a group owns columns
+// 4*l + 4*LPR*p (p < VPL) of every row it touches.  Per iteration:
+//   row pass   t_ij = K_ij + v_j, u_i = la_i - LSE_j t_ij (max then sum,
+//              reduced across the group's lanes), and the column sums
+//              S_j += E_ij * exp(a_i - A) with E_ij = exp(t_ij - max_i),
+//              a_i = max_i + u_i, A a warp-wide reference (see
+//              sinkhorn_fused.cu: one exponential per element);
+//   merge      per column over the W warps: v_j = lb_j - (A* - v_j + log S_j),
+//              with an exact max-based column LSE from shared memory when the
+//              merged sum is too small to trust.
+// The backward keeps the plan tile resident and runs the Gauss-Seidel adjoint
+// sweeps on it (reference: src/sinkhorn/kernels.cu:965-1098).
+#include <cmath>
+
+#include "common.cuh"
 #include "internal.h"
 #include "sinkhorn.h"
+#include "tma.cuh"
 
 namespace dotb {
 
-bool sk_resident_supported(int64_t, int64_t) { return false; }
+namespace {
+
+constexpr float kRaiseR = 60.0f;
+constexpr float kTinyR = 8.077935669463161e-28f;   // 2^-90
+constexpr int kMaxSmemTile = 160 * 1024;           // bytes of the resident tile
+
+template <int LPR_, int VPL_, int W_, int MINB_>
+struct RCfg {
+    static constexpr int MINB = MINB_;           // CTAs per SM the launch bounds target
+    static constexpr int LPR = LPR_;             // lanes per row
+    static constexpr int VPL = VPL_;             // float4 per lane per row
+    static constexpr int W = W_;                 // warps
+    static constexpr int G = 32 / LPR;           // row groups per warp
+    static constexpr int NC = 4 * VPL;           // columns per lane
+    static constexpr int CW = 4 * LPR * VPL;     // columns covered
+    static constexpr int ROWS_PER_SLOT = W * G;  // rows per pass over the warps
+    static constexpr int T = W * 32;
+};
+
+// Dynamic shared memory: tile [n*m] | part [W*CW] | v [CW] | aw [W] | sc [W] |
+// u [n] | fix [CW] | nfix.  tile, part and v start 16-byte aligned (n*m, W*CW
+// and CW are multiples of 4 floats) for float4 access.
+template <typename C>
+struct RSmem {
+    float* tile;
+    float* part;   // per-warp column partial sums
+    float* u;
+    float* v;
+    float* aw;     // per-warp reference (forward) ; scratch
+    float* sc;     // per-warp scale factors
+    int* fix;      // flagged columns
+    int* nfix;
+    static size_t bytes(int64_t n, int64_t m) {
+        size_t b = size_t(n * m) * 4;
+        b += size_t(C::W) * C::CW * 4;
+        b += size_t(n) * 4 + size_t(C::CW) * 4 + 2 * C::W * 4 + size_t(C::CW) * 4 + 16;
+        return (b + 127) & ~size_t(127);
+    }
+    __device__ static RSmem carve(unsigned char* base, int64_t n, int64_t m) {
+        RSmem s;
+        float* f = reinterpret_cast<float*>(base);
+        s.tile = f;
+        f += n * m;
+        s.part = f;
+        f += C::W * C::CW;
+        s.v = f;
+        f += C::CW;
+        s.aw = f;
+        f += C::W;
+        s.sc = f;
+        f += C::W;
+        s.u = f;
+        f += n;
+        s.fix = reinterpret_cast<int*>(f);
+        s.nfix = s.fix + C::CW;
+        return s;
+    }
+};
+
+template <int LPR>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+    for (int off = LPR / 2; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+template <int LPR>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int off = LPR / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+// Reduce across the G groups of a warp (lanes with the same lane % LPR).
+template <int LPR>
+__device__ __forceinline__ float across_groups_sum(float v) {
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+template <int LPR>
+__device__ __forceinline__ float across_groups_max(float v) {
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// Load the b-th n x m tile of src into shared memory with one bulk copy.
+__device__ __forceinline__ bool load_tile(float* tile, const float* src, int64_t n, int64_t m, uint64_t* bar,
+                                          int32_t* err) {
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t bytes = uint32_t(n * m * 4);
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(tile, src, bytes, bar);
+    }
+    const bool ok = mbar_wait(bar, 0, err);
+    return __syncthreads_and(ok) != 0;
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+template <typename C>
+__global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
+    constexpr int LPR = C::LPR, VPL = C::VPL, W = C::W, G = C::G, NC = C::NC;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float s_red[W];
+    const int64_t n = a.n, m = a.m, b = blockIdx.x;
+    RSmem<C> S = RSmem<C>::carve(smem, n, m);
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int grp = lane / LPR, gl = lane % LPR;
+    int32_t* err = a.status + 3;
+
+    for (int64_t j = tid; j < C::CW; j += C::T) S.v[j] = 0.0f;
+    if (!load_tile(S.tile, a.X + b * n * m, n, m, &bar, err)) return;
+
+    auto colof = [&](int p) { return 4 * gl + 4 * LPR * p; };
+    const int nslots = int((n + C::ROWS_PER_SLOT - 1) / C::ROWS_PER_SLOT);
+    const float* la = a.la ? a.la + b * n : nullptr;
+    const float* lb = a.lb ? a.lb + b * m : nullptr;
+
+    for (int it = 0; it < a.n_iters; ++it) {
+        float vr[NC];
+#pragma unroll
+        for (int p = 0; p < VPL; ++p) {
+            const float4 v4 = *reinterpret_cast<const float4*>(S.v + colof(p));
+            vr[4 * p + 0] = v4.x;
+            vr[4 * p + 1] = v4.y;
+            vr[4 * p + 2] = v4.z;
+            vr[4 * p + 3] = v4.w;
+        }
+        float cs[NC];
+#pragma unroll
+        for (int e = 0; e < NC; ++e) cs[e] = 0.0f;
+        float A = kNegBig;
+        for (int sl = 0; sl < nslots; ++sl) {
+            const int64_t i = int64_t(sl) * C::ROWS_PER_SLOT + wid * G + grp;
+            const bool rok = i < n;
+            float t[NC];
+            float mx = kNegBig;
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                const int col = colof(p);
+                if (rok && col < m) {
+                    const float4 x = *reinterpret_cast<const float4*>(S.tile + i * m + col);
+                    t[4 * p + 0] = kplus(x.x, a.kinv, vr[4 * p + 0]);
+                    t[4 * p + 1] = kplus(x.y, a.kinv, vr[4 * p + 1]);
+                    t[4 * p + 2] = kplus(x.z, a.kinv, vr[4 * p + 2]);
+                    t[4 * p + 3] = kplus(x.w, a.kinv, vr[4 * p + 3]);
+                } else {
+                    t[4 * p + 0] = t[4 * p + 1] = t[4 * p + 2] = t[4 * p + 3] = -INFINITY;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < NC; ++e) mx = fmaxf(mx, t[e]);
+            mx = group_max<LPR>(mx);
+            float s = 0.0f;
+#pragma unroll
+            for (int e = 0; e < NC; ++e) {
+                t[e] = exp_shift(t[e] - mx);
+                s += t[e];
+            }
+            s = group_sum<LPR>(s);
+            float ai = -INFINITY;
+            if (rok) {
+                const float unew = (la ? la[i] : a.la_def) - lse_finish(mx, s);
+                if (gl == 0) S.u[i] = unew;
+                ai = mx + unew;
+            }
+            const float amax = across_groups_max<LPR>(ai);
+            if (amax > A + kRaiseR) {          // warp-uniform
+                const float sc = exp_shift(A - amax);
+#pragma unroll
+                for (int e = 0; e < NC; ++e) cs[e] *= sc;
+                A = amax;
+            }
+            const float w = exp_shift(ai - A);
+#pragma unroll
+            for (int e = 0; e < NC; ++e) cs[e] = fmaf(t[e], w, cs[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < NC; ++e) cs[e] = across_groups_sum<LPR>(cs[e]);
+        if (grp == 0) {
+#pragma unroll
+            for (int p = 0; p < VPL; ++p)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) S.part[wid * C::CW + colof(p) + e] = cs[4 * p + e];
+        }
+        if (lane == 0) S.aw[wid] = A;
+        __syncthreads();
+        if (wid == 0) {
+            const float aw = lane < W ? S.aw[lane] : kNegBig;
+            const float amax = warp_max<32>(aw);
+            if (lane < W) S.sc[lane] = exp_shift(aw - amax);
+            if (lane == 0) s_red[0] = amax;
+        }
+        if (tid == 0) *S.nfix = 0;
+        __syncthreads();
+        const float amax = s_red[0];
+        for (int64_t j = tid; j < m; j += C::T) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) sum = fmaf(S.part[w * C::CW + j], S.sc[w], sum);
+            if (sum < kTinyR) {
+                S.fix[atomicAdd(S.nfix, 1)] = int(j);
+            } else {
+                S.v[j] = (lb ? lb[j] : a.lb_def) - (amax - S.v[j] + logf(sum));
+            }
+        }
+        __syncthreads();
+        const int nfix = *S.nfix;
+        for (int k = wid; k < nfix; k += W) {   // exact column LSE from the resident tile
+            const int64_t j = S.fix[k];
+            float mx = kNegBig;
+            for (int64_t i = lane; i < n; i += 32) mx = fmaxf(mx, kplus(S.tile[i * m + j], a.kinv, S.u[i]));
+            mx = warp_max<32>(mx);
+            float sm = 0.0f;
+            for (int64_t i = lane; i < n; i += 32) sm += exp_shift(kplus(S.tile[i * m + j], a.kinv, S.u[i]) - mx);
+            sm = warp_sum<32>(sm);
+            if (lane == 0) S.v[j] = (lb ? lb[j] : a.lb_def) - lse_finish(mx, sm);
+        }
+        if (nfix > 0) __syncthreads();
+    }
+
+    // epilogue: potentials, plan (P = safe_exp((K + u_i) + v_j)) and cost
+    for (int64_t i = tid; i < n; i += C::T) a.u2[b * n + i] = a.n_iters > 0 ? S.u[i] : 0.0f;
+    for (int64_t j = tid; j < m; j += C::T) a.v2[b * m + j] = S.v[j];
+    if (a.n_iters == 0)
+        for (int64_t i = tid; i < n; i += C::T) S.u[i] = 0.0f;
+    __syncthreads();
+    float acc = 0.0f;
+    float* outb = a.out + b * n * m;
+    const int64_t nm4 = (n * m) >> 2;
+    for (int64_t q = tid; q < nm4; q += C::T) {
+        const int64_t e0 = q * 4;
+        const int64_t i = e0 / m, j = e0 - i * m;
+        const float4 x = *reinterpret_cast<const float4*>(S.tile + e0);
+        const float uu = S.u[i];
+        const float t0 = __fadd_rn(kplus(x.x, a.kinv, uu), S.v[j + 0]);
+        const float t1 = __fadd_rn(kplus(x.y, a.kinv, uu), S.v[j + 1]);
+        const float t2 = __fadd_rn(kplus(x.z, a.kinv, uu), S.v[j + 2]);
+        const float t3 = __fadd_rn(kplus(x.w, a.kinv, uu), S.v[j + 3]);
+        float4 o;
+        if (a.out_mode == 0) {
+            o = make_float4(safe_expf(t0), safe_expf(t1), safe_expf(t2), safe_expf(t3));
+            acc += o.x * x.x + o.y * x.y + o.z * x.z + o.w * x.w;
+        } else {
+            o = make_float4(t0, t1, t2, t3);
+        }
+        reinterpret_cast<float4*>(outb)[q] = o;
+    }
+    if (a.cost != nullptr) {
+        acc = warp_sum<32>(acc);
+        if (lane == 0) s_red[wid] = acc;
+        __syncthreads();
+        if (tid == 0) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) tot += s_red[w];
+            a.cost[b] = tot;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// backward (implicit adjoint on the resident plan tile)
+// ---------------------------------------------------------------------------
+template <typename C>
+__global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int32_t* err) {
+    constexpr int LPR = C::LPR, VPL = C::VPL, W = C::W, G = C::G, NC = C::NC;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float s_red[W];
+    const int64_t n = a.n, m = a.m, b = blockIdx.x;
+    RSmem<C> S = RSmem<C>::carve(smem, n, m);
+    // reuse of the carve: u -> lambda [n], v -> mu [CW]; the row invariants
+    // (sum P G, sum P) live in registers of their row's group, the column
+    // invariants in `colinv` below.
+    float* lam = S.u;
+    float* mu = S.v;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int grp = lane / LPR, gl = lane % LPR;
+    auto colof = [&](int p) { return 4 * gl + 4 * LPR * p; };
+    const int nslots = int((n + C::ROWS_PER_SLOT - 1) / C::ROWS_PER_SLOT);
+    constexpr int MAXSLOTS = 8;
+    const float gc = a.gcost ? a.gcost[b] : 0.0f;
+    const float* Xb = a.X + b * n * m;
+    const float* gPb = a.gP ? a.gP + b * n * m : nullptr;
+
+    for (int64_t j = tid; j < C::CW; j += C::T) mu[j] = 0.0f;
+    if (!load_tile(S.tile, a.P + b * n * m, n, m, &bar, err)) return;
+
+    auto G_at = [&](int64_t idx) -> float {   // G = grad_cost_b * X + grad_P (autograd's rounding)
+        float g = __fmul_rn(gc, __ldg(Xb + idx));
+        if (gPb) g = __fadd_rn(g, __ldg(gPb + idx));
+        return g;
+    };
+
+    // ---- invariants: row (sum_k P G, sum_k P), column (sum_i P G, sum_i P)
+    float rPG[MAXSLOTS], rP[MAXSLOTS];
+    float cPG[NC], cP[NC];
+#pragma unroll
+    for (int e = 0; e < NC; ++e) { cPG[e] = 0.0f; cP[e] = 0.0f; }
+#pragma unroll
+    for (int sl = 0; sl < MAXSLOTS; ++sl) {
+        rPG[sl] = 0.0f;
+        rP[sl] = 1.0f;
+        if (sl >= nslots) continue;
+        const int64_t i = int64_t(sl) * C::ROWS_PER_SLOT + wid * G + grp;
+        float spg = 0.0f, sp = 0.0f;
+        if (i < n) {
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                const int col = colof(p);
+                if (col < m) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float pv = S.tile[i * m + col + e];
+                        const float gv = G_at(i * m + col + e);
+                        spg += pv * gv;
+                        sp += pv;
+                        cPG[4 * p + e] += pv * gv;
+                        cP[4 * p + e] += pv;
+                    }
+                }
+            }
+        }
+        rPG[sl] = group_sum<LPR>(spg);
+        rP[sl] = group_sum<LPR>(sp);
+    }
+    // column invariants: reduce over groups, then over warps through S.part
+    float* cinv_pg = S.part;
+#pragma unroll
+    for (int e = 0; e < NC; ++e) {
+        cPG[e] = across_groups_sum<LPR>(cPG[e]);
+        cP[e] = across_groups_sum<LPR>(cP[e]);
+    }
+    // two rounds through the per-warp partial buffer: first sum P G, then sum P
+    __shared__ float s_cpg[C::CW];
+    __shared__ float s_cp[C::CW];
+    if (grp == 0) {
+#pragma unroll
+        for (int p = 0; p < VPL; ++p)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) cinv_pg[wid * C::CW + colof(p) + e] = cPG[4 * p + e];
+    }
+    __syncthreads();
+    for (int j = tid; j < C::CW; j += C::T) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) s += cinv_pg[w * C::CW + j];
+        s_cpg[j] = s;
+    }
+    __syncthreads();
+    if (grp == 0) {
+#pragma unroll
+        for (int p = 0; p < VPL; ++p)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) cinv_pg[wid * C::CW + colof(p) + e] = cP[4 * p + e];
+    }
+    __syncthreads();
+    for (int j = tid; j < C::CW; j += C::T) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) s += cinv_pg[w * C::CW + j];
+        s_cp[j] = s;
+    }
+    __syncthreads();
+
+    // ---- Gauss-Seidel sweeps
+    for (int it = 0; it < a.bwd_iters; ++it) {
+        float mr[NC], acc[NC];
+#pragma unroll
+        for (int p = 0; p < VPL; ++p) {
+            const float4 u4 = *reinterpret_cast<const float4*>(mu + colof(p));
+            mr[4 * p + 0] = u4.x;
+            mr[4 * p + 1] = u4.y;
+            mr[4 * p + 2] = u4.z;
+            mr[4 * p + 3] = u4.w;
+        }
+#pragma unroll
+        for (int e = 0; e < NC; ++e) acc[e] = 0.0f;
+#pragma unroll
+        for (int sl = 0; sl < MAXSLOTS; ++sl) {
+            if (sl >= nslots) break;
+            const int64_t i = int64_t(sl) * C::ROWS_PER_SLOT + wid * G + grp;
+            const bool rok = i < n;
+            float pv[NC];
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                const int col = colof(p);
+                if (rok && col < m) {
+                    const float4 x = *reinterpret_cast<const float4*>(S.tile + i * m + col);
+                    pv[4 * p + 0] = x.x;
+                    pv[4 * p + 1] = x.y;
+                    pv[4 * p + 2] = x.z;
+                    pv[4 * p + 3] = x.w;
+                } else {
+                    pv[4 * p + 0] = pv[4 * p + 1] = pv[4 * p + 2] = pv[4 * p + 3] = 0.0f;
+                }
+            }
+            float s = 0.0f;
+#pragma unroll
+            for (int e = 0; e < NC; ++e) s += pv[e] * mr[e];
+            s = group_sum<LPR>(s);
+            const float l = rok ? (rPG[sl] - s) / fmaxf(rP[sl], kSumFloor) : 0.0f;
+            if (rok && gl == 0) lam[i] = l;
+#pragma unroll
+            for (int e = 0; e < NC; ++e) acc[e] += pv[e] * l;
+        }
+#pragma unroll
+        for (int e = 0; e < NC; ++e) acc[e] = across_groups_sum<LPR>(acc[e]);
+        if (grp == 0) {
+#pragma unroll
+            for (int p = 0; p < VPL; ++p)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) S.part[wid * C::CW + colof(p) + e] = acc[4 * p + e];
+        }
+        __syncthreads();
+        for (int64_t j = tid; j < m; j += C::T) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) s += S.part[w * C::CW + j];
+            mu[j] = (s_cpg[j] - s) / fmaxf(s_cp[j], kSumFloor);
+        }
+        __syncthreads();
+    }
+    if (a.bwd_iters == 0)
+        for (int64_t i = tid; i < n; i += C::T) lam[i] = 0.0f;
+    __syncthreads();
+
+    // ---- gradient epilogue
+    float accT = 0.0f;
+    const int64_t nm = n * m;
+    for (int64_t idx = tid; idx < nm; idx += C::T) {
+        const int64_t i = idx / m, j = idx - i * m;
+        const float x = __ldg(Xb + idx);
+        const float p = S.tile[idx];
+        const float centred = G_at(idx) - lam[i] - mu[j];
+        const float g = p * centred / a.tau;
+        a.gX[b * nm + idx] = __fadd_rn(a.sign * g, __fmul_rn(gc, p));
+        accT += g * (a.sign * x);
+    }
+    if (a.gtau != nullptr) {
+        accT = warp_sum<32>(accT);
+        if (lane == 0) s_red[wid] = accT;
+        __syncthreads();
+        if (tid == 0) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) tot += s_red[w];
+            a.gtau[b] = tot * (-1.0f / a.tau);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// configurations
+// ---------------------------------------------------------------------------
+using CfgS = RCfg<8, 2, 8, 4>;    // m <= 64,  32 rows per slot
+using CfgM = RCfg<8, 4, 8, 3>;    // m <= 128, 32 rows per slot
+using CfgL = RCfg<16, 4, 8, 2>;   // m <= 256, 16 rows per slot
+
+template <typename C>
+bool fits(int64_t n, int64_t m) {
+    if (m > C::CW || n > int64_t(C::ROWS_PER_SLOT) * 8) return false;
+    return RSmem<C>::bytes(n, m) <= size_t(kMaxSmemTile) + 32 * 1024 && n * m * 4 <= kMaxSmemTile;
+}
+
+enum class RKind { None, S, M, L };
+
+RKind pick(int64_t n, int64_t m) {
+    if (m % 4 != 0 || n < 1) return RKind::None;
+    if (m <= 64 && fits<CfgS>(n, m)) return RKind::S;
+    if (m <= 128 && fits<CfgM>(n, m)) return RKind::M;
+    if (m <= 256 && fits<CfgL>(n, m)) return RKind::L;
+    return RKind::None;
+}
+
+template <typename C>
+int launch_fwd(const SkFwdArgs& a, cudaStream_t st) {
+    const size_t sm = RSmem<C>::bytes(a.n, a.m);
+    cudaFuncSetAttribute(skr_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    ProfScope ps(DOT_K_SK_RESIDENT, st);
+    skr_fwd_kernel<C><<<unsigned(a.B), C::T, sm, st>>>(a);
+    return check_launch("sinkhorn forward (resident)");
+}
+
+template <typename C>
+int launch_bwd(const SkBwdArgs& a, int32_t* err, cudaStream_t st) {
+    const size_t sm = RSmem<C>::bytes(a.n, a.m);
+    cudaFuncSetAttribute(skr_bwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    ProfScope ps(DOT_K_SK_RESIDENT, st);
+    skr_bwd_kernel<C><<<unsigned(a.B), C::T, sm, st>>>(a, err);
+    return check_launch("sinkhorn backward (resident)");
+}
+
+__global__ void skr_status_kernel(int32_t* status, int n_iters) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        status[0] = n_iters;
+        status[1] = 0;
+    }
+}
+
+}  // namespace
+
+bool sk_resident_supported(int64_t n, int64_t m) { return pick(n, m) != RKind::None; }
+
 size_t sk_resident_fwd_ws(int64_t, int64_t, int64_t, bool) { return 0; }
-int sk_resident_fwd(const SkFwdArgs&, void*, cudaStream_t) { return fail(DOT_ERR_UNSUPPORTED, "resident"); }
-size_t sk_resident_bwd_ws(int64_t, int64_t, int64_t) { return 0; }
-int sk_resident_bwd(const SkBwdArgs&, void*, cudaStream_t) { return fail(DOT_ERR_UNSUPPORTED, "resident"); }
+size_t sk_resident_bwd_ws(int64_t, int64_t, int64_t) { return 256; }
+
+int sk_resident_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
+    if ((reinterpret_cast<uintptr_t>(a.X) & 15u) != 0) return sk_stream_fwd(a, ws, st);
+    cudaMemsetAsync(a.status, 0, sizeof(int32_t) * 4, st);
+    int rc;
+    switch (pick(a.n, a.m)) {
+        case RKind::S: rc = launch_fwd<CfgS>(a, st); break;
+        case RKind::M: rc = launch_fwd<CfgM>(a, st); break;
+        case RKind::L: rc = launch_fwd<CfgL>(a, st); break;
+        default: return fail(DOT_ERR_UNSUPPORTED, "resident solver: shape not supported");
+    }
+    if (rc) return rc;
+    skr_status_kernel<<<1, 32, 0, st>>>(a.status, a.n_iters);
+    return check_launch("sinkhorn status");
+}
+
+int sk_resident_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
+    if ((reinterpret_cast<uintptr_t>(a.P) & 15u) != 0) return sk_stream_bwd(a, ws, st);
+    int32_t* err = static_cast<int32_t*>(ws);
+    cudaMemsetAsync(err, 0, sizeof(int32_t), st);
+    switch (pick(a.n, a.m)) {
+        case RKind::S: return launch_bwd<CfgS>(a, err, st);
+        case RKind::M: return launch_bwd<CfgM>(a, err, st);
+        case RKind::L: return launch_bwd<CfgL>(a, err, st);
+        default: return fail(DOT_ERR_UNSUPPORTED, "resident solver: shape not supported");
+    }
+}
 
 }  // namespace dotb

@@ -124,8 +124,9 @@ def test_far_columns_take_the_exact_path(B, n, m, reg):
     With |K| up to 400 one ulp of K is 3e-5: on these inputs the reference's
     own two formulations -- its CUDA dual iteration and its CPU primal one --
     differ by up to 1.6e-5 normwise in the plan and 1.2e-4 in the gradient
-    (measured with the oracle's restatements of both).  The tolerances here
-    are about 3x that inherent gap; without the exact path the far columns'
+    (measured with the oracle's restatements of both); the cost, dominated by
+    the C = 200 columns, inherits the plan's gap.  The tolerances here are
+    about 3x that inherent gap; without the exact path the far columns'
     potentials would be infinite."""
     g = U.gen(n + m)
     C = torch.rand(B, n, m, generator=g)
@@ -142,7 +143,7 @@ def test_far_columns_take_the_exact_path(B, n, m, reg):
     r = run_api(C, reg, 20)
     assert np.isfinite(r["P"]).all() and np.isfinite(r["dC"]).all()
     U.assert_normwise(r["P"], P_dual, 5e-5, "plan vs dual form")
-    U.assert_rel(r["cost"], (P_dual.astype(np.float64) * Cn).sum((1, 2)), U.COST_RTOL, "cost", atol=1e-9)
+    U.assert_rel(r["cost"], (P_dual.astype(np.float64) * Cn).sum((1, 2)), 5e-5, "cost", atol=1e-9)
     U.assert_normwise(r["dC"], dC_dual, 4e-4, "dC vs dual form")
     ref = O.sinkhorn_api(Cn, reg, 20, bwd_tol=0.0)
     U.assert_normwise(r["P"], ref["P"], 5e-5, "plan vs primal form")
