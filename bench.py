@@ -53,7 +53,10 @@ CONFIGS = {
                  desc="configs[1]: Sinkhorn fwd+bwd B=256 512x512 normalised sq-dist of N(0,1) 64-D clouds, "
                       "reg 0.05, 200 it, uniform marginals"),
     "cfg3": dict(kind="bidir", B=64, n=1024, m=1024, tau=0.1, dtype="f32",
-                 desc="configs[2]: bidirectional softmax fwd+bwd B=64 1024x1024 N(0,1) scores, tau 0.1"),
+                 desc="configs[2]: bidirectional softmax fwd+bwd B=64 1024x1024 N(0,1) scores, tau 0.1, fp32"),
+    "cfg3bf16": dict(kind="bidir", B=64, n=1024, m=1024, tau=0.1, dtype="bf16",
+                     desc="configs[2]: bidirectional softmax fwd+bwd B=64 1024x1024 N(0,1) scores, tau 0.1, bf16 "
+                          "input (fp32 output and upstream gradient, bf16 input gradient)"),
     "cfg4": dict(kind="sinkhorn", B=4096, n=128, m=128, reg=0.1, iters=100, cost="uniform", marg="dirichlet",
                  desc="configs[3]: Sinkhorn fwd+bwd B=4096 128x128 U[0,1) cost, Dirichlet(1) marginals, "
                       "reg 0.1, 100 it"),
@@ -191,7 +194,22 @@ def run_ours(args, cfg: dict) -> None:
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    inputs = make_inputs(cfg, seed=1234 + rank)
+    rowshard = cfg["kind"] == "sinkhorn_fwd" and world > 1
+    if cfg.get("cost") == "sqdist3u":
+        # one problem (cfg5): the same seeded points on every rank; each rank
+        # builds the cost rows it owns on its GPU (row sharding for world > 1)
+        from dot_b200.distributed import shard_range
+
+        g = torch.Generator(device="cpu")
+        g.manual_seed(1234)
+        x = torch.rand(cfg["B"], cfg["n"], 3, generator=g)
+        y = torch.rand(cfg["B"], cfg["m"], 3, generator=g)
+        lo, hi = shard_range(cfg["n"], rank, world) if rowshard else (0, cfg["n"])
+        C_gpu = torch.cdist(x[:, lo:hi].to(dev), y.to(dev)).square().contiguous()
+        inputs = {"C": C_gpu.cpu()}
+        del C_gpu
+    else:
+        inputs = make_inputs(cfg, seed=1234 + rank)
 
     def barrier():
         if world > 1:
@@ -227,6 +245,11 @@ def run_ours(args, cfg: dict) -> None:
         fwd_only = cfg["kind"] == "sinkhorn_fwd"
 
         def step(C):
+            if rowshard:
+                from dot_b200.distributed import sinkhorn_rowshard
+
+                res = sinkhorn_rowshard(C, cfg["reg"], cfg["iters"], n_total=cfg["n"])
+                return res["cost"].sum()
             Cg = C if fwd_only else C.detach().requires_grad_(True)
             res = dot.sinkhorn(Cg, reg=cfg["reg"], n_iters=cfg["iters"], a=a_dev, b=b_dev, tol=0)
             loss = res.cost.sum()
@@ -282,13 +305,14 @@ def run_ours(args, cfg: dict) -> None:
     ms_e2e = float(t_e2e.item())
 
     units = units_per_step(cfg)
-    value = units * world * args.steps / (ms_max / 1e3)
-    e2e_value = units * world * args.steps / (ms_e2e / 1e3)
+    jobs = 1 if rowshard else world   # row sharding splits one problem; otherwise each rank runs its own batch
+    value = units * jobs * args.steps / (ms_max / 1e3)
+    e2e_value = units * jobs * args.steps / (ms_e2e / 1e3)
     launches = sum(v["launches"] for v in prof.values())
 
     if rank == 0:
         peaks = measured_peaks()
-        roof = roofline(cfg, prof, peaks)
+        roof = roofline(cfg, prof, peaks, args.steps)
         line = {
             "metric": METRIC if cfg["kind"] != "bidir" else "bidirectional softmax fwd+bwd elements/s",
             "value": value,
@@ -298,7 +322,7 @@ def run_ours(args, cfg: dict) -> None:
             "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if rowshard else "weak",
             "vs_baseline": None,
             "dtype": "f32" if cfg.get("dtype", "f32") == "f32" else "bf16-in/f32",
             "data": "synthetic (seeded; shapes and distributions of the BASELINE config)",
@@ -308,7 +332,9 @@ def run_ours(args, cfg: dict) -> None:
                        "per_rank_batch": cfg["B"],
                        "l2": "inputs larger than L2 (126 MB)" if units_per_step(cfg) // max(cfg.get("iters", 1), 1) * 4
                        > 126e6 else "small working set: L2-resident by design (on-chip solver)",
-                       "parallelism": f"batch-independent x{world} (no collective)"},
+                       "parallelism": (f"rows sharded x{world}, NCCL all-reduce of column (max,sum) partials "
+                                       "per iteration" if rowshard else
+                                       f"batch-independent x{world} (no collective)")},
             "e2e": {"value": e2e_value, "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
                     "ms_per_step": ms_e2e / args.steps},
@@ -325,20 +351,21 @@ def run_ours(args, cfg: dict) -> None:
         dist.destroy_process_group()
 
 
-def roofline(cfg: dict, prof: dict, peaks: dict) -> dict:
-    """Dominant kernel class: algorithmic bytes per launch / measured launch time.
+def roofline(cfg: dict, prof: dict, peaks: dict, steps: int) -> dict:
+    """Dominant kernel class: algorithmic bytes / measured kernel time.
 
-    Sinkhorn sweep kernels (row pass, column pass, adjoint row/column mat-vecs)
-    each stream the B x n x m fp32 matrix once: 4 B per element per launch;
-    forward + backward = 4 launches per iteration = 16 B per cost-element-
-    iteration (the survey's sweep model: 8 B/unit forward + 8 B/unit backward).
+    Sinkhorn: every sweep kernel (fused forward iteration, fused adjoint
+    iteration, or one pass of the two-pass path) streams the B x n x m fp32
+    matrix once: 4 B per element per launch.  The resident solver reads the
+    cost once and writes the plan once per call (8 B per element), all
+    iterations on chip; its bound is the SFU, so its roofline is reported
+    against HBM only for completeness.  Bidirectional softmax: compulsory
+    bytes per step, fwd = read sim + write out, bwd = read sim + read grad_out
+    + write grad_sim.
     """
     B, n, m = cfg["B"], cfg["n"], cfg["m"]
     elems = B * n * m
-    cands = []
-    for k, v in prof.items():
-        if v["launches"] and v["ms"] > 0:
-            cands.append((v["ms"], k, v))
+    cands = [(v["ms"], k, v) for k, v in prof.items() if v["launches"] and v["ms"] > 0]
     if not cands:
         return {"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": None,
                 "traffic": None}
@@ -346,33 +373,44 @@ def roofline(cfg: dict, prof: dict, peaks: dict) -> dict:
     ms, k, v = cands[0]
     avg_ms = v["ms"] / v["launches"]
     if k in ("sk_fwd_iter", "sk_bwd_iter"):
-        # per iteration: row launch + column launch (+ a merge launch, which moves
-        # no matrix bytes, when n spans several 512-row column chunks)
-        per_iter = 3 if n > 1024 else 2
-        sweeps = v["launches"] * 2 // per_iter
+        # two-pass path (m > 1024 or m % 4 != 0): row + column launch (+ a merge
+        # launch, which moves no matrix bytes, when n spans several chunks)
+        fused = m <= 1024 and m % 4 == 0
+        per_iter = 1 if fused else (3 if n > 1024 else 2)
+        sweeps = v["launches"] * (1 if fused else 2) // per_iter
         total_bytes = 4 * elems * sweeps
+        bytes_per_launch = total_bytes / v["launches"]
+    elif k == "sk_resident":
+        total_bytes = 20 * elems * steps   # fwd: read C, write P; bwd: read P, read C, write grad
+        bytes_per_launch = total_bytes / v["launches"]
     elif k in ("bs_fwd", "bs_bwd"):
         per = 4 if cfg.get("dtype", "f32") == "f32" else 2
-        total_bytes = ((per + 4) if k == "bs_fwd" else (per + 4 + 4)) * elems
+        per_step = (per + 4) if k == "bs_fwd" else (per + 4 + per)
+        total_bytes = per_step * elems * steps
+        bytes_per_launch = total_bytes / v["launches"]
     else:
         total_bytes = 8 * elems * v["launches"]
+        bytes_per_launch = 8 * elems
     achieved = total_bytes / (v["ms"] / 1e3) / 1e9
     peak = peaks["hbm_gbs"]
     return {"bound": "hbm", "kernel_class": k, "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
-            "launches": v["launches"], "traffic": traffic_from_profiles(k)}
+            "launches": v["launches"], "algorithmic_bytes_per_launch": bytes_per_launch,
+            "traffic": traffic_from_profiles(k, cfg.get("name", ""))}
 
 
-def traffic_from_profiles(kclass: str):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+def traffic_from_profiles(kclass: str, workload: str):
+    """DRAM bytes (read + write) per launch of the dominant kernel, from the
+    committed ncu summary profiles/traffic_per_launch.txt (lines:
+    `<workload> <kernel class> <bytes>`), or None when not captured."""
     path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
     if not os.path.exists(path):
         return None
     with open(path) as f:
         for line in f:
             p = line.split()
-            if len(p) >= 2 and p[0] == kclass:
-                return float(p[1])
+            if len(p) >= 3 and p[0] == workload and p[1] == kclass:
+                return float(p[2])
     return None
 
 
@@ -431,7 +469,7 @@ def cpu_threads() -> int:
 
 def sample_problems(cfg: dict, threads: int, seconds: float) -> int:
     """Problems per CPU sample: about `seconds` of CPU work, at least one per thread."""
-    per_problem = {"cfg1": 0.011, "cfg2": 1.7, "cfg3": 0.12, "cfg4": 0.046, "cfg5": 1e9}
+    per_problem = {"cfg1": 0.011, "cfg2": 1.7, "cfg3": 0.12, "cfg3bf16": 0.12, "cfg4": 0.046, "cfg5": 1e9}
     est = per_problem.get(cfg.get("name", ""), 1.0)
     p = max(threads, int(seconds / est))
     p = (p // threads) * threads if p >= threads else threads
@@ -497,9 +535,13 @@ def main() -> None:
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work per baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--iters", type=int, default=None, help="override the config's iteration count (profiling)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     cfg["name"] = args.config
+    if args.iters is not None and "iters" in cfg:
+        cfg["iters"] = args.iters
+        cfg["desc"] += f" (run with {args.iters} iterations)"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -213,6 +213,86 @@ int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P, const flo
     return sk_stream_bwd(a, workspace, st);
 }
 
+int dot_sinkhorn_rows(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n, int64_t m,
+                      int64_t n_total, float tau, const float* pot_v, float* pot_u, void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (n_total < n) return fail(DOT_ERR_INVALID, "n_total must be >= the shard's row count");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !pot_v || !pot_u) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    return sk_split_rows(X, score_sign * (1.0f / tau), log_a, -logf(float(n_total)), B, n, m, pot_v, pot_u,
+                         static_cast<cudaStream_t>(stream));
+}
+
+size_t dot_sinkhorn_col_partials_workspace_bytes(int64_t B, int64_t n, int64_t m) {
+    if (B <= 0 || n <= 0 || m <= 0) return 0;
+    return sk_split_colpart_ws(B, n, m);
+}
+
+int dot_sinkhorn_col_partials(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n, int64_t m,
+                              float tau, float* col_max, float* col_sum, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !pot_u || !col_max || !col_sum) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    const size_t need = sk_split_colpart_ws(B, n, m);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    return sk_split_colpart(X, score_sign * (1.0f / tau), pot_u, B, n, m, col_max, col_sum, workspace,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int dot_sinkhorn_col_rescale(const float* col_max, float* col_sum, const float* global_max, int64_t count,
+                             void* stream) {
+    clear_error();
+    if (count < 0) return fail(DOT_ERR_INVALID, "negative count");
+    if (count == 0) return DOT_OK;
+    if (!col_max || !col_sum || !global_max) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    return sk_split_rescale(col_max, col_sum, global_max, count, static_cast<cudaStream_t>(stream));
+}
+
+int dot_sinkhorn_col_finish(const float* global_max, const float* global_sum, const float* log_b, int64_t B,
+                            int64_t m, float* pot_v, void* stream) {
+    clear_error();
+    if (B < 0 || m < 0) return fail(DOT_ERR_INVALID, "negative dimension");
+    if (B == 0 || m == 0) return DOT_OK;
+    if (!global_max || !global_sum || !pot_v) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    return sk_split_finish(global_max, global_sum, log_b, -logf(float(m)), B * m, pot_v,
+                           static_cast<cudaStream_t>(stream));
+}
+
+size_t dot_sinkhorn_plan_workspace_bytes(int64_t B, int64_t n, int64_t m) {
+    (void)m;
+    if (B <= 0 || n <= 0) return 0;
+    return sk_split_plan_ws(B, n);
+}
+
+int dot_sinkhorn_plan(const float* X, float score_sign, const float* pot_u, const float* pot_v, int64_t B, int64_t n,
+                      int64_t m, float tau, int out_mode, float* out, float* cost, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (out_mode != 0 && out_mode != 1) return fail(DOT_ERR_INVALID, "out_mode must be 0 or 1");
+    if (cost != nullptr && out_mode != 0) return fail(DOT_ERR_INVALID, "cost requires out_mode 0");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !pot_u || !pot_v || !out) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    const size_t need = cost ? sk_split_plan_ws(B, n) : 0;
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    return sk_split_plan(X, score_sign * (1.0f / tau), pot_u, pot_v, B, n, m, out_mode, out, cost, workspace,
+                         static_cast<cudaStream_t>(stream));
+}
+
 size_t dot_bidir_fwd_workspace_bytes(int64_t B, int64_t L1, int64_t L2) {
     if (B <= 0 || L1 <= 0 || L2 <= 0) return 0;
     return bs_fwd_ws(B, L1, L2);

@@ -62,6 +62,19 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 size_t sk_stream_bwd_ws(int64_t B, int64_t n, int64_t m);
 int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
 
+// Split half-steps for row-sharded problems (sinkhorn_stream.cu).
+int sk_split_rows(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
+                  const float* v2, float* u2, cudaStream_t st);
+size_t sk_split_colpart_ws(int64_t B, int64_t n, int64_t m);
+int sk_split_colpart(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m,
+                     float* col_max, float* col_sum, void* ws, cudaStream_t st);
+int sk_split_rescale(const float* col_max, float* col_sum, const float* gmax, int64_t count, cudaStream_t st);
+int sk_split_finish(const float* gmax, const float* gsum, const float* lb, float lb_def, int64_t count, float* v2,
+                    cudaStream_t st);
+size_t sk_split_plan_ws(int64_t B, int64_t n);
+int sk_split_plan(const float* X, float kinv, const float* u2, const float* v2, int64_t B, int64_t n, int64_t m,
+                  int out_mode, float* out, float* cost, void* ws, cudaStream_t st);
+
 // On-chip resident solvers (one CTA per problem).  *_supported() tells whether
 // a shape has a resident configuration; the entry points then need the same
 // workspace as reported by *_ws().

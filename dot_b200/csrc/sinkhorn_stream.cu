@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kColWarps * 32)
 sk_col_kernel(const float* __restrict__ X, float kinv, const float* __restrict__ u2,
               const float* __restrict__ lb, float lb_def, float* __restrict__ v2,
               float2* __restrict__ part, int64_t n, int64_t m, int64_t rows_per_chunk,
-              int chunks, SkCtl ctl) {
+              int chunks, SkCtl ctl, float2* __restrict__ pair_out) {
     __shared__ float sm_M[kColWarps][kColTile];
     __shared__ float sm_S[kColWarps][kColTile];
     if (ctl_done(ctl)) return;
@@ -196,18 +196,16 @@ sk_col_kernel(const float* __restrict__ X, float kinv, const float* __restrict__
 #pragma unroll
         for (int w = 1; w < kColWarps; ++w) lse_merge(mm, ss, sm_M[w][ci], sm_S[w][ci]);
         if (col < m) {
-            if (chunks == 1) {
-                v2[b * m + col] = (lb ? lb[b * m + col] : lb_def) - lse_finish(mm, ss);
-            } else {
-                part[(b * chunks + chunk) * m + col] = make_float2(mm, ss);
-            }
+            if (chunks > 1) part[(b * chunks + chunk) * m + col] = make_float2(mm, ss);
+            else if (pair_out != nullptr) pair_out[b * m + col] = make_float2(mm, ss);
+            else v2[b * m + col] = (lb ? lb[b * m + col] : lb_def) - lse_finish(mm, ss);
         }
     }
 }
 
 __global__ void sk_col_merge_kernel(const float2* __restrict__ part, const float* __restrict__ lb,
                                     float lb_def, float* __restrict__ v2, int64_t B, int64_t m,
-                                    int chunks, SkCtl ctl) {
+                                    int chunks, SkCtl ctl, float2* __restrict__ pair_out) {
     if (ctl_done(ctl)) return;
     const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= B * m) return;
@@ -217,7 +215,35 @@ __global__ void sk_col_merge_kernel(const float2* __restrict__ part, const float
         const float2 p = part[(b * chunks + c) * m + col];
         lse_merge(mm, ss, p.x, p.y);
     }
-    v2[idx] = (lb ? lb[idx] : lb_def) - lse_finish(mm, ss);
+    if (pair_out != nullptr) pair_out[idx] = make_float2(mm, ss);
+    else v2[idx] = (lb ? lb[idx] : lb_def) - lse_finish(mm, ss);
+}
+
+// (max, sum) pairs -> two arrays (the form the shard all-reduces take).
+__global__ void sk_pair_unpack_kernel(const float2* __restrict__ pair, float* __restrict__ max_out,
+                                      float* __restrict__ sum_out, int64_t count) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const float2 p = pair[i];
+    max_out[i] = p.x;
+    sum_out[i] = p.y;
+}
+
+// Shard combine, step 1 (array form): sum_j *= exp(max_local_j - max_global_j).
+__global__ void sk_pair_rescale_kernel(const float* __restrict__ lmax, float* __restrict__ lsum,
+                                       const float* __restrict__ gmax, int64_t count) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    lsum[i] = lsum[i] * exp_shift(lmax[i] - gmax[i]);
+}
+
+// Shard combine, step 2: v_j = lb_j - (max_j + log(max(sum_j, 1e-12))).
+__global__ void sk_col_finish_kernel(const float* __restrict__ gmax, const float* __restrict__ gsum,
+                                     const float* __restrict__ lb, float lb_def, float* __restrict__ v2,
+                                     int64_t count) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    v2[i] = (lb ? lb[i] : lb_def) - lse_finish(gmax[i], gsum[i]);
 }
 
 // ---------------------------------------------------------------------------
@@ -599,12 +625,12 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
         {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
             sk_col_kernel<<<col_grid, kColWarps * 32, 0, st>>>(a.X, a.kinv, a.u2, a.lb, a.lb_def, a.v2,
-                                                               w.part, a.n, a.m, rpc, chunks, ctl);
+                                                               w.part, a.n, a.m, rpc, chunks, ctl, nullptr);
         }
         if (chunks > 1) {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
             sk_col_merge_kernel<<<merge_grid, 256, 0, st>>>(w.part, a.lb, a.lb_def, a.v2, a.B, a.m,
-                                                            chunks, ctl);
+                                                            chunks, ctl, nullptr);
         }
     }
     {
@@ -719,6 +745,87 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
                                                                         -1.0f / a.tau);
     }
     return check_launch("sinkhorn backward (streaming)");
+}
+
+
+// ---------------------------------------------------------------------------
+// split half-steps for row-sharded problems (host combines column partials
+// across shards between them)
+// ---------------------------------------------------------------------------
+
+int sk_split_rows(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
+                  const float* v2, float* u2, cudaStream_t st) {
+    const int64_t rows = B * n;
+    SkCtl ctl{nullptr, nullptr, 0.0f, 0};
+    ProfScope ps(DOT_K_SK_FWD_ITER, st);
+    sk_row_kernel<<<unsigned(ceil_div(rows, kRowsPerCta)), kRowThreads, 0, st>>>(X, kinv, v2, la, la_def, u2, rows,
+                                                                                 n, m, ctl);
+    return check_launch("sinkhorn row half-step");
+}
+
+size_t sk_split_colpart_ws(int64_t B, int64_t n, int64_t m) {
+    Carve c(nullptr);
+    const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
+    c.take<float2>(size_t(B * m));
+    if (chunks > 1) c.take<float2>(size_t(B * chunks * m));
+    return c.size();
+}
+
+int sk_split_colpart(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m,
+                     float* col_max, float* col_sum, void* ws, cudaStream_t st) {
+    Carve c(ws);
+    float2* pair = c.take<float2>(size_t(B * m));
+    const int64_t rpc = col_rows_per_chunk(n);
+    const int chunks = int(ceil_div(n, rpc));
+    float2* part = chunks > 1 ? c.take<float2>(size_t(B * chunks * m)) : nullptr;
+    SkCtl ctl{nullptr, nullptr, 0.0f, 0};
+    const dim3 col_grid(unsigned(ceil_div(m, kColTile)), unsigned(chunks), unsigned(B));
+    {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st);
+        sk_col_kernel<<<col_grid, kColWarps * 32, 0, st>>>(X, kinv, u2, nullptr, 0.0f, nullptr, part, n, m, rpc,
+                                                           chunks, ctl, pair);
+    }
+    if (chunks > 1) {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st);
+        sk_col_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(part, nullptr, 0.0f, nullptr, B, m,
+                                                                            chunks, ctl, pair);
+    }
+    sk_pair_unpack_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pair, col_max, col_sum, B * m);
+    return check_launch("sinkhorn column partials");
+}
+
+int sk_split_rescale(const float* col_max, float* col_sum, const float* gmax, int64_t count, cudaStream_t st) {
+    sk_pair_rescale_kernel<<<unsigned(ceil_div(count, 256)), 256, 0, st>>>(col_max, col_sum, gmax, count);
+    return check_launch("sinkhorn column rescale");
+}
+
+int sk_split_finish(const float* gmax, const float* gsum, const float* lb, float lb_def, int64_t count, float* v2,
+                    cudaStream_t st) {
+    sk_col_finish_kernel<<<unsigned(ceil_div(count, 256)), 256, 0, st>>>(gmax, gsum, lb, lb_def, v2, count);
+    return check_launch("sinkhorn column finish");
+}
+
+size_t sk_split_plan_ws(int64_t B, int64_t n) {
+    Carve c(nullptr);
+    c.take<float>(size_t(B * n));
+    return c.size();
+}
+
+int sk_split_plan(const float* X, float kinv, const float* u2, const float* v2, int64_t B, int64_t n, int64_t m,
+                  int out_mode, float* out, float* cost, void* ws, cudaStream_t st) {
+    Carve c(ws);
+    float* cost_row = cost ? c.take<float>(size_t(B * n)) : nullptr;
+    const int64_t rows = B * n;
+    {
+        ProfScope ps(DOT_K_SK_FWD_EPI, st);
+        sk_plan_kernel<<<unsigned(ceil_div(rows, kRowsPerCta)), kRowThreads, 0, st>>>(X, kinv, u2, v2, out, out_mode,
+                                                                                      cost_row, rows, n, m);
+    }
+    if (cost != nullptr) {
+        ProfScope ps(DOT_K_SK_FWD_EPI, st);
+        sk_batch_sum_kernel<<<unsigned(ceil_div(B, 8)), 256, 0, st>>>(cost_row, cost, B, n, 1.0f);
+    }
+    return check_launch("sinkhorn plan");
 }
 
 }  // namespace dotb

@@ -146,6 +146,42 @@ DOT_API int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P,
                      size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Sinkhorn half-steps for problems whose rows are sharded across GPUs       */
+/* ------------------------------------------------------------------------ */
+/*
+ * One forward iteration of dot_sinkhorn_fwd split at its only exchange point,
+ * for a shard holding rows [r0, r0 + n) of each problem's n_total x m matrix.
+ * Per iteration every shard runs
+ *     dot_sinkhorn_rows          u_i = log_a_i - LSE_j(K_ij + v_j)      (local rows)
+ *     dot_sinkhorn_col_partials  (max_j, sum_j) of LSE_i(K_ij + u_i)     (local rows)
+ *     all-reduce MAX of max_j -> gmax_j   (caller, e.g. NCCL)
+ *     dot_sinkhorn_col_rescale   sum_j *= exp(max_j - gmax_j)
+ *     all-reduce SUM of sum_j -> gsum_j   (caller)
+ *     dot_sinkhorn_col_finish    v_j = log_b_j - (gmax_j + log(max(gsum_j, 1e-12)))
+ * and finally dot_sinkhorn_plan for its rows (plus an all-reduce SUM of the
+ * per-shard costs).  Same arithmetic as the reference's row/column update
+ * kernels (src/sinkhorn/kernels.cu:503-545, 629-753 -- its split-column
+ * phase1/phase2 merge is the same max-then-rescaled-sum combine) and
+ * materialisation (kernels.cu:755-775); the reference itself has no
+ * multi-GPU path.
+ */
+DOT_API int dot_sinkhorn_rows(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n,
+                              int64_t m, int64_t n_total, float tau, const float* pot_v, float* pot_u,
+                              void* stream);
+DOT_API size_t dot_sinkhorn_col_partials_workspace_bytes(int64_t B, int64_t n, int64_t m);
+DOT_API int dot_sinkhorn_col_partials(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n,
+                                      int64_t m, float tau, float* col_max, float* col_sum, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+DOT_API int dot_sinkhorn_col_rescale(const float* col_max, float* col_sum, const float* global_max,
+                                     int64_t count, void* stream);
+DOT_API int dot_sinkhorn_col_finish(const float* global_max, const float* global_sum, const float* log_b,
+                                    int64_t B, int64_t m, float* pot_v, void* stream);
+DOT_API size_t dot_sinkhorn_plan_workspace_bytes(int64_t B, int64_t n, int64_t m);
+DOT_API int dot_sinkhorn_plan(const float* X, float score_sign, const float* pot_u, const float* pot_v, int64_t B,
+                              int64_t n, int64_t m, float tau, int out_mode, float* out, float* cost,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Bidirectional softmax                                                     */
 /* ------------------------------------------------------------------------ */
 

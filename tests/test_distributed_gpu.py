@@ -1,0 +1,62 @@
+"""Row-sharded Sinkhorn over NCCL (2 ranks, one GPU each) against the
+single-GPU forward on the same problem.  Needs >= 2 GPUs; skipped otherwise."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from dot_b200 import ops
+    from dot_b200.distributed import shard_range, sinkhorn_rowshard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        g = torch.Generator().manual_seed(0)
+        B, n, m, reg, T = 2, 1030, 2000, 0.05, 30
+        C = torch.rand(B, n, m, generator=g)
+        lo, hi = shard_range(n, rank, world)
+        res = sinkhorn_rowshard(C[:, lo:hi].cuda(), reg, T, n_total=n)
+        torch.cuda.synchronize()
+        P_ref, cost_ref, u_ref, v_ref, _ = ops.sinkhorn_forward_raw(C.cuda(), -1.0, reg, T, want_cost=True)
+        torch.cuda.synchronize()
+        dP = (res["P"] - P_ref[:, lo:hi]).abs().amax().item() / P_ref.abs().amax().item()
+        dv = (res["v"] - v_ref).abs().amax().item()
+        dc = ((res["cost"] - cost_ref).abs() / cost_ref.abs()).amax().item()
+        out[rank] = (dP, dv, dc)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_rowshard_two_gpus_matches_single_gpu():
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    assert len(out) == world
+    for rank, (dP, dv, dc) in out.items():
+        assert dP < 1e-5, (rank, dP)
+        assert dv < 1e-4, (rank, dv)
+        assert dc < 1e-5, (rank, dc)
