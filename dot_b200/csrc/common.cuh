@@ -74,9 +74,31 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 template <int W>
 __device__ __forceinline__ float warp_max(float v) {
+    if constexpr (W == 32) {
+        // one instruction on sm_100a (redux.sync with .f32, PTX ISA 8.6); max is
+        // exact, so this equals the shuffle tree bit for bit
+        float r;
+        asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+        return r;
+    } else {
 #pragma unroll
-    for (int off = W / 2; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-    return v;
+        for (int off = W / 2; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        return v;
+    }
+}
+
+// Sum of N registers as a balanced tree (short dependency chain).
+template <int N>
+__device__ __forceinline__ float tree_sum(const float (&x)[N]) {
+    if constexpr (N == 1) {
+        return x[0];
+    } else {
+        float h[(N + 1) / 2];
+#pragma unroll
+        for (int k = 0; k < N / 2; ++k) h[k] = x[2 * k] + x[2 * k + 1];
+        if constexpr (N % 2 == 1) h[N / 2] = x[N - 1];
+        return tree_sum<(N + 1) / 2>(h);
+    }
 }
 
 // Online update of a (max, sum) partial with a group of K new values

@@ -269,13 +269,9 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_fwd_iter_kernel(F
             for (int e = 0; e < NC; ++e) mx = fmaxf(mx, t[e]);
             // row LSE, max pass then sum pass (the reference's two-pass order)
             mx = warp_max<32>(mx);
-            float s = 0.0f;
 #pragma unroll
-            for (int e = 0; e < NC; ++e) {
-                t[e] = exp_shift(t[e] - mx);   // t now holds E_ij
-                s += t[e];
-            }
-            s = warp_sum<32>(s);
+            for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);   // t now holds E_ij
+            const float s = warp_sum<32>(tree_sum(t));
             const int64_t grow = row0 + int64_t(j) * R + i;
             const float unew = (a.la ? a.la[grow] : a.la_def) - lse_finish(mx, s);
             if (lane == 0) {
