@@ -13,6 +13,8 @@
 // accumulates row and column terms with atomicAdd (kernels.cu:277-361).
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -432,20 +434,32 @@ int bs_bwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int
 
 }  // namespace
 
+// fused passes (bidir_fused.cu) for L2 <= 1024, L2 % 4 == 0
+bool bsf_supported(int64_t L2, const void* sim, int dtype, const void* gout, const void* gsim);
+size_t bsf_fwd_ws(int64_t B, int64_t L1, int64_t L2);
+size_t bsf_bwd_ws(int64_t B, int64_t L1, int64_t L2);
+int bsf_fwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau,
+            float* out, float* row_stats, float* col_stats, void* ws, cudaStream_t st);
+int bsf_bwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau,
+            const float* row_stats, const float* col_stats, const float* gout, void* gsim, int gdtype, float* gtau,
+            void* ws, cudaStream_t st);
+
 size_t bs_fwd_ws(int64_t B, int64_t L1, int64_t L2) {
     Carve c(nullptr);
     carve_bs_fwd(c, B, L1, L2);
-    return c.size();
+    return std::max(c.size(), bsf_fwd_ws(B, L1, L2));
 }
 
 size_t bs_bwd_ws(int64_t B, int64_t L1, int64_t L2) {
     Carve c(nullptr);
     carve_bs_bwd(c, B, L1, L2);
-    return c.size();
+    return std::max(c.size(), bsf_bwd_ws(B, L1, L2));
 }
 
 int bs_fwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2,
            float tau, float* out, float* row_stats, float* col_stats, void* ws, cudaStream_t st) {
+    if (bsf_supported(L2, sim, dtype, nullptr, out))
+        return bsf_fwd(sim, dtype, lengths, B, L1, L2, tau, out, row_stats, col_stats, ws, st);
     float2* rs = reinterpret_cast<float2*>(row_stats);
     float2* cs = reinterpret_cast<float2*>(col_stats);
     if (dtype == DOT_F32)
@@ -456,6 +470,8 @@ int bs_fwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_
 int bs_bwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau,
            const float* row_stats, const float* col_stats, const float* gout, void* gsim, int gdtype,
            float* gtau, void* ws, cudaStream_t st) {
+    if (bsf_supported(L2, sim, dtype, gout, gsim))
+        return bsf_bwd(sim, dtype, lengths, B, L1, L2, tau, row_stats, col_stats, gout, gsim, gdtype, gtau, ws, st);
     const float2* rs = reinterpret_cast<const float2*>(row_stats);
     const float2* cs = reinterpret_cast<const float2*>(col_stats);
     if (dtype == DOT_F32) {
