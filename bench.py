@@ -127,35 +127,61 @@ def units_per_step(cfg: dict) -> int:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi sampling every 100 ms, started before the warm-up (the tool
+    takes a moment to print its first sample) and stopped after the timed
+    region; only samples whose timestamp falls inside the marked region count.
+    A region shorter than the sampling period falls back to the samples within
+    0.5 s of it, and says so."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def __exit__(self, *exc):
+    def mark_begin(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
         if self.proc is not None:
+            time.sleep(0.25)   # let the sample covering the region's end land
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.fh.close()
+
+    @staticmethod
+    def _stamp(s: str):
+        import datetime
+
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
+            try:
+                return datetime.datetime.strptime(s.strip(), fmt).timestamp()
+            except ValueError:
+                pass
+        return None
 
     def summary(self) -> dict:
         if self.proc is None or self.path is None:
@@ -164,18 +190,31 @@ class ClockSampler:
         with open(self.path) as f:
             for line in f:
                 p = [x.strip() for x in line.split(",")]
-                if len(p) >= 9:
-                    rows.append(p)
+                if len(p) >= 10:
+                    rows.append((self._stamp(p[0]), p[1:]))
         os.unlink(self.path)
-        if not rows:
+        inside = [r for t, r in rows if t is not None and self.t0 is not None and self.t0 <= t <= self.t1]
+        window = "timed region"
+        if not inside:
+            inside = [r for t, r in rows if t is not None and self.t0 is not None
+                      and self.t0 - 0.5 <= t <= self.t1 + 0.5]
+            window = "within 0.5 s of the timed region (region shorter than the 100 ms sampling period)"
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [v for v in (num(r[1]) for r in inside) if v is not None]
+        mx = [v for v in (num(r[2]) for r in inside) if v is not None]
+        pw = [v for v in (num(r[3]) for r in inside) if v is not None]
+        reasons = sorted({self.REASONS[k] for r in inside for k in range(4) if r[5 + k].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+                "reasons": reasons, "samples": len(inside), "window": window,
+                "power_w_max": max(pw) if pw else None}
 
 
 # ---------------------------------------------------------------------------
@@ -264,6 +303,7 @@ def run_ours(args, cfg: dict) -> None:
         step_dev = lambda: step(C_dev)  # noqa: E731
         h2d = C_host.numel() * 4
 
+    clocks = ClockSampler(local_rank).start()
     for _ in range(args.warmup):
         step_dev()
     torch.cuda.synchronize()
@@ -274,12 +314,14 @@ def run_ours(args, cfg: dict) -> None:
     barrier()
     torch.cuda.synchronize()
     _lib.prof_begin(time_events=True)
-    with ClockSampler(local_rank) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step_dev()
-        ev1.record(stream)
-        torch.cuda.synchronize()
+    clocks.mark_begin()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step_dev()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    clocks.stop()
     prof = _lib.prof_end()
     barrier()
     ms = ev0.elapsed_time(ev1)
@@ -289,6 +331,7 @@ def run_ours(args, cfg: dict) -> None:
     ms_max = float(t_local.item())
 
     # ---- timed region (end to end from pinned host memory) ----
+    step_e2e().item()   # untimed: first use of the e2e path's allocations
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -71,10 +71,10 @@ cudaEvent_t take_event(Prof& p) {
 }
 }  // namespace
 
-void prof_pre(int k, cudaStream_t s) {
+void prof_pre(int k, cudaStream_t s, int count) {
     Prof& p = prof();
     std::lock_guard<std::mutex> g(p.mu);
-    p.launches[k] += 1;
+    p.launches[k] += count;
     if (p.timing) {
         cudaEvent_t a = take_event(p);
         cudaEventRecord(a, s);

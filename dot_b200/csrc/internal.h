@@ -21,13 +21,15 @@ int check_launch(const char* what);
 // ---- launch accounting ------------------------------------------------------
 // Every kernel launch goes through prof_pre/prof_post with its class.  The
 // counters are always on; event timing only between dot_prof_begin/end.
-void prof_pre(int kclass, cudaStream_t s);
+// A scope may cover several launches of one class (`count`): its events then
+// time the whole run of launches, gaps included.
+void prof_pre(int kclass, cudaStream_t s, int count = 1);
 void prof_post(int kclass, cudaStream_t s);
 
 struct ProfScope {
     int k;
     cudaStream_t s;
-    ProfScope(int kclass, cudaStream_t st) : k(kclass), s(st) { prof_pre(k, s); }
+    ProfScope(int kclass, cudaStream_t st, int count = 1) : k(kclass), s(st) { prof_pre(k, s, count); }
     ~ProfScope() { prof_post(k, s); }
 };
 

@@ -46,16 +46,28 @@ struct SkBwdArgs {
 
 // Fused single-pass iteration kernels (sinkhorn_fused.cu) for m <= 1024,
 // m % 4 == 0, 16-byte aligned data.
+// Persistent balanced schedule: the B*nblk row blocks are split into G equal
+// contiguous ranges, one per CTA (G = CTAs resident at once).
 struct FusedPlan {
-    int nseg = 1;          // segments (CTAs) per problem
-    int64_t seg_rows = 0;  // rows per segment
+    int nseg = 1;              // segment slots per problem in the partial buffers (= maxseg)
+    int G = 1;                 // CTAs
+    int64_t nblk = 1;          // row blocks per problem
+    int64_t total_blocks = 1;  // B * nblk
+    int maxseg = 1;            // most CTAs whose ranges touch one problem
+    int keep = 0;              // leading blocks per CTA range copied with L2 evict_last
+    int stages = 2;            // bulk-copy pipeline depth
 };
-bool sk_fused_supported(int64_t n, int64_t m, const void* data);
+bool sk_fused_shape_ok(int64_t B, int64_t n, int64_t m);
+bool sk_fused_supported(int64_t B, int64_t n, int64_t m, const void* data);
 FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m);
+// first: launched without programmatic dependency (the previous stream work
+// writes what the kernel reads before its dependency wait); last: plain
+// copies, which leave the L2 keep set at normal priority.
 int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta,
-                      int iter, cudaStream_t st);
+                      int iter, bool first, bool last, cudaStream_t st);
 int sk_fused_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv, const float2* cinv,
-                      float* lam, float* mu, float* part, int32_t* cnt, int32_t* err, cudaStream_t st);
+                      float* lam, float* mu, float* part, int32_t* cnt, int32_t* err, bool first, bool last,
+                      cudaStream_t st);
 
 size_t sk_stream_fwd_ws(int64_t B, int64_t n, int64_t m, int n_iters, float tol, bool want_cost);
 int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);

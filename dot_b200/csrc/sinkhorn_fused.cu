@@ -3,7 +3,7 @@
 // One kernel launch per iteration reads the B x n x m matrix once (the
 // streaming two-kernel path in sinkhorn_stream.cu reads it twice):
 //
-//   forward   for each row i of the CTA's rows:   u_i = la_i - LSE_j(K_ij + v_j)
+//   forward   for each row i:   u_i = la_i - LSE_j(K_ij + v_j)
 //             then, with the fresh u, per-column partials of LSE_i(K_ij + u_i)
 //   backward  lambda_i = (sum_k P G - sum_k P_ik mu_k) / max(sum_k P, 1e-12)
 //             then per-column partials of sum_i P_ik lambda_i
@@ -12,17 +12,30 @@
 // v from the new u: src/sinkhorn/torch_cuda.cpp:200-223; lambda from the
 // previous mu, mu from the new lambda: kernels.cu:1715-1718).
 //
-// Work decomposition: grid (nseg, B); a CTA owns a segment of consecutive
-// rows of one problem and streams it through shared memory in row blocks of
-// R rows (R*m <= 8192 floats, 32 KB) with double-buffered 1-D bulk copies
-// (cp.async.bulk, the TMA engine) completing on mbarriers.  Warp per row; each
-// lane owns fixed columns, so after its row's reduction it folds the same
-// registers into its columns' running partials (no second pass over shared
-// memory).  At the end of its segment a CTA merges its warps' partials and
-// publishes them; the last CTA of the problem to finish (atomic arrival
-// counter, no waiting) merges the nseg partials in segment order and writes v
+// Work decomposition (persistent, balanced): every problem is cut into row
+// blocks of R rows (R*m <= 8192 floats, 32 KB); the B*nblk blocks, in memory
+// order, are split into G contiguous ranges of equal length, one per CTA,
+// with G = the number of CTAs the GPU holds at once (one wave).  A CTA
+// streams its range through shared memory with an S-stage ring of 1-D bulk
+// copies (cp.async.bulk, the TMA engine) completing on mbarriers.  Warp per
+// row; each lane owns fixed columns, so after its row's reduction it folds
+// the same registers into its columns' running partials.  When the CTA's
+// range leaves a problem (or ends), it merges its warps' partials through the
+// just-consumed stage buffer and publishes them as that problem's segment
+// partial; the CTA that arrives last for a problem (atomic arrival counter,
+// no waiting) merges the problem's segments in segment order and writes v
 // (or mu), so results are deterministic.  The next launch consumes them.
+//
+// Launches of consecutive iterations overlap through programmatic dependent
+// launch: a CTA initialises its barriers and starts its first bulk copies of
+// the (read-only) matrix, then waits for the previous iteration's grid before
+// reading the potentials.  When the matrix is larger than L2, a fixed leading
+// part of every CTA's range can be copied with an L2 evict_last policy and
+// the rest with evict_first, so that the kept part is served from L2 on the next
+// iteration (opt-in, DOT_B200_L2_KEEP_MB).  The last iteration uses no hint,
+// which leaves the kept lines at normal priority.
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -35,20 +48,37 @@ namespace {
 
 constexpr int kFT = 256;              // threads per CTA
 constexpr int kFW = kFT / 32;         // warps per CTA
-constexpr int kTileFloats = 8192;     // one row-block buffer (32 KB)
-constexpr size_t kFusedSmem = 2 * kTileFloats * sizeof(float);
+constexpr int kTileFloats = 8192;     // one stage buffer (32 KB)
+constexpr int kMergeCols = 512;       // columns merged per round (kFW * 512 * 8 B = 32 KB)
 
 template <int VPL>
 struct FCfg {
     static constexpr int R = 64 / VPL;    // rows per block (R * 128 * VPL floats = 32 KB)
     static constexpr int RPW = R / kFW;   // rows per warp per block
+    static constexpr int NC = 4 * VPL;    // columns per lane
 };
+
+// Balanced schedule: CTA k owns blocks [q(k), q(k+1)), q(k) = floor(k*T/G).
+struct Sched {
+    int T;           // total blocks B * nblk (< 2^31: sk_fused_supported)
+    int nblk;        // blocks per problem
+    int G;           // CTAs
+    int maxseg;      // max segments (CTAs) touching one problem
+    int keep;        // leading blocks of each range copied with evict_last
+    int hint;        // 0: plain copies; 1: evict_last / evict_first split
+};
+
+__host__ __device__ __forceinline__ int sched_q(const Sched& s, int k) { return int(int64_t(k) * s.T / s.G); }
+// The CTA whose range contains block x: the largest k with q(k) <= x.
+__host__ __device__ __forceinline__ int sched_owner(const Sched& s, int x) {
+    return int((int64_t(x + 1) * s.G + s.T - 1) / s.T) - 1;
+}
 
 struct FusedCommon {
     const float* data;   // X (forward) or P (backward), [B, n, m]
     int64_t n, m;
-    int64_t seg_rows;    // rows per segment (multiple of R)
-    int nseg;
+    int R;               // rows per block
+    Sched s;
     int32_t* cnt;        // [B] arrival counters, zero between launches
     int32_t* err;        // device error word (bounded-wait timeouts)
 };
@@ -62,7 +92,7 @@ struct FwdIter {
     float lb_def;
     float* u2;
     float* v2;
-    float2* part;        // [B, nseg, m] column (max, sum) partials
+    float2* part;        // [B, maxseg, m] column (max, sum) partials
     float* delta;        // tol > 0: per-iteration max |du|; else nullptr
     int32_t* status;
     float tol;
@@ -75,87 +105,85 @@ struct BwdIter {
     const float2* cinv;  // [B, m] (sum_i P G, sum_i P)
     float* lam;
     float* mu;
-    float* part;         // [B, nseg, m] column sums
+    float* part;         // [B, maxseg, m] column sums
 };
 
-// Double-buffered row-block stream of one CTA's segment.
-struct BlockStream {
-    float* buf0;         // buffer k at buf0 + k * kTileFloats
-    uint64_t* bar;
-    const float* src;    // first row of the segment
-    int64_t rows, m;
-    int R;
+// S-stage ring over the CTA's block range [g0, g1).  Only the range bounds
+// live in registers; shapes and schedule come from the kernel parameters.
+template <int S>
+struct Ring {
+    const FusedCommon* c;
+    unsigned char* smem; // stage k at smem + k * 32 KB
+    uint64_t* bar;       // S mbarriers
+    int g0, g1;
 
-    __device__ int nblk() const { return int((rows + R - 1) / R); }
-    __device__ int rows_in(int j) const { return int(min(int64_t(R), rows - int64_t(j) * R)); }
-    __device__ float* buf(int j) const { return buf0 + (j & 1) * kTileFloats; }
-    __device__ void issue(int j) const {   // one thread
-        const uint32_t bytes = uint32_t(rows_in(j)) * uint32_t(m) * 4u;
-        uint64_t* b = bar + (j & 1);
-        mbar_arrive_expect_tx(b, bytes);
-        bulk_g2s(buf(j), src + int64_t(j) * R * m, bytes, b);
+    __device__ float* buf(int g) const {
+        return reinterpret_cast<float*>(smem) + int((g - g0) % S) * kTileFloats;
     }
+    __device__ uint64_t* barrier(int g) const { return bar + (g - g0) % S; }
+    __device__ uint32_t parity(int g) const { return uint32_t(((g - g0) / S) & 1); }
+    __device__ int rows_in(int g) const {
+        const int jb = g % c->s.nblk;
+        return int(min(int64_t(c->R), c->n - int64_t(jb) * c->R));
+    }
+    __device__ void issue(int g) const {   // one thread
+        const int b = g / c->s.nblk, jb = g - b * c->s.nblk;
+        const uint32_t bytes = uint32_t(rows_in(g)) * uint32_t(c->m) * 4u;
+        const float* src = c->data + (int64_t(b) * c->n + int64_t(jb) * c->R) * c->m;
+        uint64_t* bb = barrier(g);
+        mbar_arrive_expect_tx(bb, bytes);
+        if (c->s.hint) {
+            const uint64_t pol = (g - g0) < c->s.keep ? l2_policy_evict_last() : l2_policy_evict_first();
+            bulk_g2s_hint(buf(g), src, bytes, bb, pol);
+        } else {
+            bulk_g2s(buf(g), src, bytes, bb);
+        }
+    }
+    __device__ bool wait(int g, int32_t* err) const { return mbar_wait_sleep(barrier(g), parity(g), err); }
 };
 
-// Shared prologue: barriers, first two copies.
-__device__ __forceinline__ BlockStream stream_begin(const FusedCommon& c, int R, uint64_t* bars,
-                                                    unsigned char* smem) {
-    BlockStream s;
-    s.buf0 = reinterpret_cast<float*>(smem);
-    s.bar = bars;
-    const int64_t b = blockIdx.y;
-    const int64_t r0 = int64_t(blockIdx.x) * c.seg_rows;
-    s.rows = min(c.n, r0 + c.seg_rows) - r0;
-    s.m = c.m;
-    s.R = R;
-    s.src = c.data + (b * c.n + r0) * c.m;
+template <int S>
+__device__ __forceinline__ Ring<S> ring_init(const FusedCommon& c, uint64_t* bars, unsigned char* smem) {
+    Ring<S> r;
+    r.c = &c;
+    r.smem = smem;
+    r.bar = bars;
+    r.g0 = sched_q(c.s, blockIdx.x);
+    r.g1 = sched_q(c.s, int(blockIdx.x) + 1);
     if (threadIdx.x == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+#pragma unroll
+        for (int k = 0; k < S; ++k) mbar_init(&bars[k], 1);
         mbar_fence_init();
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        s.issue(0);
-        if (s.nblk() > 1) s.issue(1);
-    }
-    return s;
+    return r;
 }
 
-// After a failed wait: wait (bounded) for copies still in flight into this
-// CTA's shared memory before the CTA exits.
-__device__ __forceinline__ void stream_drain(const BlockStream& s, int j, int32_t* err) {
-    if (threadIdx.x == 0) {
-        for (int k = j; k < s.nblk() && k < j + 2; ++k) mbar_wait(s.bar + (k & 1), (k >> 1) & 1, err);
-    }
+template <int S>
+__device__ __forceinline__ void ring_prime(const Ring<S>& r) {
+    if (threadIdx.x == 0)
+        for (int g = r.g0; g < r.g1 && g < r.g0 + S; ++g) r.issue(g);
+}
+
+// After a failed wait at block g: wait (bounded) for the copies still in
+// flight into this CTA's shared memory before the CTA exits.
+template <int S>
+__device__ __forceinline__ void ring_drain(const Ring<S>& r, int g, int32_t* err) {
+    if (threadIdx.x == 0)
+        for (int k = g; k < r.g1 && k < g + S; ++k) r.wait(k, err);
     __syncthreads();
 }
 
-// Arrival at the end of a segment; returns true (to every thread) in the CTA
-// that arrived last for its problem.
-__device__ __forceinline__ bool arrive_last(int32_t* cnt, int nseg, int* s_flag) {
+// Arrival at the end of a problem segment; returns true (to every thread) in
+// the CTA that arrived last for problem b.
+__device__ __forceinline__ bool arrive_last(int32_t* cnt, int64_t b, int nseg, int* s_flag) {
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) *s_flag = (atomicAdd(cnt + blockIdx.y, 1) == nseg - 1) ? 1 : 0;
+    if (threadIdx.x == 0) *s_flag = (atomicAdd(cnt + b, 1) == nseg - 1) ? 1 : 0;
     __syncthreads();
     const bool last = *s_flag != 0;
     if (last) __threadfence();
     return last;
-}
-
-// ---------------------------------------------------------------------------
-// Row-owner layout shared by both kernels: warp w takes rows w, w+8, ... of
-// each row block; lane l takes columns 4l + 128p (p < VPL) of every row it
-// touches.  Each lane therefore sees the same columns in every row and keeps
-// their column partials in registers for the whole segment; the 8 warps'
-// partials are merged once, at the end of the segment, through shared memory
-// (the row-block buffers, free by then).
-// ---------------------------------------------------------------------------
-
-// Cross-warp merge buffer layout: [kFW][m] entries of T (float2 or float).
-template <typename T>
-__device__ __forceinline__ T* merge_slot(unsigned char* smem, int w, int64_t m, int64_t col) {
-    return reinterpret_cast<T*>(smem) + int64_t(w) * m + col;
 }
 
 // ---------------------------------------------------------------------------
@@ -194,63 +222,79 @@ __device__ __forceinline__ float exact_column(const float* X, const float* u2, f
     return lse_finish(mx, sm);
 }
 
-template <int VPL, bool FULL>
-__global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_fwd_iter_kernel(FwdIter a) {
+template <int VPL, bool FULL, int S>
+__global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fwd_iter_kernel(FwdIter a) {
     using Cfg = FCfg<VPL>;
-    constexpr int R = Cfg::R, RPW = Cfg::RPW;
-    constexpr int NC = 4 * VPL;   // columns per lane
+    constexpr int R = Cfg::R, RPW = Cfg::RPW, NC = Cfg::NC;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ __align__(8) uint64_t bars[S];
     __shared__ float s_dmax[kFW];
     __shared__ int s_flag;
     __shared__ int s_nfix;
     __shared__ int s_fix[1024];
 
-    if (a.delta != nullptr) {   // device-side early stop (tol > 0)
+    pdl_launch_dependents();
+    const FusedCommon& c = a.c;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int64_t m = c.m, n = c.n;
+    Ring<S> rg = ring_init<S>(c, bars, smem);
+    const bool tolmode = a.delta != nullptr;
+    if (!tolmode) ring_prime(rg);   // the matrix is read-only across launches
+    pdl_wait();
+    if (tolmode) {   // device-side early stop
         if (*reinterpret_cast<volatile int32_t*>(a.status + 2) != 0) return;
-        if (a.iter > 0 && a.delta[a.iter - 1] < a.tol) {
-            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+        if (a.iter > 0 && __ldcg(a.delta + a.iter - 1) < a.tol) {
+            if (blockIdx.x == 0 && tid == 0) {
                 a.status[0] = a.iter;
                 a.status[1] = 1;
                 a.status[2] = 1;
             }
             return;
         }
+        ring_prime(rg);
     }
-    const FusedCommon& c = a.c;
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int64_t b = blockIdx.y, m = c.m;
-    const int64_t row0 = b * c.n + int64_t(blockIdx.x) * c.seg_rows;   // global row of local row 0
     if (tid == 0) s_nfix = 0;
-    BlockStream st = stream_begin(c, R, bars, smem);
 
     auto live = [&](int p) -> bool { return FULL || (4 * lane + 128 * p) < m; };
-    float vr[NC];
-#pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        const int64_t col = 4 * lane + 128 * p;
-        const float4 v4 = live(p) ? *reinterpret_cast<const float4*>(a.v2 + b * m + col) : make_float4(0, 0, 0, 0);
-        vr[4 * p + 0] = v4.x;
-        vr[4 * p + 1] = v4.y;
-        vr[4 * p + 2] = v4.z;
-        vr[4 * p + 3] = v4.w;
-    }
-    float cS[NC];
-#pragma unroll
-    for (int e = 0; e < NC; ++e) cS[e] = 0.0f;
+    float vr[NC], cS[NC];
     float A = kNegBig;   // warp-wide column reference (uniform across the warp)
     float dmax = 0.0f;
+    int cur = -1;
 
-    const int nblk = st.nblk();
-    for (int j = 0; j < nblk; ++j) {
-        const bool ok = mbar_wait(st.bar + (j & 1), (j >> 1) & 1, c.err);
+    for (int g = rg.g0; g < rg.g1; ++g) {
+        const int b = g / c.s.nblk, jb = g - b * c.s.nblk;
+        if (b != cur) {   // first block of a problem in this range
+            cur = b;
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                const int64_t col = 4 * lane + 128 * p;
+                const float4 v4 = live(p) ? __ldcg(reinterpret_cast<const float4*>(a.v2 + b * m + col))
+                                          : make_float4(0, 0, 0, 0);
+                vr[4 * p + 0] = v4.x;
+                vr[4 * p + 1] = v4.y;
+                vr[4 * p + 2] = v4.z;
+                vr[4 * p + 3] = v4.w;
+            }
+#pragma unroll
+            for (int e = 0; e < NC; ++e) cS[e] = 0.0f;
+            A = kNegBig;
+        }
+        const int rj = rg.rows_in(g);
+        const int64_t grow0 = int64_t(b) * n + int64_t(jb) * R;   // global row of the block's row 0
+        float lar[RPW];
+#pragma unroll
+        for (int q = 0; q < RPW; ++q) {
+            const int i = wid + kFW * q;
+            lar[q] = (a.la != nullptr && i < rj) ? __ldg(a.la + grow0 + i) : a.la_def;
+        }
+        const bool ok = rg.wait(g, c.err);
         if (!__syncthreads_and(ok)) {
-            stream_drain(st, j, c.err);
+            ring_drain(rg, g, c.err);
             return;
         }
-        const float* xs = st.buf(j);
-        const int rj = st.rows_in(j);
-        auto do_row = [&](int i) {
+        const float* xs = rg.buf(g);
+        auto do_row = [&](int q) {
+            const int i = wid + kFW * q;
             float t[NC];
             float mx = kNegBig;
 #pragma unroll
@@ -272,10 +316,10 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_fwd_iter_kernel(F
 #pragma unroll
             for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);   // t now holds E_ij
             const float s = warp_sum<32>(tree_sum(t));
-            const int64_t grow = row0 + int64_t(j) * R + i;
-            const float unew = (a.la ? a.la[grow] : a.la_def) - lse_finish(mx, s);
+            const int64_t grow = grow0 + i;
+            const float unew = lar[q] - lse_finish(mx, s);
             if (lane == 0) {
-                if (a.delta != nullptr) dmax = fmaxf(dmax, fabsf(unew - a.u2[grow]));
+                if (tolmode) dmax = fmaxf(dmax, fabsf(unew - __ldcg(a.u2 + grow)));
                 a.u2[grow] = unew;
             }
             const float ai = mx + unew;
@@ -291,126 +335,147 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_fwd_iter_kernel(F
         };
         if (rj == R) {
 #pragma unroll
-            for (int q = 0; q < RPW; ++q) do_row(wid + kFW * q);
+            for (int q = 0; q < RPW; ++q) do_row(q);
         } else {
             for (int q = 0; q < RPW; ++q)
-                if (wid + kFW * q < rj) do_row(wid + kFW * q);
+                if (wid + kFW * q < rj) do_row(q);
         }
-        __syncthreads();   // buffer (j & 1) is free again
-        if (tid == 0 && j + 2 < nblk) st.issue(j + 2);
+        __syncthreads();   // stage buffer of block g is free again
+
+        if (g + 1 == rg.g1 || jb + 1 == c.s.nblk) {
+            // ---- end of this CTA's part of problem b: publish its column partials ----
+            const int kfirst = sched_owner(c.s, b * c.s.nblk);
+            const int nseg = sched_owner(c.s, (b + 1) * c.s.nblk - 1) - kfirst + 1;
+            const int seg = int(blockIdx.x) - kfirst;
+            float2* mb = reinterpret_cast<float2*>(rg.buf(g));   // [kFW][kMergeCols]
+            float2* mypart = a.part + (b * c.s.maxseg + seg) * m;
+            auto finish = [&](int64_t col, float mm, float ss) {
+                if (ss < kTinySum) s_fix[atomicAdd(&s_nfix, 1)] = int(col);
+                else a.v2[b * m + col] = (a.lb ? a.lb[b * m + col] : a.lb_def) - lse_finish(mm, ss);
+            };
+#pragma unroll
+            for (int ch = 0; ch < (VPL + 3) / 4; ++ch) {
+#pragma unroll
+                for (int p = 4 * ch; p < VPL && p < 4 * ch + 4; ++p) {
+                    if (live(p)) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            mb[wid * kMergeCols + 4 * lane + 128 * (p - 4 * ch) + e] =
+                                make_float2(A - vr[4 * p + e], cS[4 * p + e]);
+                    }
+                }
+                __syncthreads();
+                const int ncols = int(min(int64_t(kMergeCols), m - int64_t(kMergeCols) * ch));
+                for (int cl = tid; cl < ncols; cl += kFT) {
+                    float mm = kNegBig, ss = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < kFW; ++w) {
+                        const float2 pw = mb[w * kMergeCols + cl];
+                        lse_merge(mm, ss, pw.x, pw.y);
+                    }
+                    const int64_t col = int64_t(kMergeCols) * ch + cl;
+                    if (nseg == 1) finish(col, mm, ss);
+                    else mypart[col] = make_float2(mm, ss);
+                }
+                __syncthreads();
+            }
+            bool merged = nseg == 1;
+            if (nseg > 1 && arrive_last(c.cnt, b, nseg, &s_flag)) {
+                merged = true;
+                for (int64_t col = tid; col < m; col += kFT) {
+                    float mm = kNegBig, ss = 0.0f;
+                    for (int sg = 0; sg < nseg; ++sg) {
+                        const float2 pp = __ldcg(a.part + (b * c.s.maxseg + sg) * m + col);
+                        lse_merge(mm, ss, pp.x, pp.y);
+                    }
+                    finish(col, mm, ss);
+                }
+                if (tid == 0) c.cnt[b] = 0;
+            }
+            if (merged) {
+                if (nseg == 1) __threadfence();   // this CTA's u rows are read back by exact_column
+                __syncthreads();
+                const int nfix = s_nfix;
+                for (int k = wid; k < nfix; k += kFW) {
+                    const int64_t col = s_fix[k];
+                    const float lse = exact_column(c.data, a.u2, a.kinv, b, n, m, col);
+                    if (lane == 0) a.v2[b * m + col] = (a.lb ? a.lb[b * m + col] : a.lb_def) - lse;
+                }
+                __syncthreads();
+                if (tid == 0) s_nfix = 0;
+            }
+            fence_proxy_async_smem();   // merge-buffer writes before the stage is refilled by a bulk copy
+            __syncthreads();
+        }
+        if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
     }
 
-    if (a.delta != nullptr) {
+    if (tolmode) {
         if (lane == 0) s_dmax[wid] = dmax;
-    }
-    // cross-warp merge of the column partials through the (now idle) buffers
+        __syncthreads();
+        if (tid == 0) {
+            float mx = 0.0f;
 #pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        if (live(p)) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                *merge_slot<float2>(smem, wid, m, 4 * lane + 128 * p + e) =
-                    make_float2(A - vr[4 * p + e], cS[4 * p + e]);
+            for (int w = 0; w < kFW; ++w) mx = fmaxf(mx, s_dmax[w]);
+            atomic_max_nonneg(a.delta + a.iter, mx);
         }
-    }
-    __syncthreads();
-    if (a.delta != nullptr && tid == 0) {
-        float mx = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kFW; ++w) mx = fmaxf(mx, s_dmax[w]);
-        atomic_max_nonneg(a.delta + a.iter, mx);
-    }
-    // Finalise one column from its merged (max, sum); flag it for the exact
-    // path when the shared-reference sum is too small to trust.
-    auto finish = [&](int64_t col, float mm, float ss) {
-        if (ss < kTinySum) {
-            s_fix[atomicAdd(&s_nfix, 1)] = int(col);
-        } else {
-            a.v2[b * m + col] = (a.lb ? a.lb[b * m + col] : a.lb_def) - lse_finish(mm, ss);
-        }
-    };
-    float2* mypart = a.part + (b * c.nseg + blockIdx.x) * m;
-    for (int64_t col = tid; col < m; col += kFT) {
-        float mm = kNegBig, ss = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kFW; ++w) {
-            const float2 pw = *merge_slot<float2>(smem, w, m, col);
-            lse_merge(mm, ss, pw.x, pw.y);
-        }
-        if (c.nseg == 1) finish(col, mm, ss);
-        else mypart[col] = make_float2(mm, ss);
-    }
-    if (c.nseg > 1) {
-        if (!arrive_last(c.cnt, c.nseg, &s_flag)) return;
-        for (int64_t col = tid; col < m; col += kFT) {
-            float mm = kNegBig, ss = 0.0f;
-            for (int sg = 0; sg < c.nseg; ++sg) {
-                const float2 pp = __ldcg(a.part + (b * c.nseg + sg) * m + col);
-                lse_merge(mm, ss, pp.x, pp.y);
-            }
-            finish(col, mm, ss);
-        }
-        if (tid == 0) c.cnt[b] = 0;
-    } else {
-        __threadfence();   // this CTA's u rows are read back by exact_column
-    }
-    __syncthreads();
-    const int nfix = s_nfix;
-    for (int k = wid; k < nfix; k += kFW) {
-        const int64_t col = s_fix[k];
-        const float lse = exact_column(c.data, a.u2, a.kinv, b, c.n, m, col);
-        if (lane == 0) a.v2[b * m + col] = (a.lb ? a.lb[b * m + col] : a.lb_def) - lse;
     }
 }
 
 // ---------------------------------------------------------------------------
 // backward (adjoint) iteration
 // ---------------------------------------------------------------------------
-template <int VPL, bool FULL>
-__global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_bwd_iter_kernel(BwdIter a) {
+template <int VPL, bool FULL, int S>
+__global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_bwd_iter_kernel(BwdIter a) {
     using Cfg = FCfg<VPL>;
-    constexpr int R = Cfg::R, RPW = Cfg::RPW;
-    constexpr int NC = 4 * VPL;
+    constexpr int R = Cfg::R, RPW = Cfg::RPW, NC = Cfg::NC;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ __align__(8) uint64_t bars[S];
     __shared__ int s_flag;
 
+    pdl_launch_dependents();
     const FusedCommon& c = a.c;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int64_t b = blockIdx.y, m = c.m;
-    const int64_t row0 = b * c.n + int64_t(blockIdx.x) * c.seg_rows;
-    BlockStream st = stream_begin(c, R, bars, smem);
+    const int64_t m = c.m, n = c.n;
+    Ring<S> rg = ring_init<S>(c, bars, smem);
+    ring_prime(rg);   // the plan is read-only across launches
+    pdl_wait();
 
     auto live = [&](int p) -> bool { return FULL || (4 * lane + 128 * p) < m; };
-    float mr[NC];
-#pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        const int64_t col = 4 * lane + 128 * p;
-        const float4 u4 = live(p) ? *reinterpret_cast<const float4*>(a.mu + b * m + col) : make_float4(0, 0, 0, 0);
-        mr[4 * p + 0] = u4.x;
-        mr[4 * p + 1] = u4.y;
-        mr[4 * p + 2] = u4.z;
-        mr[4 * p + 3] = u4.w;
-    }
-    float acc[NC];
-#pragma unroll
-    for (int e = 0; e < NC; ++e) acc[e] = 0.0f;
+    float mr[NC], acc[NC];
+    int cur = -1;
 
-    const int nblk = st.nblk();
-    for (int j = 0; j < nblk; ++j) {
-        const int rj = st.rows_in(j);
+    for (int g = rg.g0; g < rg.g1; ++g) {
+        const int b = g / c.s.nblk, jb = g - b * c.s.nblk;
+        if (b != cur) {
+            cur = b;
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                const int64_t col = 4 * lane + 128 * p;
+                const float4 u4 = live(p) ? __ldcg(reinterpret_cast<const float4*>(a.mu + b * m + col))
+                                          : make_float4(0, 0, 0, 0);
+                mr[4 * p + 0] = u4.x;
+                mr[4 * p + 1] = u4.y;
+                mr[4 * p + 2] = u4.z;
+                mr[4 * p + 3] = u4.w;
+            }
+#pragma unroll
+            for (int e = 0; e < NC; ++e) acc[e] = 0.0f;
+        }
+        const int rj = rg.rows_in(g);
+        const int64_t grow0 = int64_t(b) * n + int64_t(jb) * R;
         float2 ri[RPW];   // row invariants, loaded before waiting on the block
 #pragma unroll
         for (int q = 0; q < RPW; ++q) {
             const int i = wid + kFW * q;
-            ri[q] = i < rj ? a.rinv[row0 + int64_t(j) * R + i] : make_float2(0.0f, 1.0f);
+            ri[q] = i < rj ? __ldg(a.rinv + grow0 + i) : make_float2(0.0f, 1.0f);
         }
-        const bool ok = mbar_wait(st.bar + (j & 1), (j >> 1) & 1, c.err);
+        const bool ok = rg.wait(g, c.err);
         if (!__syncthreads_and(ok)) {
-            stream_drain(st, j, c.err);
+            ring_drain(rg, g, c.err);
             return;
         }
-        const float* ps = st.buf(j);
+        const float* ps = rg.buf(g);
 #pragma unroll
         for (int q = 0; q < RPW; ++q) {
             const int i = wid + kFW * q;
@@ -419,7 +484,7 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_bwd_iter_kernel(B
 #pragma unroll
             for (int p = 0; p < VPL; ++p) {
                 if (live(p)) {
-                    const float4 x = *reinterpret_cast<const float4*>(ps + int64_t(i) * m + 4 * lane + 128 * p);
+                    const float4 x = *reinterpret_cast<const float4*>(ps + i * int(m) + 4 * lane + 128 * p);
                     pv[4 * p + 0] = x.x;
                     pv[4 * p + 1] = x.y;
                     pv[4 * p + 2] = x.z;
@@ -432,56 +497,60 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_bwd_iter_kernel(B
 #pragma unroll
             for (int e = 0; e < NC; ++e) s += pv[e] * mr[e];
             s = warp_sum<32>(s);
-            const int64_t grow = row0 + int64_t(j) * R + i;
             const float l = (ri[q].x - s) / fmaxf(ri[q].y, kSumFloor);
-            if (lane == 0) a.lam[grow] = l;
+            if (lane == 0) a.lam[grow0 + i] = l;
 #pragma unroll
             for (int e = 0; e < NC; ++e) acc[e] += pv[e] * l;
         }
         __syncthreads();
-        if (tid == 0 && j + 2 < nblk) st.issue(j + 2);
-    }
 
+        if (g + 1 == rg.g1 || jb + 1 == c.s.nblk) {
+            const int kfirst = sched_owner(c.s, b * c.s.nblk);
+            const int nseg = sched_owner(c.s, (b + 1) * c.s.nblk - 1) - kfirst + 1;
+            const int seg = int(blockIdx.x) - kfirst;
+            float* mb = rg.buf(g);   // [kFW][m], m <= 1024: 32 KB
 #pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        if (live(p)) {
+            for (int p = 0; p < VPL; ++p) {
+                if (live(p)) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) *merge_slot<float>(smem, wid, m, 4 * lane + 128 * p + e) = acc[4 * p + e];
+                    for (int e = 0; e < 4; ++e) mb[wid * int(m) + 4 * lane + 128 * p + e] = acc[4 * p + e];
+                }
+            }
+            __syncthreads();
+            float* mypart = a.part + (b * c.s.maxseg + seg) * m;
+            for (int64_t col = tid; col < m; col += kFT) {
+                float sum = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kFW; ++w) sum += mb[w * int(m) + col];
+                if (nseg == 1) {
+                    const float2 ci = a.cinv[b * m + col];
+                    a.mu[b * m + col] = (ci.x - sum) / fmaxf(ci.y, kSumFloor);
+                } else {
+                    mypart[col] = sum;
+                }
+            }
+            __syncthreads();
+            if (nseg > 1 && arrive_last(c.cnt, b, nseg, &s_flag)) {
+                for (int64_t col = tid; col < m; col += kFT) {
+                    float sum = 0.0f;
+                    for (int sg = 0; sg < nseg; ++sg) sum += __ldcg(a.part + (b * c.s.maxseg + sg) * m + col);
+                    const float2 ci = a.cinv[b * m + col];
+                    a.mu[b * m + col] = (ci.x - sum) / fmaxf(ci.y, kSumFloor);
+                }
+                if (tid == 0) c.cnt[b] = 0;
+            }
+            fence_proxy_async_smem();   // merge-buffer writes before the stage is refilled by a bulk copy
+            __syncthreads();
         }
+        if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
     }
-    __syncthreads();
-    float* mypart = a.part + (b * c.nseg + blockIdx.x) * m;
-    for (int64_t col = tid; col < m; col += kFT) {
-        float sum = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kFW; ++w) sum += *merge_slot<float>(smem, w, m, col);
-        if (c.nseg == 1) {
-            const float2 ci = a.cinv[b * m + col];
-            a.mu[b * m + col] = (ci.x - sum) / fmaxf(ci.y, kSumFloor);
-        } else {
-            mypart[col] = sum;
-        }
-    }
-    if (c.nseg == 1) return;
-    if (!arrive_last(c.cnt, c.nseg, &s_flag)) return;
-    for (int64_t col = tid; col < m; col += kFT) {
-        float sum = 0.0f;
-        for (int sg = 0; sg < c.nseg; ++sg) sum += __ldcg(a.part + (b * c.nseg + sg) * m + col);
-        const float2 ci = a.cinv[b * m + col];
-        a.mu[b * m + col] = (ci.x - sum) / fmaxf(ci.y, kSumFloor);
-    }
-    if (tid == 0) c.cnt[b] = 0;
 }
 
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
 int vpl_for(int64_t m) { return m <= 128 ? 1 : m <= 256 ? 2 : m <= 512 ? 4 : 8; }
 int rows_per_block(int64_t m) { return 64 / vpl_for(m); }
-
-template <typename K>
-int blocks_per_sm(K kernel) {
-    int nb = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, kFT, kFusedSmem);
-    return nb > 0 ? nb : 1;
-}
 
 int sm_count() {
     int dev = 0, n = 0;
@@ -490,87 +559,175 @@ int sm_count() {
     return n > 0 ? n : 148;
 }
 
-// Segments per problem: minimise (CTA waves) x (rows per CTA + merge cost).
-int choose_nseg(int64_t B, int64_t n, int64_t m, int slots) {
-    const int64_t R = rows_per_block(m);
-    const int64_t nblk = (n + R - 1) / R;
-    int best = 1;
-    double best_cost = 1e300;
-    for (int64_t blocks_per_seg = 1; blocks_per_seg <= nblk; ++blocks_per_seg) {
-        const int64_t nseg = (nblk + blocks_per_seg - 1) / blocks_per_seg;
-        if (nseg > 4096) continue;
-        const double waves = std::ceil(double(B * nseg) / slots);
-        const double cost = waves * double(blocks_per_seg * R + (nseg > 1 ? 3 : 0));
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = int(nseg);
-        }
-    }
-    return best;
+// Pipeline depth: 2 stages (3 CTAs per SM) or 3 stages (2 CTAs per SM).
+// DOT_B200_FUSED_STAGES overrides the default for tuning runs.
+int stages() {
+    static int s = [] {
+        const char* e = std::getenv("DOT_B200_FUSED_STAGES");
+        const int v = e ? std::atoi(e) : 0;
+        return (v == 2 || v == 3) ? v : 2;
+    }();
+    return s;
 }
 
-template <int VPL>
-void set_smem_attrs() {
-    cudaFuncSetAttribute(skf_fwd_iter_kernel<VPL, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kFusedSmem));
-    cudaFuncSetAttribute(skf_bwd_iter_kernel<VPL, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kFusedSmem));
-    cudaFuncSetAttribute(skf_fwd_iter_kernel<VPL, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kFusedSmem));
-    cudaFuncSetAttribute(skf_bwd_iter_kernel<VPL, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kFusedSmem));
+// Bytes of every iteration's matrix stream copied with L2 evict_last
+// (DOT_B200_L2_KEEP_MB, 0 = off).  Off by default: at B=256, 512x512 a keep
+// set of 48, 64 or 96 MiB measured the same launch time as none.
+int64_t l2_keep_bytes() {
+    static int64_t k = [] {
+        const char* e = std::getenv("DOT_B200_L2_KEEP_MB");
+        const long v = e ? std::atol(e) : 0;
+        return int64_t(v < 0 ? 0 : v) << 20;
+    }();
+    return k;
+}
+
+template <int VPL, bool FULL, int S>
+void set_attr_one() {
+    const int sm = S * kTileFloats * int(sizeof(float));
+    cudaFuncSetAttribute(skf_fwd_iter_kernel<VPL, FULL, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    cudaFuncSetAttribute(skf_bwd_iter_kernel<VPL, FULL, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+}
+
+template <int S>
+void set_attrs_s() {
+    set_attr_one<1, false, S>();
+    set_attr_one<1, true, S>();
+    set_attr_one<2, false, S>();
+    set_attr_one<2, true, S>();
+    set_attr_one<4, false, S>();
+    set_attr_one<4, true, S>();
+    set_attr_one<8, false, S>();
+    set_attr_one<8, true, S>();
 }
 
 void ensure_attrs() {
-    // Per-device attribute; cheap enough to set on every call.
-    set_smem_attrs<1>();
-    set_smem_attrs<2>();
-    set_smem_attrs<4>();
-    set_smem_attrs<8>();
+    constexpr int kMaxDev = 64;
+    static bool done[kMaxDev] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDev && done[dev]) return;
+    set_attrs_s<2>();
+    set_attrs_s<3>();
+    if (dev >= 0 && dev < kMaxDev) done[dev] = true;
 }
 
-template <int VPL>
-void launch_fwd(const FwdIter& a, dim3 grid, cudaStream_t st) {
-    if (a.c.m == 128 * VPL) skf_fwd_iter_kernel<VPL, true><<<grid, kFT, kFusedSmem, st>>>(a);
-    else skf_fwd_iter_kernel<VPL, false><<<grid, kFT, kFusedSmem, st>>>(a);
+template <int S>
+int per_sm_for(int vpl) {
+    const int sm = S * kTileFloats * int(sizeof(float));
+    int nb = 0;
+    switch (vpl) {
+        case 1: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<1, false, S>, kFT, sm); break;
+        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<2, false, S>, kFT, sm); break;
+        case 4: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<4, false, S>, kFT, sm); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<8, false, S>, kFT, sm); break;
+    }
+    return nb > 0 ? nb : 1;
 }
-template <int VPL>
-void launch_bwd(const BwdIter& a, dim3 grid, cudaStream_t st) {
-    if (a.c.m == 128 * VPL) skf_bwd_iter_kernel<VPL, true><<<grid, kFT, kFusedSmem, st>>>(a);
-    else skf_bwd_iter_kernel<VPL, false><<<grid, kFT, kFusedSmem, st>>>(a);
+
+template <typename Args, typename K>
+void launch(K kernel, const Args& a, int G, int S, bool pdl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(G));
+    cfg.blockDim = dim3(kFT);
+    cfg.dynamicSmemBytes = size_t(S) * kTileFloats * sizeof(float);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
+template <int VPL, int S>
+void launch_fwd_v(const FwdIter& a, int G, bool pdl, cudaStream_t st) {
+    if (a.c.m == 128 * VPL) launch(skf_fwd_iter_kernel<VPL, true, S>, a, G, S, pdl, st);
+    else launch(skf_fwd_iter_kernel<VPL, false, S>, a, G, S, pdl, st);
+}
+template <int VPL, int S>
+void launch_bwd_v(const BwdIter& a, int G, bool pdl, cudaStream_t st) {
+    if (a.c.m == 128 * VPL) launch(skf_bwd_iter_kernel<VPL, true, S>, a, G, S, pdl, st);
+    else launch(skf_bwd_iter_kernel<VPL, false, S>, a, G, S, pdl, st);
+}
+
+template <int S>
+void launch_fwd_s(const FwdIter& a, int G, bool pdl, cudaStream_t st) {
+    switch (vpl_for(a.c.m)) {
+        case 1: launch_fwd_v<1, S>(a, G, pdl, st); break;
+        case 2: launch_fwd_v<2, S>(a, G, pdl, st); break;
+        case 4: launch_fwd_v<4, S>(a, G, pdl, st); break;
+        default: launch_fwd_v<8, S>(a, G, pdl, st); break;
+    }
+}
+template <int S>
+void launch_bwd_s(const BwdIter& a, int G, bool pdl, cudaStream_t st) {
+    switch (vpl_for(a.c.m)) {
+        case 1: launch_bwd_v<1, S>(a, G, pdl, st); break;
+        case 2: launch_bwd_v<2, S>(a, G, pdl, st); break;
+        case 4: launch_bwd_v<4, S>(a, G, pdl, st); break;
+        default: launch_bwd_v<8, S>(a, G, pdl, st); break;
+    }
+}
+
+Sched sched_of(const FusedPlan& p) {
+    Sched s;
+    s.T = int(p.total_blocks);
+    s.nblk = int(p.nblk);
+    s.G = p.G;
+    s.maxseg = p.maxseg;
+    s.keep = p.keep;
+    s.hint = 1;
+    return s;
 }
 
 }  // namespace
 
-bool sk_fused_supported(int64_t n, int64_t m, const void* data) {
-    return n >= 1 && m >= 4 && m <= 1024 && (m % 4) == 0 && (reinterpret_cast<uintptr_t>(data) & 15u) == 0;
+bool sk_fused_shape_ok(int64_t B, int64_t n, int64_t m) {
+    if (B < 1 || n < 1 || m < 4 || m > 1024 || (m % 4) != 0) return false;
+    const int64_t R = rows_per_block(m);
+    return B * ((n + R - 1) / R) < (int64_t(1) << 31);   // block indices are 32-bit
+}
+
+bool sk_fused_supported(int64_t B, int64_t n, int64_t m, const void* data) {
+    return sk_fused_shape_ok(B, n, m) && (reinterpret_cast<uintptr_t>(data) & 15u) == 0;
 }
 
 FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m) {
     FusedPlan p;
-    const int R = rows_per_block(m);
     ensure_attrs();
-    int per_sm = 1;
-    switch (vpl_for(m)) {
-        case 1: per_sm = blocks_per_sm(skf_fwd_iter_kernel<1, false>); break;
-        case 2: per_sm = blocks_per_sm(skf_fwd_iter_kernel<2, false>); break;
-        case 4: per_sm = blocks_per_sm(skf_fwd_iter_kernel<4, false>); break;
-        default: per_sm = blocks_per_sm(skf_fwd_iter_kernel<8, false>); break;
+    const int R = rows_per_block(m);
+    p.stages = stages();
+    const int per_sm = p.stages == 3 ? per_sm_for<3>(vpl_for(m)) : per_sm_for<2>(vpl_for(m));
+    p.nblk = (n + R - 1) / R;
+    p.total_blocks = B * p.nblk;
+    const int64_t slots = int64_t(sm_count()) * per_sm;
+    p.G = int(std::min<int64_t>(p.total_blocks, slots));
+    Sched s = sched_of(p);
+    int maxseg = 1;
+    for (int b = 0; b < int(B); ++b) {
+        const int k0 = sched_owner(s, b * s.nblk), k1 = sched_owner(s, (b + 1) * s.nblk - 1);
+        maxseg = std::max(maxseg, k1 - k0 + 1);
     }
-    const int slots = sm_count() * per_sm;
-    p.nseg = choose_nseg(B, n, m, slots);
-    const int64_t nblk = (n + R - 1) / R;
-    const int64_t bps = (nblk + p.nseg - 1) / p.nseg;
-    p.seg_rows = bps * R;
-    p.nseg = int((n + p.seg_rows - 1) / p.seg_rows);
+    p.maxseg = maxseg;
+    p.nseg = maxseg;
+    // L2 keep set: only when the matrix does not fit L2 by itself
+    const int64_t bytes = B * n * m * 4;
+    const int64_t blk_bytes = int64_t(R) * m * 4;
+    const int64_t keep_total = l2_keep_bytes();
+    p.keep = (bytes > keep_total && keep_total > 0) ? int(keep_total / (blk_bytes * p.G)) : 0;
     return p;
 }
 
 int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta,
-                      int iter, cudaStream_t st) {
-    ensure_attrs();
+                      int iter, bool first, bool last, cudaStream_t st) {
     FwdIter f{};
     f.c.data = a.X;
     f.c.n = a.n;
     f.c.m = a.m;
-    f.c.seg_rows = p.seg_rows;
-    f.c.nseg = p.nseg;
+    f.c.R = rows_per_block(a.m);
+    f.c.s = sched_of(p);
+    f.c.s.hint = last ? 0 : 1;
     f.c.cnt = cnt;
     f.c.err = a.status + 3;
     f.kinv = a.kinv;
@@ -585,25 +742,21 @@ int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int3
     f.status = a.status;
     f.tol = a.tol;
     f.iter = iter;
-    const dim3 grid(unsigned(p.nseg), unsigned(a.B));
-    switch (vpl_for(a.m)) {
-        case 1: launch_fwd<1>(f, grid, st); break;
-        case 2: launch_fwd<2>(f, grid, st); break;
-        case 4: launch_fwd<4>(f, grid, st); break;
-        default: launch_fwd<8>(f, grid, st); break;
-    }
+    if (p.stages == 3) launch_fwd_s<3>(f, p.G, !first, st);
+    else launch_fwd_s<2>(f, p.G, !first, st);
     return DOT_OK;
 }
 
 int sk_fused_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv, const float2* cinv,
-                      float* lam, float* mu, float* part, int32_t* cnt, int32_t* err, cudaStream_t st) {
-    ensure_attrs();
+                      float* lam, float* mu, float* part, int32_t* cnt, int32_t* err, bool first, bool last,
+                      cudaStream_t st) {
     BwdIter f{};
     f.c.data = a.P;
     f.c.n = a.n;
     f.c.m = a.m;
-    f.c.seg_rows = p.seg_rows;
-    f.c.nseg = p.nseg;
+    f.c.R = rows_per_block(a.m);
+    f.c.s = sched_of(p);
+    f.c.s.hint = last ? 0 : 1;
     f.c.cnt = cnt;
     f.c.err = err;
     f.rinv = rinv;
@@ -611,13 +764,8 @@ int sk_fused_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv
     f.lam = lam;
     f.mu = mu;
     f.part = part;
-    const dim3 grid(unsigned(p.nseg), unsigned(a.B));
-    switch (vpl_for(a.m)) {
-        case 1: launch_bwd<1>(f, grid, st); break;
-        case 2: launch_bwd<2>(f, grid, st); break;
-        case 4: launch_bwd<4>(f, grid, st); break;
-        default: launch_bwd<8>(f, grid, st); break;
-    }
+    if (p.stages == 3) launch_bwd_s<3>(f, p.G, !first, st);
+    else launch_bwd_s<2>(f, p.G, !first, st);
     return DOT_OK;
 }
 

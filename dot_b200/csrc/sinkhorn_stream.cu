@@ -573,7 +573,7 @@ static SkFwdWs carve_fwd(Carve& c, int64_t B, int64_t n, int64_t m, int n_iters,
                          bool want_cost) {
     SkFwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
-    const int64_t fseg = (m <= 1024 && m % 4 == 0) ? sk_fused_plan(B, n, m).nseg : 1;
+    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m).nseg : 1;
     const int64_t parts = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
     w.part = parts > 0 ? c.take<float2>(size_t(B * parts * m)) : nullptr;
     w.delta = tol > 0.0f ? c.take<float>(size_t(n_iters > 0 ? n_iters : 1)) : nullptr;
@@ -604,19 +604,19 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     if (w.delta) cudaMemsetAsync(w.delta, 0, sizeof(float) * size_t(a.n_iters > 0 ? a.n_iters : 1), st);
 
     SkCtl ctl{w.delta, a.status, a.tol, 0};
-    const bool fused = sk_fused_supported(a.n, a.m, a.X);
+    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.X);
     FusedPlan plan;
     if (fused) {
         plan = sk_fused_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
     }
-    for (int it = 0; it < a.n_iters; ++it) {
+    if (fused && a.n_iters > 0) {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st, a.n_iters);
+        for (int it = 0; it < a.n_iters; ++it)
+            sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, it == 0, it == a.n_iters - 1, st);
+    }
+    for (int it = 0; it < (fused ? 0 : a.n_iters); ++it) {
         ctl.iter = it;
-        if (fused) {
-            ProfScope ps(DOT_K_SK_FWD_ITER, st);
-            sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, st);
-            continue;
-        }
         {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
             sk_row_kernel<<<row_grid, kRowThreads, 0, st>>>(a.X, a.kinv, a.v2, a.la, a.la_def, a.u2,
@@ -663,7 +663,7 @@ struct SkBwdWs {
 static SkBwdWs carve_bwd(Carve& c, int64_t B, int64_t n, int64_t m) {
     SkBwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
-    const int64_t fseg = (m <= 1024 && m % 4 == 0) ? sk_fused_plan(B, n, m).nseg : 1;
+    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m).nseg : 1;
     w.rinv = c.take<float2>(size_t(B * n));
     w.cinv = c.take<float2>(size_t(B * m));
     w.lam = c.take<float>(size_t(B * n));
@@ -707,18 +707,19 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
         ProfScope ps(DOT_K_SK_BWD_EPI, st);
         skb_col_prep_merge_kernel<<<merge_grid, 256, 0, st>>>(w.part2, w.cinv, a.B, a.m, chunks);
     }
-    const bool fused = sk_fused_supported(a.n, a.m, a.P);
+    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.P);
     FusedPlan plan;
     if (fused) {
         plan = sk_fused_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B + 1), st);
     }
-    for (int it = 0; it < a.bwd_iters; ++it) {
-        if (fused) {
-            ProfScope ps(DOT_K_SK_BWD_ITER, st);
-            sk_fused_bwd_iter(a, plan, w.rinv, w.cinv, w.lam, w.mu, w.part1, w.cnt, w.cnt + a.B, st);
-            continue;
-        }
+    if (fused && a.bwd_iters > 0) {
+        ProfScope ps(DOT_K_SK_BWD_ITER, st, a.bwd_iters);
+        for (int it = 0; it < a.bwd_iters; ++it)
+            sk_fused_bwd_iter(a, plan, w.rinv, w.cinv, w.lam, w.mu, w.part1, w.cnt, w.cnt + a.B, it == 0,
+                              it == a.bwd_iters - 1, st);
+    }
+    for (int it = 0; it < (fused ? 0 : a.bwd_iters); ++it) {
         {
             ProfScope ps(DOT_K_SK_BWD_ITER, st);
             skb_row_iter_kernel<<<row_grid, kRowThreads, 0, st>>>(a.P, w.rinv, w.mu, w.lam, rows, a.n, a.m);

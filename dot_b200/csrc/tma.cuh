@@ -45,6 +45,74 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// L2 eviction-priority policies (createpolicy) for bulk copies: evict_last
+// keeps a line resident across launches that stream the same matrix again;
+// evict_first marks a line that will not be read again soon.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// bulk_g2s with an L2 cache-policy operand (no multicast).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Programmatic dependent launch (sm_90+).  launch_dependents lets the next
+// kernel in the stream be scheduled once every CTA of this grid has issued it
+// (or exited); wait blocks until the preceding grid has completed and its
+// memory is visible.  Before wait a kernel may only read data that the
+// preceding grid does not write.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// One bounded hardware wait: the thread may be suspended until the phase
+// completes or about kSuspendNs elapse.
+constexpr uint32_t kSuspendNs = 4000;
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` with suspending try_wait; gives up after
+// 2^19 attempts (between ~10 ms and ~2 s), records kErrBarrierTimeout in *err
+// and returns false.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int32_t* err) {
+    for (uint32_t i = 0; i < (1u << 19); ++i) {
+        if (mbar_try(bar, parity)) return true;
+    }
+    if (err != nullptr) atomicOr(err, kErrBarrierTimeout);
+    return false;
+}
+
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
