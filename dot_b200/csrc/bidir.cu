@@ -435,8 +435,10 @@ int bs_bwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int
 }  // namespace
 
 // fused passes (bidir_fused.cu) for L2 <= 1024, L2 % 4 == 0
-bool bsf_supported(int64_t L2, const void* sim, int dtype, const void* gout, const void* gsim);
+bool bsf_supported(int64_t B, int64_t L1, int64_t L2, int dtype, const void* sim, const void* gout, const void* dst,
+                   int dst_dtype);
 size_t bsf_fwd_ws(int64_t B, int64_t L1, int64_t L2);
+inline bool aligned16_host(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 size_t bsf_bwd_ws(int64_t B, int64_t L1, int64_t L2);
 int bsf_fwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau,
             float* out, float* row_stats, float* col_stats, void* ws, cudaStream_t st);
@@ -458,7 +460,9 @@ size_t bs_bwd_ws(int64_t B, int64_t L1, int64_t L2) {
 
 int bs_fwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2,
            float tau, float* out, float* row_stats, float* col_stats, void* ws, cudaStream_t st) {
-    if (bsf_supported(L2, sim, dtype, nullptr, out))
+    // the fused kernels read the statistics as float4
+    const bool stats16 = aligned16_host(row_stats) && aligned16_host(col_stats);
+    if (stats16 && bsf_supported(B, L1, L2, dtype, sim, nullptr, out, DOT_F32))
         return bsf_fwd(sim, dtype, lengths, B, L1, L2, tau, out, row_stats, col_stats, ws, st);
     float2* rs = reinterpret_cast<float2*>(row_stats);
     float2* cs = reinterpret_cast<float2*>(col_stats);
@@ -470,7 +474,8 @@ int bs_fwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_
 int bs_bwd(const void* sim, int dtype, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau,
            const float* row_stats, const float* col_stats, const float* gout, void* gsim, int gdtype,
            float* gtau, void* ws, cudaStream_t st) {
-    if (bsf_supported(L2, sim, dtype, gout, gsim))
+    const bool stats16 = aligned16_host(row_stats) && aligned16_host(col_stats);
+    if (stats16 && bsf_supported(B, L1, L2, dtype, sim, gout, gsim, gdtype))
         return bsf_bwd(sim, dtype, lengths, B, L1, L2, tau, row_stats, col_stats, gout, gsim, gdtype, gtau, ws, st);
     const float2* rs = reinterpret_cast<const float2*>(row_stats);
     const float2* cs = reinterpret_cast<const float2*>(col_stats);

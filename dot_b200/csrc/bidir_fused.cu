@@ -1,87 +1,167 @@
-// Bidirectional softmax, fused passes for rows that fit a warp's registers
-// (L2 <= 1024, L2 % 4 == 0; fp32 or bf16 input).
+// Bidirectional softmax for rows that fit a warp's registers (L2 <= 1024;
+// fp32 input with L2 % 4 == 0 or bf16 input with L2 % 8 == 0; 16-byte
+// aligned tensors): one persistent launch per direction, one thread-block
+// cluster per problem at a time.
 //
-//   forward  stats  one read of sim: row (max, 1/sum) exactly (max pass then
-//                   sum pass over the row in registers) and column sums
-//                   reusing the row exponentials -- exp(v_ij - A) =
-//                   E_ij * exp(max_i - A) for a warp-wide reference A >= every
-//                   row max -- merged over warps and row segments (last CTA
-//                   of a batch, no waiting); a column whose merged sum is too
-//                   small to trust is recomputed exactly from sim.
-//            out    out_ij = sqrt(1e-9 + row_ij * col_ij), vectorised.
-//   backward dots   one read of sim and grad_out: per-row dots
-//                   sum_j d_row*row and per-column dots sum_i d_col*col.
-//            grad   vectorised: grad = (d_row - rdot_i)*row/T + (d_col - cdot_j)*col/T.
-// Formulas: src/bidirectional_softmax/kernels_cpu.cpp:41-232.  Column
-// statistics use the reference A instead of the column maximum; any reference
-// gives the same softmax (exp(v - A)/sum_i exp(v - A)); exponentials go
-// through the SFU (ex2), about 1e-6 relative on the outputs.
+//   out_ij  = sqrt(1e-9 + row_ij * col_ij),  row = softmax_j(sim/T),
+//             col = softmax_i(sim/T), 0 outside the length window
+//   grad_ij = (d_row - rdot_i)*row/T + (d_col - cdot_j)*col/T
+//           = (2 q_ij - rdot_i*row_ij - cdot_j*col_ij) / T,
+//             q = dp*row*col, dp = g * 0.5 / out, rdot_i = sum_j q_ij,
+//             cdot_j = sum_i q_ij
+// (reference: src/bidirectional_softmax/kernels_cpu.cpp:41-232).
+//
+// Layout of the work.  A cluster of kC CTAs takes one problem at a time
+// (problems cid, cid + nclusters, ...); CTA r of the cluster owns rows
+// [r*rows_per, (r+1)*rows_per) of the problem and columns
+// [r*cols_per, (r+1)*cols_per) for the column reduction.  Per problem:
+//   pass 1   stream the CTA's rows through shared memory (1-D bulk copies on
+//            an S-stage mbarrier ring, L2 evict_last): forward -- row
+//            (max, 1/sum) exactly (max then sum over the row in registers)
+//            and column partial sums reusing the row exponentials,
+//            exp(v_ij - A) = E_ij * exp(max_i - A) for a warp-wide reference
+//            A >= every row max; backward -- rdot_i and column partial sums
+//            of q.  The CTA's warps are merged into one partial per column.
+//   reduce   cluster barrier; each CTA merges its column slice over the kC
+//            partials read through distributed shared memory (in rank
+//            order: deterministic), then after a second barrier gathers
+//            every column's result from its owner.  A forward column whose
+//            merged sum is too small to trust is recomputed exactly from sim.
+//   pass 2   stream the same rows again (served from L2, evict_first) and
+//            write out (forward) or grad_sim (backward) with evict_first stores.
+// Pass 2 of one problem and pass 1 of the next run on the same ring, so the
+// copies of the next rows are in flight across the barriers.  No CTA waits
+// on anything but its own copies and the cluster's hardware barriers.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
 #include "internal.h"
+#include "tma.cuh"
 
 namespace dotb {
 
 namespace {
 
-constexpr int kBT = 256;
-constexpr int kBW = kBT / 32;
+constexpr int kC = 8;               // CTAs per cluster
+constexpr int kStage = 32768;       // bytes per ring stage
+constexpr int kMergeCols = 512;
+constexpr int kMaxL2 = 1024;
+constexpr int kFwdWarps = 8;
+constexpr int kBwdWarps = 4;
+constexpr int kFwdStages = 2;
+constexpr int kBwdStages = 3;
 constexpr float kRaiseB = 60.0f;
 constexpr float kTinyB = 8.077935669463161e-28f;   // 2^-90
 
-// 4 consecutive values of sim as fp32.
-__device__ __forceinline__ void ld4(const float* p, float (&v)[4]) {
-    const float4 x = __ldg(reinterpret_cast<const float4*>(p));
+// ---------------------------------------------------------------------------
+// cluster primitives (sm_90+)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA of the cluster; release/acquire orders the
+// shared-memory writes before it with the remote reads after it.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// `p` (in this CTA's shared memory) as seen in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    return a;
+}
+__device__ __forceinline__ float2 ld_dsmem2(uint32_t a) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t a) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// element access
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ld4s(const float* p, float (&v)[4]) {   // shared memory
+    const float4 x = *reinterpret_cast<const float4*>(p);
     v[0] = x.x;
     v[1] = x.y;
     v[2] = x.z;
     v[3] = x.w;
 }
-__device__ __forceinline__ void ld4(const __nv_bfloat16* p, float (&v)[4]) {
-    const uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
+__device__ __forceinline__ void ld4s(const __nv_bfloat16* p, float (&v)[4]) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
     v[0] = __uint_as_float(x.x << 16);
     v[1] = __uint_as_float(x.x & 0xffff0000u);
     v[2] = __uint_as_float(x.y << 16);
     v[3] = __uint_as_float(x.y & 0xffff0000u);
 }
-__device__ __forceinline__ void st4(float* p, const float (&v)[4]) {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+__device__ __forceinline__ void st4g(float* p, const float (&v)[4], uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(v[0]), "f"(v[1]),
+                 "f"(v[2]), "f"(v[3]), "l"(pol)
+                 : "memory");
 }
-__device__ __forceinline__ void st4(__nv_bfloat16* p, const float (&v)[4]) {
+__device__ __forceinline__ void st4g(__nv_bfloat16* p, const float (&v)[4], uint64_t pol) {
     const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
     const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
-    uint2 x;
-    x.x = *reinterpret_cast<const uint32_t*>(&a);
-    x.y = *reinterpret_cast<const uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(p) = x;
+    const uint32_t x = *reinterpret_cast<const uint32_t*>(&a);
+    const uint32_t y = *reinterpret_cast<const uint32_t*>(&b);
+    asm volatile("st.global.L2::cache_hint.v2.u32 [%0], {%1, %2}, %3;" ::"l"(p), "r"(x), "r"(y), "l"(pol)
+                 : "memory");
+}
+
+__device__ __forceinline__ float rsqrt_approx(float x) {
+    float y;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ void window(const int32_t* lengths, int64_t b, int64_t L1, int64_t L2, int64_t& l1,
                                        int64_t& l2) {
-    l1 = min(max(int64_t(lengths[2 * b]), int64_t(0)), L1);
-    l2 = min(max(int64_t(lengths[2 * b + 1]), int64_t(0)), L2);
+    l1 = min(max(int64_t(__ldg(lengths + 2 * b)), int64_t(0)), L1);
+    l2 = min(max(int64_t(__ldg(lengths + 2 * b + 1)), int64_t(0)), L2);
 }
 
-struct BsfCommon {
-    const int32_t* lengths;
-    int64_t L1, L2;
-    float invT;
-    int64_t seg_rows;
-    int nseg;
-    int32_t* cnt;   // [B] arrival counters
+// Per-element values from the statistics, the same expressions in every pass
+// (so the backward sees the forward's values bit for bit):
+//   row = exp(v - rmax) * rinv, col = exp(v - cmax) * cinv, rc = row * col,
+//   out = min(sqrt(1e-9 + rc), 1), iout = 1 / out.
+// sqrt and 1/sqrt come from one rsqrt (SFU, ~2^-22 relative).  The column
+// value's numerator exp(v - A) and its share of the column sum (accumulated
+// as E*w) can differ by an ulp, so rc may exceed 1 by rounding where one
+// element dominates its row and column; out is capped at 1, its
+// exact-arithmetic bound.  out >= sqrt(1e-9) > 1e-9, so the reference's guard
+// dp = 0 for out <= 1e-9 never applies.
+struct BsVals {
+    float row, col, rc, out, iout;
 };
-
-__device__ __forceinline__ bool arrive_last_b(int32_t* cnt, int nseg, int* s_flag) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) *s_flag = (atomicAdd(cnt + blockIdx.y, 1) == nseg - 1) ? 1 : 0;
-    __syncthreads();
-    const bool last = *s_flag != 0;
-    if (last) __threadfence();
-    return last;
+__device__ __forceinline__ BsVals bs_vals(float v, float2 rs, float2 cs) {
+    BsVals q;
+    q.row = exp_shift(v - rs.x) * rs.y;
+    q.col = exp_shift(v - cs.x) * cs.y;
+    q.rc = q.row * q.col;
+    const float x = 1e-9f + q.rc;
+    const float r = rsqrt_approx(x);
+    q.out = fminf(x * r, 1.0f);
+    q.iout = fmaxf(r, 1.0f);
+    return q;
 }
 
 // Exact column softmax statistics (max, 1/sum) over rows [0, l1) -- one warp.
@@ -98,290 +178,451 @@ __device__ float2 exact_col_stats(const T* sb, int64_t L2, int64_t l1, int64_t c
 }
 
 // ---------------------------------------------------------------------------
-// forward statistics
+// the CTA's block sequence: for each of its cluster's problems, the nb blocks
+// of its row slice for pass 1, then the same nb blocks for pass 2
 // ---------------------------------------------------------------------------
-template <typename T, int VPL>
-__global__ void __launch_bounds__(kBT, 2)
-bsf_stats_kernel(const T* __restrict__ sim, BsfCommon c, float2* __restrict__ rstat, float2* __restrict__ cpart,
-                 float2* __restrict__ cstat) {
-    constexpr int NC = 4 * VPL;
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int s_flag, s_nfix;
-    __shared__ int s_fix[1024];
-    float2* mrg = reinterpret_cast<float2*>(smem);   // [kBW][L2]
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int64_t b = blockIdx.y, L1 = c.L1, L2 = c.L2;
-    int64_t l1, l2;
-    window(c.lengths, b, L1, L2, l1, l2);
-    const int64_t r0 = int64_t(blockIdx.x) * c.seg_rows, r1 = min(L1, r0 + c.seg_rows);
-    const T* sb = sim + b * L1 * L2;
-    if (tid == 0) s_nfix = 0;
+struct ClArgs {
+    const unsigned char* src[2];   // sim, grad_out (backward)
+    uint32_t row_bytes[2];
+    uint32_t tile_off1;            // byte offset of grad_out's tile in a stage
+    int nsrc;
+    const int32_t* lengths;
+    int64_t B, L1, L2;
+    int64_t rows_per, cols_per;    // per CTA of a cluster
+    int R;                         // rows per block
+    float invT;
+    float2* rstat;                 // [B, L1] forward output / backward input
+    float2* cstat;                 // [B, L2]
+    float* out;                    // forward: [B, L1, L2]
+    void* gsim;                    // backward: [B, L1, L2], float or bf16
+    float* rdot;                   // backward scratch [B, L1]
+    float* tau_row;                // backward: [B, L1] or nullptr
+    int32_t* err;                  // bounded-wait expiry word
+};
 
-    float S[NC];
-#pragma unroll
-    for (int e = 0; e < NC; ++e) S[e] = 0.0f;
-    float A = kNegBig;
-    for (int64_t i = r0 + wid; i < r1; i += kBW) {
-        if (i >= l1 || l2 == 0) {
-            if (lane == 0) rstat[b * L1 + i] = make_float2(0.0f, 0.0f);
-            continue;
-        }
-        float t[NC];
-#pragma unroll
-        for (int p = 0; p < VPL; ++p) {
-            const int64_t col = 4 * lane + 128 * p;
-            float v[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (col < L2) {
-                ld4(sb + i * L2 + col, v);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[e] = (col + e < l2) ? __fmul_rn(v[e], c.invT) : -INFINITY;
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) t[4 * p + e] = v[e];
-        }
-        float mx = t[0];
-#pragma unroll
-        for (int e = 1; e < NC; ++e) mx = fmaxf(mx, t[e]);
-        mx = warp_max<32>(mx);
-#pragma unroll
-        for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
-        const float s = warp_sum<32>(tree_sum(t));
-        if (lane == 0) rstat[b * L1 + i] = make_float2(mx, s > 0.0f ? 1.0f / s : 0.0f);
-        if (mx > A + kRaiseB) {   // warp-uniform
-            const float sc = exp_shift(A - mx);
-#pragma unroll
-            for (int e = 0; e < NC; ++e) S[e] *= sc;
-            A = mx;
-        }
-        const float w = exp_shift(mx - A);
-#pragma unroll
-        for (int e = 0; e < NC; ++e) S[e] = fmaf(t[e], w, S[e]);
+template <int S>
+struct ClRing {
+    const ClArgs* a;
+    unsigned char* smem;
+    uint64_t* bar;
+    int64_t r0, r1;   // row slice
+    int nb;           // blocks per pass
+    int K;            // blocks in the whole sequence
+    uint32_t cid, ncl;
+
+    __device__ unsigned char* stage(int k) const { return smem + size_t(k % S) * kStage; }
+    __device__ int rows_in(int j) const { return int(min(int64_t(a->R), r1 - (r0 + int64_t(j) * a->R))); }
+    __device__ void issue(int k) const {   // one thread
+        const int per = 2 * nb;
+        const int64_t b = cid + int64_t(k / per) * ncl;
+        const int pass = (k % per) / nb, j = k % nb;
+        const int rows = rows_in(j);
+        const int64_t row = b * a->L1 + r0 + int64_t(j) * a->R;
+        uint64_t* bb = bar + k % S;
+        uint32_t total = 0;
+        for (int s = 0; s < a->nsrc; ++s) total += uint32_t(rows) * a->row_bytes[s];
+        mbar_arrive_expect_tx(bb, total);
+        const uint64_t pol = pass == 0 ? l2_policy_evict_last() : l2_policy_evict_first();
+        for (int s = 0; s < a->nsrc; ++s)
+            bulk_g2s_hint(stage(k) + (s == 0 ? 0u : a->tile_off1), a->src[s] + row * a->row_bytes[s],
+                          uint32_t(rows) * a->row_bytes[s], bb, pol);
     }
+    __device__ bool wait(int k, int32_t* err) const {
+        return mbar_wait_sleep(bar + k % S, uint32_t((k / S) & 1), err);
+    }
+};
+
+template <int S>
+__device__ __forceinline__ ClRing<S> cl_ring_init(const ClArgs& a, uint64_t* bars, unsigned char* smem) {
+    ClRing<S> r;
+    r.a = &a;
+    r.smem = smem;
+    r.bar = bars;
+    r.cid = cluster_id();
+    r.ncl = cluster_count();
+    const int64_t rank = cluster_rank();
+    r.r0 = min(a.L1, rank * a.rows_per);
+    r.r1 = min(a.L1, r.r0 + a.rows_per);
+    r.nb = int((r.r1 - r.r0 + a.R - 1) / a.R);
+    const int64_t nprob = int64_t(r.cid) < a.B ? (a.B - 1 - r.cid) / r.ncl + 1 : 0;
+    r.K = int(nprob * 2 * r.nb);
+    if (threadIdx.x == 0) {
 #pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        const int64_t col = 4 * lane + 128 * p;
-        if (col < L2) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) mrg[int64_t(wid) * L2 + col + e] = make_float2(A, S[4 * p + e]);
-        }
+        for (int k = 0; k < S; ++k) mbar_init(&bars[k], 1);
+        mbar_fence_init();
     }
     __syncthreads();
-    auto finish = [&](int64_t col, float mm, float ss) {
-        if (col >= l2) {
-            cstat[b * L2 + col] = make_float2(0.0f, 0.0f);
-        } else if (ss < kTinyB) {
-            s_fix[atomicAdd(&s_nfix, 1)] = int(col);
-        } else {
-            cstat[b * L2 + col] = make_float2(mm, 1.0f / ss);
-        }
-    };
-    float2* mypart = cpart + (b * c.nseg + blockIdx.x) * L2;
-    for (int64_t col = tid; col < L2; col += kBT) {
-        float mm = kNegBig, ss = 0.0f;
+    if (threadIdx.x == 0)
+        for (int k = 0; k < r.K && k < S; ++k) r.issue(k);
+    return r;
+}
+
+// Wait for block k of the sequence; after a failed wait the CTA stops waiting
+// and issuing (results are invalid, *err is set) but keeps taking part in the
+// cluster barriers.  Returns whether the block may be used.
+template <int S>
+__device__ __forceinline__ bool cl_wait(const ClRing<S>& r, int k, int& kfail) {
+    if (kfail >= 0) return false;
+    const bool ok = __syncthreads_and(r.wait(k, r.a->err));
+    if (!ok) kfail = k;
+    return ok;
+}
+
+// Issue block k + S once block k's stage is free.
+template <int S>
+__device__ __forceinline__ void cl_next(const ClRing<S>& r, int k, int kfail) {
+    if (threadIdx.x == 0 && kfail < 0 && k + S < r.K) r.issue(k + S);
+}
+
+// Before exit after a failed wait: wait (bounded) for copies still in flight.
+template <int S>
+__device__ __forceinline__ void cl_drain(const ClRing<S>& r, int kfail) {
+    if (kfail >= 0 && threadIdx.x == 0)
+        for (int k = kfail; k < r.K && k < kfail + S; ++k) r.wait(k, nullptr);
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArgs a) {
+    constexpr int NW = kFwdWarps, NC = 4 * VPL, S = kFwdStages, NT = NW * 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float2* cp = reinterpret_cast<float2*>(smem + size_t(S) * kStage);   // [kMaxL2] this CTA's column partials
+    float2* cs = cp + kMaxL2;                                             // [kMaxL2] column statistics
+    __shared__ __align__(8) uint64_t bars[S];
+    __shared__ int s_nfix;
+    __shared__ int s_fix[kMaxL2];
+
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int64_t L1 = a.L1, L2 = a.L2;
+    const uint32_t rank = cluster_rank();
+    ClRing<S> rg = cl_ring_init<S>(a, bars, smem);
+    const int64_t c0 = min(L2, int64_t(rank) * a.cols_per), c1 = min(L2, c0 + a.cols_per);
+    const uint64_t pol_out = l2_policy_evict_first();
+    int kfail = -1;
+    int k = 0;
+    for (int64_t b = rg.cid; b < a.B; b += rg.ncl) {
+        int64_t l1, l2;
+        window(a.lengths, b, L1, L2, l1, l2);
+        const T* sb = reinterpret_cast<const T*>(a.src[0]) + b * L1 * L2;
+
+        // ---- pass 1: row statistics, column partials ----
+        float Sc[NC];
 #pragma unroll
-        for (int w = 0; w < kBW; ++w) {
-            const float2 q = mrg[int64_t(w) * L2 + col];
-            lse_merge(mm, ss, q.x, q.y);
+        for (int e = 0; e < NC; ++e) Sc[e] = 0.0f;
+        float A = kNegBig;
+        const bool full = l2 == L2;
+        for (int j = 0; j < rg.nb; ++j, ++k) {
+            const bool ok = cl_wait(rg, k, kfail);
+            const T* xs = reinterpret_cast<const T*>(rg.stage(k));
+            const int rows = rg.rows_in(j);
+            for (int il = wid; ok && il < rows; il += NW) {
+                const int64_t i = rg.r0 + int64_t(j) * a.R + il;
+                if (i >= l1 || l2 == 0) {
+                    if (lane == 0) a.rstat[b * L1 + i] = make_float2(0.0f, 0.0f);
+                    continue;
+                }
+                float t[NC];
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    const int64_t col = 4 * lane + 128 * p;
+                    float v[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    if (col < L2) {
+                        ld4s(xs + il * L2 + col, v);
+                        if (full) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) v[e] = __fmul_rn(v[e], a.invT);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) v[e] = (col + e < l2) ? __fmul_rn(v[e], a.invT) : -INFINITY;
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) t[4 * p + e] = v[e];
+                }
+                float mx = t[0];
+#pragma unroll
+                for (int e = 1; e < NC; ++e) mx = fmaxf(mx, t[e]);
+                mx = warp_max<32>(mx);
+#pragma unroll
+                for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
+                const float s = warp_sum<32>(tree_sum(t));
+                if (lane == 0) a.rstat[b * L1 + i] = make_float2(mx, s > 0.0f ? 1.0f / s : 0.0f);
+                if (mx > A + kRaiseB) {   // warp-uniform
+                    const float sc = exp_shift(A - mx);
+#pragma unroll
+                    for (int e = 0; e < NC; ++e) Sc[e] *= sc;
+                    A = mx;
+                }
+                const float w = exp_shift(mx - A);
+#pragma unroll
+                for (int e = 0; e < NC; ++e) Sc[e] = fmaf(t[e], w, Sc[e]);
+            }
+            __syncthreads();
+            if (j == rg.nb - 1) {
+                // merge the warps' partials into cp through the free stage buffer
+                float2* mb = reinterpret_cast<float2*>(rg.stage(k));   // [NW][kMergeCols]
+#pragma unroll
+                for (int ch = 0; ch < (VPL + 3) / 4; ++ch) {
+#pragma unroll
+                    for (int p = 4 * ch; p < VPL && p < 4 * ch + 4; ++p) {
+                        const int64_t col = 4 * lane + 128 * p;
+                        if (col < L2) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                mb[wid * kMergeCols + 4 * lane + 128 * (p - 4 * ch) + e] = make_float2(A, Sc[4 * p + e]);
+                        }
+                    }
+                    __syncthreads();
+                    const int ncols = int(min(int64_t(kMergeCols), L2 - int64_t(kMergeCols) * ch));
+                    for (int cl = tid; cl < ncols; cl += NT) {
+                        float mm = kNegBig, ss = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < NW; ++w) {
+                            const float2 q = mb[w * kMergeCols + cl];
+                            lse_merge(mm, ss, q.x, q.y);
+                        }
+                        cp[kMergeCols * ch + cl] = make_float2(mm, ss);
+                    }
+                    __syncthreads();
+                }
+                fence_proxy_async_smem();
+                __syncthreads();
+            }
+            cl_next(rg, k, kfail);
         }
-        if (c.nseg == 1) finish(col, mm, ss);
-        else mypart[col] = make_float2(mm, ss);
-    }
-    if (c.nseg > 1) {
-        if (!arrive_last_b(c.cnt, c.nseg, &s_flag)) return;
-        for (int64_t col = tid; col < L2; col += kBT) {
+        if (rg.nb == 0)
+            for (int64_t col = tid; col < L2; col += NT) cp[col] = make_float2(kNegBig, 0.0f);
+        if (tid == 0) s_nfix = 0;
+        cluster_sync();
+
+        // ---- column reduction: this CTA's slice over the cluster's partials ----
+        for (int64_t col = c0 + tid; col < c1; col += NT) {
             float mm = kNegBig, ss = 0.0f;
-            for (int sg = 0; sg < c.nseg; ++sg) {
-                const float2 q = __ldcg(cpart + (b * c.nseg + sg) * L2 + col);
+            for (uint32_t rr = 0; rr < kC; ++rr) {
+                const float2 q = ld_dsmem2(dsmem(cp + col, rr));
                 lse_merge(mm, ss, q.x, q.y);
             }
-            finish(col, mm, ss);
+            float2 st = make_float2(0.0f, 0.0f);
+            if (col < l2) {
+                if (ss < kTinyB) s_fix[atomicAdd(&s_nfix, 1)] = int(col);
+                else st = make_float2(mm, 1.0f / ss);
+            }
+            cs[col] = st;
+            a.cstat[b * L2 + col] = st;
         }
-        if (tid == 0) c.cnt[b] = 0;
-    }
-    __syncthreads();
-    const int nfix = s_nfix;
-    for (int k = wid; k < nfix; k += kBW) {
-        const int64_t col = s_fix[k];
-        const float2 st = exact_col_stats(sb, L2, l1, col, c.invT);
-        if (lane == 0) cstat[b * L2 + col] = st;
-    }
-}
-
-// Per-element softmax values from the statistics (the same expressions in
-// every pass, so forward and backward see identical values).
-struct BsVals {
-    float row, col, out;
-};
-// The column value's numerator exp(v - A) and its share of the column sum
-// (accumulated as E*w) can differ by an ulp, so row*col may exceed 1 by
-// rounding where one element dominates its row and column; out is capped at 1,
-// its exact-arithmetic bound.
-__device__ __forceinline__ BsVals bs_vals(float val, float2 rs, float2 cs) {
-    BsVals v;
-    v.row = exp_shift(val - rs.x) * rs.y;
-    v.col = exp_shift(val - cs.x) * cs.y;
-    v.out = fminf(sqrtf(__fadd_rn(1e-9f, __fmul_rn(v.row, v.col))), 1.0f);
-    return v;
-}
-
-// ---------------------------------------------------------------------------
-// forward output, warp per row
-// ---------------------------------------------------------------------------
-template <typename T, int VPL>
-__global__ void __launch_bounds__(kBT)
-bsf_out_kernel(const T* __restrict__ sim, BsfCommon c, int64_t B, const float2* __restrict__ rstat,
-               const float2* __restrict__ cstat, float* __restrict__ out) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t L1 = c.L1, L2 = c.L2;
-    const int64_t row = int64_t(blockIdx.x) * kBW + wid;
-    if (row >= B * L1) return;
-    const int64_t b = row / L1, i = row - b * L1;
-    int64_t l1, l2;
-    window(c.lengths, b, L1, L2, l1, l2);
-    const float2 rs = rstat[row];
-    const float2* cb = cstat + b * L2;
-#pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        const int64_t col = 4 * lane + 128 * p;
-        if (col >= L2) continue;
-        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (i < l1 && col < l2) {
-            float v[4];
-            ld4(sim + row * L2 + col, v);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                if (col + e < l2) o[e] = bs_vals(__fmul_rn(v[e], c.invT), rs, cb[col + e]).out;
+        __syncthreads();
+        for (int f = wid; f < s_nfix; f += NW) {
+            const int64_t col = s_fix[f];
+            const float2 st = exact_col_stats(sb, L2, l1, col, a.invT);
+            if (lane == 0) {
+                cs[col] = st;
+                a.cstat[b * L2 + col] = st;
+            }
         }
-        st4(out + row * L2 + col, o);
+        cluster_sync();
+        for (int64_t col = tid; col < L2; col += NT) {
+            const uint32_t owner = uint32_t(col / a.cols_per);
+            if (owner != rank) cs[col] = ld_dsmem2(dsmem(cs + col, owner));
+        }
+        __syncthreads();
+
+        // ---- pass 2: out ----
+        for (int j = 0; j < rg.nb; ++j, ++k) {
+            const bool ok = cl_wait(rg, k, kfail);
+            const T* xs = reinterpret_cast<const T*>(rg.stage(k));
+            const int rows = rg.rows_in(j);
+            for (int il = wid; ok && il < rows; il += NW) {
+                const int64_t i = rg.r0 + int64_t(j) * a.R + il;
+                const float2 rs = __ldcg(a.rstat + b * L1 + i);
+                float* orow = a.out + (b * L1 + i) * L2;
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    const int64_t col = 4 * lane + 128 * p;
+                    if (col >= L2) continue;
+                    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (i < l1 && col < l2) {
+                        float v[4];
+                        ld4s(xs + il * L2 + col, v);
+                        const float4 c01 = *reinterpret_cast<const float4*>(cs + col);
+                        const float4 c23 = *reinterpret_cast<const float4*>(cs + col + 2);
+                        const float2 cc[4] = {make_float2(c01.x, c01.y), make_float2(c01.z, c01.w),
+                                              make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (full || col + e < l2) o[e] = bs_vals(__fmul_rn(v[e], a.invT), rs, cc[e]).out;
+                    }
+                    st4g(orow + col, o, pol_out);
+                }
+            }
+            __syncthreads();
+            cl_next(rg, k, kfail);
+        }
     }
+    cluster_sync();   // no CTA leaves while another may still read its shared memory
+    cl_drain(rg, kfail);
 }
 
 // ---------------------------------------------------------------------------
-// backward dots: row dots sum_j d_row*row, column dots sum_i d_col*col
+// backward
 // ---------------------------------------------------------------------------
-template <typename T, int VPL>
-__global__ void __launch_bounds__(kBT, 2)
-bsf_dots_kernel(const T* __restrict__ sim, const float* __restrict__ gout, BsfCommon c,
-                const float2* __restrict__ rstat, const float2* __restrict__ cstat, float* __restrict__ rdot,
-                float* __restrict__ cpart, float* __restrict__ cdot) {
-    constexpr int NC = 4 * VPL;
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int s_flag;
+template <typename T, typename G, int VPL>
+__global__ void __launch_bounds__(kBwdWarps * 32, 2) bs_bwd_cluster_kernel(ClArgs a) {
+    constexpr int NW = kBwdWarps, NC = 4 * VPL, S = kBwdStages, NT = NW * 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float2* cs = reinterpret_cast<float2*>(smem + size_t(S) * kStage);   // [kMaxL2] column statistics
+    float* cp = reinterpret_cast<float*>(cs + kMaxL2);                    // [kMaxL2] column partials of q
+    float* cd = cp + kMaxL2;                                              // [kMaxL2] cdot
+    __shared__ __align__(8) uint64_t bars[S];
+
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int64_t b = blockIdx.y, L1 = c.L1, L2 = c.L2;
-    float2* cs = reinterpret_cast<float2*>(smem);               // [L2] column statistics
-    float* mrg = reinterpret_cast<float*>(smem) + 2 * L2;       // [kBW][L2]
-    int64_t l1, l2;
-    window(c.lengths, b, L1, L2, l1, l2);
-    const int64_t r0 = int64_t(blockIdx.x) * c.seg_rows, r1 = min(L1, r0 + c.seg_rows);
-    const T* sb = sim + b * L1 * L2;
-    const float* gb = gout + b * L1 * L2;
-    for (int64_t col = tid; col < L2; col += kBT) cs[col] = cstat[b * L2 + col];
-    __syncthreads();
-    float C[NC];
+    const int64_t L1 = a.L1, L2 = a.L2;
+    const uint32_t rank = cluster_rank();
+    ClRing<S> rg = cl_ring_init<S>(a, bars, smem);
+    const int64_t c0 = min(L2, int64_t(rank) * a.cols_per), c1 = min(L2, c0 + a.cols_per);
+    const uint64_t pol_out = l2_policy_evict_first();
+    G* gsim = static_cast<G*>(a.gsim);
+    int kfail = -1;
+    int k = 0;
+    for (int64_t b = rg.cid; b < a.B; b += rg.ncl) {
+        int64_t l1, l2;
+        window(a.lengths, b, L1, L2, l1, l2);
+        const bool full = l2 == L2;
+        for (int64_t col = tid; col < L2; col += NT) cs[col] = __ldcg(a.cstat + b * L2 + col);
+        __syncthreads();
+
+        // ---- pass 1: rdot and column partials of q ----
+        float C[NC];
 #pragma unroll
-    for (int e = 0; e < NC; ++e) C[e] = 0.0f;
-    for (int64_t i = r0 + wid; i < r1; i += kBW) {
-        float rd = 0.0f;
-        if (i < l1) {
-            const float2 rs = rstat[b * L1 + i];
+        for (int e = 0; e < NC; ++e) C[e] = 0.0f;
+        for (int j = 0; j < rg.nb; ++j, ++k) {
+            const bool ok = cl_wait(rg, k, kfail);
+            const T* xs = reinterpret_cast<const T*>(rg.stage(k));
+            const float* gs = reinterpret_cast<const float*>(rg.stage(k) + a.tile_off1);
+            const int rows = rg.rows_in(j);
+            for (int il = wid; ok && il < rows; il += NW) {
+                const int64_t i = rg.r0 + int64_t(j) * a.R + il;
+                float rd = 0.0f;
+                if (i < l1) {
+                    const float2 rs = __ldcg(a.rstat + b * L1 + i);
 #pragma unroll
-            for (int p = 0; p < VPL; ++p) {
-                const int64_t col = 4 * lane + 128 * p;
-                if (col < l2) {
-                    float v[4], g[4];
-                    ld4(sb + i * L2 + col, v);
-                    ld4(gb + i * L2 + col, g);
+                    for (int p = 0; p < VPL; ++p) {
+                        const int64_t col = 4 * lane + 128 * p;
+                        if (col < l2) {
+                            float v[4], g[4];
+                            ld4s(xs + il * L2 + col, v);
+                            ld4s(gs + il * L2 + col, g);
+                            const float4 c01 = *reinterpret_cast<const float4*>(cs + col);
+                            const float4 c23 = *reinterpret_cast<const float4*>(cs + col + 2);
+                            const float2 cc[4] = {make_float2(c01.x, c01.y), make_float2(c01.z, c01.w),
+                                                  make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (col + e < l2) {
-                            const BsVals q = bs_vals(__fmul_rn(v[e], c.invT), rs, cs[col + e]);
-                            const float dp = q.out > 1e-9f ? g[e] * 0.5f / q.out : 0.0f;
-                            rd += __fmul_rn(__fmul_rn(dp, q.col), q.row);
-                            C[4 * p + e] += __fmul_rn(__fmul_rn(dp, q.row), q.col);
+                            for (int e = 0; e < 4; ++e) {
+                                if (full || col + e < l2) {
+                                    const BsVals q = bs_vals(__fmul_rn(v[e], a.invT), rs, cc[e]);
+                                    const float qq = (g[e] * 0.5f) * q.iout * q.rc;
+                                    rd += qq;
+                                    C[4 * p + e] += qq;
+                                }
+                            }
                         }
                     }
                 }
+                rd = warp_sum<32>(rd);
+                if (lane == 0) a.rdot[b * L1 + i] = rd;
             }
+            __syncthreads();
+            if (j == rg.nb - 1) {
+                float* mb = reinterpret_cast<float*>(rg.stage(k));   // [NW][L2], 16 KB at most
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    const int64_t col = 4 * lane + 128 * p;
+                    if (col < L2) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) mb[wid * L2 + col + e] = C[4 * p + e];
+                    }
+                }
+                __syncthreads();
+                for (int64_t col = tid; col < L2; col += NT) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) s += mb[w * L2 + col];
+                    cp[col] = s;
+                }
+                fence_proxy_async_smem();
+                __syncthreads();
+            }
+            cl_next(rg, k, kfail);
         }
-        rd = warp_sum<32>(rd);
-        if (lane == 0) rdot[b * L1 + i] = rd;
-    }
-#pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        const int64_t col = 4 * lane + 128 * p;
-        if (col < L2) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) mrg[int64_t(wid) * L2 + col + e] = C[4 * p + e];
-        }
-    }
-    __syncthreads();
-    float* mypart = cpart + (b * c.nseg + blockIdx.x) * L2;
-    for (int64_t col = tid; col < L2; col += kBT) {
-        float s = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kBW; ++w) s += mrg[int64_t(w) * L2 + col];
-        if (c.nseg == 1) cdot[b * L2 + col] = s;
-        else mypart[col] = s;
-    }
-    if (c.nseg == 1) return;
-    if (!arrive_last_b(c.cnt, c.nseg, &s_flag)) return;
-    for (int64_t col = tid; col < L2; col += kBT) {
-        float s = 0.0f;
-        for (int sg = 0; sg < c.nseg; ++sg) s += __ldcg(cpart + (b * c.nseg + sg) * L2 + col);
-        cdot[b * L2 + col] = s;
-    }
-    if (tid == 0) c.cnt[b] = 0;
-}
+        if (rg.nb == 0)
+            for (int64_t col = tid; col < L2; col += NT) cp[col] = 0.0f;
+        cluster_sync();
 
-// ---------------------------------------------------------------------------
-// backward gradient, warp per row
-// ---------------------------------------------------------------------------
-template <typename T, typename G, int VPL>
-__global__ void __launch_bounds__(kBT)
-bsf_grad_kernel(const T* __restrict__ sim, const float* __restrict__ gout, BsfCommon c, int64_t B,
-                const float2* __restrict__ rstat, const float2* __restrict__ cstat, const float* __restrict__ rdot,
-                const float* __restrict__ cdot, G* __restrict__ gsim, float* __restrict__ tau_row) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t L1 = c.L1, L2 = c.L2;
-    const int64_t row = int64_t(blockIdx.x) * kBW + wid;
-    if (row >= B * L1) return;
-    const int64_t b = row / L1, i = row - b * L1;
-    int64_t l1, l2;
-    window(c.lengths, b, L1, L2, l1, l2);
-    const float2 rs = rstat[row];
-    const float rd = rdot[row];
-    const float2* cb = cstat + b * L2;
-    const float* cd = cdot + b * L2;
-    float acc = 0.0f;
+        // ---- column reduction ----
+        for (int64_t col = c0 + tid; col < c1; col += NT) {
+            float s = 0.0f;
+            for (uint32_t rr = 0; rr < kC; ++rr) s += ld_dsmem(dsmem(cp + col, rr));
+            cd[col] = s;
+        }
+        cluster_sync();
+        for (int64_t col = tid; col < L2; col += NT) {
+            const uint32_t owner = uint32_t(col / a.cols_per);
+            if (owner != rank) cd[col] = ld_dsmem(dsmem(cd + col, owner));
+        }
+        __syncthreads();
+
+        // ---- pass 2: gradient ----
+        for (int j = 0; j < rg.nb; ++j, ++k) {
+            const bool ok = cl_wait(rg, k, kfail);
+            const T* xs = reinterpret_cast<const T*>(rg.stage(k));
+            const float* gs = reinterpret_cast<const float*>(rg.stage(k) + a.tile_off1);
+            const int rows = rg.rows_in(j);
+            for (int il = wid; ok && il < rows; il += NW) {
+                const int64_t i = rg.r0 + int64_t(j) * a.R + il;
+                const float2 rs = __ldcg(a.rstat + b * L1 + i);
+                const float rd = __ldcg(a.rdot + b * L1 + i);
+                G* grow = gsim + (b * L1 + i) * L2;
+                float acc = 0.0f;
 #pragma unroll
-    for (int p = 0; p < VPL; ++p) {
-        const int64_t col = 4 * lane + 128 * p;
-        if (col >= L2) continue;
-        float gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (i < l1 && col < l2) {
-            float v[4], g[4];
-            ld4(sim + row * L2 + col, v);
-            ld4(gout + row * L2 + col, g);
+                for (int p = 0; p < VPL; ++p) {
+                    const int64_t col = 4 * lane + 128 * p;
+                    if (col >= L2) continue;
+                    float gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (i < l1 && col < l2) {
+                        float v[4], g[4];
+                        ld4s(xs + il * L2 + col, v);
+                        ld4s(gs + il * L2 + col, g);
+                        const float4 c01 = *reinterpret_cast<const float4*>(cs + col);
+                        const float4 c23 = *reinterpret_cast<const float4*>(cs + col + 2);
+                        const float4 d4 = *reinterpret_cast<const float4*>(cd + col);
+                        const float2 cc[4] = {make_float2(c01.x, c01.y), make_float2(c01.z, c01.w),
+                                              make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
+                        const float cdv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                if (col + e < l2) {
-                    const BsVals q = bs_vals(__fmul_rn(v[e], c.invT), rs, cb[col + e]);
-                    const float dp = q.out > 1e-9f ? g[e] * 0.5f / q.out : 0.0f;
-                    const float a = __fmul_rn(__fmul_rn(__fsub_rn(__fmul_rn(dp, q.col), rd), q.row), c.invT);
-                    const float cc =
-                        __fmul_rn(__fmul_rn(__fsub_rn(__fmul_rn(dp, q.row), cd[col + e]), q.col), c.invT);
-                    gr[e] = __fadd_rn(a, cc);
-                    acc += gr[e] * v[e] * c.invT;
+                        for (int e = 0; e < 4; ++e) {
+                            if (full || col + e < l2) {
+                                const BsVals q = bs_vals(__fmul_rn(v[e], a.invT), rs, cc[e]);
+                                const float qq = (g[e] * 0.5f) * q.iout * q.rc;
+                                gr[e] = (2.0f * qq - rd * q.row - cdv[e] * q.col) * a.invT;
+                                acc = fmaf(gr[e], v[e] * a.invT, acc);
+                            }
+                        }
+                    }
+                    st4g(grow + col, gr, pol_out);
+                }
+                if (a.tau_row != nullptr) {
+                    acc = warp_sum<32>(acc);
+                    if (lane == 0) a.tau_row[b * L1 + i] = acc;
                 }
             }
+            __syncthreads();
+            cl_next(rg, k, kfail);
         }
-        st4(gsim + row * L2 + col, gr);
     }
-    if (tau_row != nullptr) {
-        acc = warp_sum<32>(acc);
-        if (lane == 0) tau_row[row] = acc;
-    }
+    cluster_sync();
+    cl_drain(rg, kfail);
 }
 
 __global__ void bsf_batch_sum_kernel(const float* __restrict__ row_part, float* __restrict__ outv, int64_t B,
@@ -395,95 +636,120 @@ __global__ void bsf_batch_sum_kernel(const float* __restrict__ row_part, float* 
     if (lane == 0) outv[b] = acc * scale;
 }
 
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
 int vpl_of(int64_t L2) { return L2 <= 128 ? 1 : L2 <= 256 ? 2 : L2 <= 512 ? 4 : 8; }
 
-int bsf_sm_count() {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 148;
+// Rows per ring block: as many as fit one stage, a multiple of the warp
+// count, at most 64.
+int rows_per_block(int64_t row_bytes_total, int nw) {
+    int64_t r = kStage / row_bytes_total;
+    r = std::min<int64_t>(r, 64);
+    r = (r / nw) * nw;
+    return int(std::max<int64_t>(r, 1));
 }
 
-// Rows per segment: about 4 CTA waves over the batch, at least 8 rows per warp.
-int64_t bsf_seg_rows(int64_t B, int64_t L1) {
-    const int64_t slots = int64_t(bsf_sm_count()) * 2;
-    int64_t nseg = (4 * slots + B - 1) / B;
-    nseg = std::max<int64_t>(1, std::min<int64_t>(nseg, (L1 + 63) / 64));
-    int64_t seg = (L1 + nseg - 1) / nseg;
-    return ((seg + kBW - 1) / kBW) * kBW;
+size_t fwd_smem() { return size_t(kFwdStages) * kStage + 2 * kMaxL2 * sizeof(float2); }
+size_t bwd_smem() { return size_t(kBwdStages) * kStage + kMaxL2 * sizeof(float2) + 2 * kMaxL2 * sizeof(float); }
+
+cudaLaunchConfig_t cluster_config(int grid, int threads, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(unsigned(threads));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kC;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
 }
 
-struct BsfWs {
-    float2* cpart2;
-    float* cpart1;
-    float* rdot;
-    float* cdot;
-    float* tau_row;
-    int32_t* cnt;
-};
-
-BsfWs carve_bsf(Carve& c, int64_t B, int64_t L1, int64_t L2, bool bwd) {
-    const int64_t seg = bsf_seg_rows(B, L1);
-    const int64_t nseg = (L1 + seg - 1) / seg;
-    BsfWs w{};
-    if (!bwd) {
-        w.cpart2 = c.take<float2>(size_t(B * nseg * L2));
-    } else {
-        w.cpart1 = c.take<float>(size_t(B * nseg * L2));
-        w.rdot = c.take<float>(size_t(B * L1));
-        w.cdot = c.take<float>(size_t(B * L2));
-        w.tau_row = c.take<float>(size_t(B * L1));
+// Persistent grid: as many clusters as the GPU holds at once, at most B.
+template <typename K>
+int cluster_grid(K kernel, int threads, size_t smem, int64_t B, cudaStream_t st) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cluster_config(kC, threads, smem, st, attr);
+    int ncl = 0;
+    if (cudaOccupancyMaxActiveClusters(&ncl, kernel, &cfg) != cudaSuccess || ncl < 1) {
+        cudaGetLastError();
+        ncl = 1;
     }
-    w.cnt = c.take<int32_t>(size_t(B));
-    return w;
+    return int(std::min<int64_t>(ncl, B)) * kC;
+}
+
+ClArgs base_args(const void* sim, int esz, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau,
+                 int nw, bool with_grad) {
+    ClArgs a{};
+    a.src[0] = static_cast<const unsigned char*>(sim);
+    a.row_bytes[0] = uint32_t(L2 * esz);
+    a.nsrc = 1;
+    const int64_t row_total = L2 * esz + (with_grad ? L2 * 4 : 0);
+    a.R = rows_per_block(row_total, nw);
+    if (with_grad) {
+        a.nsrc = 2;
+        a.row_bytes[1] = uint32_t(L2 * 4);
+        a.tile_off1 = uint32_t((int64_t(a.R) * L2 * esz + 127) / 128 * 128);
+    }
+    a.lengths = lengths;
+    a.B = B;
+    a.L1 = L1;
+    a.L2 = L2;
+    a.rows_per = (L1 + kC - 1) / kC;
+    a.cols_per = (L2 + kC - 1) / kC;
+    a.invT = 1.0f / tau;
+    return a;
 }
 
 template <typename T, int VPL>
 int fwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau, float* out,
              float2* rstat, float2* cstat, void* ws, cudaStream_t st) {
-    Carve cv(ws);
-    BsfWs w = carve_bsf(cv, B, L1, L2, false);
-    BsfCommon c{lengths, L1, L2, 1.0f / tau, bsf_seg_rows(B, L1), 0, w.cnt};
-    c.nseg = int((L1 + c.seg_rows - 1) / c.seg_rows);
-    const size_t sm = size_t(kBW) * L2 * sizeof(float2);
-    cudaFuncSetAttribute(bsf_stats_kernel<T, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-    cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(B), st);
+    ClArgs a = base_args(sim, sizeof(T), lengths, B, L1, L2, tau, kFwdWarps, false);
+    a.rstat = rstat;
+    a.cstat = cstat;
+    a.out = out;
+    a.err = static_cast<int32_t*>(ws);
+    cudaMemsetAsync(a.err, 0, sizeof(int32_t), st);
+    const int grid = cluster_grid(bs_fwd_cluster_kernel<T, VPL>, kFwdWarps * 32, fwd_smem(), B, st);
     {
         ProfScope ps(DOT_K_BS_FWD, st);
-        bsf_stats_kernel<T, VPL><<<dim3(unsigned(c.nseg), unsigned(B)), kBT, sm, st>>>(sim, c, rstat, w.cpart2, cstat);
+        cudaLaunchAttribute attr[1];
+        cudaLaunchConfig_t cfg = cluster_config(grid, kFwdWarps * 32, fwd_smem(), st, attr);
+        cudaLaunchKernelEx(&cfg, bs_fwd_cluster_kernel<T, VPL>, a);
     }
-    {
-        ProfScope ps(DOT_K_BS_FWD, st);
-        bsf_out_kernel<T, VPL><<<unsigned(ceil_div(B * L1, kBW)), kBT, 0, st>>>(sim, c, B, rstat, cstat, out);
-    }
-    return check_launch("bidirectional softmax forward (fused)");
+    return check_launch("bidirectional softmax forward (cluster)");
 }
 
 template <typename T, typename G, int VPL>
 int bwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau, const float2* rstat,
              const float2* cstat, const float* gout, G* gsim, float* gtau, void* ws, cudaStream_t st) {
+    ClArgs a = base_args(sim, sizeof(T), lengths, B, L1, L2, tau, kBwdWarps, true);
+    a.src[1] = reinterpret_cast<const unsigned char*>(gout);
+    a.rstat = const_cast<float2*>(rstat);
+    a.cstat = const_cast<float2*>(cstat);
+    a.gsim = gsim;
     Carve cv(ws);
-    BsfWs w = carve_bsf(cv, B, L1, L2, true);
-    BsfCommon c{lengths, L1, L2, 1.0f / tau, bsf_seg_rows(B, L1), 0, w.cnt};
-    c.nseg = int((L1 + c.seg_rows - 1) / c.seg_rows);
-    const size_t sm = size_t(kBW) * L2 * sizeof(float) + size_t(L2) * sizeof(float2);
-    cudaFuncSetAttribute(bsf_dots_kernel<T, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-    cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(B), st);
+    a.err = cv.take<int32_t>(1);
+    a.rdot = cv.take<float>(size_t(B * L1));
+    float* tau_row = cv.take<float>(size_t(B * L1));
+    a.tau_row = gtau ? tau_row : nullptr;
+    cudaMemsetAsync(a.err, 0, sizeof(int32_t), st);
+    const int grid = cluster_grid(bs_bwd_cluster_kernel<T, G, VPL>, kBwdWarps * 32, bwd_smem(), B, st);
     {
         ProfScope ps(DOT_K_BS_BWD, st);
-        bsf_dots_kernel<T, VPL><<<dim3(unsigned(c.nseg), unsigned(B)), kBT, sm, st>>>(sim, gout, c, rstat, cstat,
-                                                                                      w.rdot, w.cpart1, w.cdot);
-    }
-    {
-        ProfScope ps(DOT_K_BS_BWD, st);
-        bsf_grad_kernel<T, G, VPL><<<unsigned(ceil_div(B * L1, kBW)), kBT, 0, st>>>(
-            sim, gout, c, B, rstat, cstat, w.rdot, w.cdot, gsim, gtau ? w.tau_row : nullptr);
+        cudaLaunchAttribute attr[1];
+        cudaLaunchConfig_t cfg = cluster_config(grid, kBwdWarps * 32, bwd_smem(), st, attr);
+        cudaLaunchKernelEx(&cfg, bs_bwd_cluster_kernel<T, G, VPL>, a);
     }
     if (gtau != nullptr) {
         ProfScope ps(DOT_K_BS_BWD, st);
-        bsf_batch_sum_kernel<<<unsigned(ceil_div(B, 8)), 256, 0, st>>>(w.tau_row, gtau, B, L1, -1.0f);
+        bsf_batch_sum_kernel<<<unsigned(ceil_div(B, 8)), 256, 0, st>>>(tau_row, gtau, B, L1, -1.0f);
     }
-    return check_launch("bidirectional softmax backward (fused)");
+    return check_launch("bidirectional softmax backward (cluster)");
 }
 
 template <typename T>
@@ -510,21 +776,28 @@ int bwd_dispatch(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, in
 
 }  // namespace
 
-bool bsf_supported(int64_t L2, const void* sim, int dtype, const void* gout, const void* gsim) {
-    const uintptr_t al = dtype == DOT_F32 ? 15u : 7u;
-    auto ok = [&](const void* p, uintptr_t mask) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & mask) == 0; };
-    return L2 >= 4 && L2 <= 1024 && (L2 % 4) == 0 && ok(sim, al) && ok(gout, 15u) && ok(gsim, 7u);
+// dst: out (forward, fp32) or grad_sim (backward, dst_dtype); gout non-null
+// for the backward.
+bool bsf_supported(int64_t B, int64_t L1, int64_t L2, int dtype, const void* sim, const void* gout, const void* dst,
+                   int dst_dtype) {
+    auto aligned = [](const void* p, uintptr_t a) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % a) == 0; };
+    if (L2 < 4 || L2 > kMaxL2 || L1 < 1 || B < 1) return false;
+    if (dtype == DOT_F32 ? (L2 % 4) != 0 : (L2 % 8) != 0) return false;
+    const int64_t esz = dtype == DOT_F32 ? 4 : 2;
+    const int R = gout ? rows_per_block(L2 * (esz + 4), kBwdWarps) : rows_per_block(L2 * esz, kFwdWarps);
+    // the block sequence index of a CTA is 32-bit
+    const int64_t nb = ((L1 + kC - 1) / kC + R - 1) / R;
+    if (2 * nb * B >= (int64_t(1) << 31)) return false;
+    return aligned(sim, 16) && aligned(gout, 16) && aligned(dst, dst_dtype == DOT_F32 ? 16 : 8);
 }
 
-size_t bsf_fwd_ws(int64_t B, int64_t L1, int64_t L2) {
-    Carve c(nullptr);
-    carve_bsf(c, B, L1, L2, false);
-    return c.size();
-}
+size_t bsf_fwd_ws(int64_t, int64_t, int64_t) { return 256; }
 
-size_t bsf_bwd_ws(int64_t B, int64_t L1, int64_t L2) {
+size_t bsf_bwd_ws(int64_t B, int64_t L1, int64_t) {
     Carve c(nullptr);
-    carve_bsf(c, B, L1, L2, true);
+    c.take<int32_t>(1);
+    c.take<float>(size_t(B * L1));
+    c.take<float>(size_t(B * L1));
     return c.size();
 }
 

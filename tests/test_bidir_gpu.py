@@ -69,6 +69,11 @@ CASES = [
     (2, 129, 127, 0.05, None),
     (1, 1300, 40, 0.2, [[1250, 33]]),   # tall: column statistics span several row chunks
     (2, 64, 1024, 0.1, None),
+    # cluster path (L2 <= 1024, L2 % 4 == 0): fewer rows than CTAs per cluster,
+    # ragged and empty windows, more problems than resident clusters
+    (5, 3, 64, 0.5, None),
+    (4, 37, 256, 0.2, [[37, 256], [30, 200], [1, 8], [0, 0]]),
+    (300, 16, 96, 0.3, None),
 ]
 
 
@@ -89,6 +94,24 @@ def test_oracle_and_fp64_parity(B, L1, L2, tau, lengths):
     (o64 * go.double()).sum().backward()
     U.assert_normwise(out, o64.detach(), U.PLAN_RTOL, "out vs fp64")
     U.assert_normwise(grad, s64.grad, U.GRAD_RTOL, "grad vs fp64")
+
+
+@pytest.mark.parametrize("B,L1,L2,lengths", [(3, 45, 136, [[45, 136], [20, 64], [45, 7]]), (2, 9, 1024, None)])
+def test_bf16_input_against_oracle(B, L1, L2, lengths):
+    """bf16 input on the cluster path: the oracle runs on the same bf16 values
+    upcast to fp32 (the reference's own cast); the bf16 gradient is compared
+    within one bf16 rounding."""
+    g = U.gen(L1 * 11 + L2)
+    sim = torch.randn(B, L1, L2, generator=g).bfloat16()
+    go = torch.randn(B, L1, L2, generator=g)
+    ln = np.array(lengths if lengths is not None else [[L1, L2]] * B, np.int32)
+    ref = O.bidir_api(sim.float().numpy(), 0.1, ln, go.numpy())
+    out, grad = run(sim, 0.1, ln, go)
+    assert grad.dtype == torch.bfloat16
+    assert np.abs(U.to_np(out) - ref["out"]).max() <= OUT_ATOL
+    U.assert_normwise(out, ref["out"], U.PLAN_RTOL, "out")
+    ref_bf = torch.from_numpy(ref["grad"]).bfloat16().float()
+    U.assert_normwise(grad.float(), ref_bf, 1e-2, "grad")
 
 
 def test_reference_behaviour():
