@@ -36,6 +36,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -47,10 +48,9 @@ namespace {
 
 constexpr int kC = 8;               // CTAs per cluster
 constexpr int kStage = 32768;       // bytes per ring stage
-constexpr int kMergeCols = 512;
 constexpr int kMaxL2 = 1024;
 constexpr int kFwdWarps = 8;
-constexpr int kBwdWarps = 4;
+constexpr int kBwdWarps = 8;
 constexpr int kFwdStages = 2;
 constexpr int kBwdStages = 3;
 constexpr float kRaiseB = 60.0f;
@@ -282,20 +282,36 @@ __device__ __forceinline__ void cl_drain(const ClRing<S>& r, int kfail) {
     __syncthreads();
 }
 
+// Warp layout.  The NW warps of a CTA form NW/WPR row slots of WPR warps;
+// slot q takes rows q, q + NW/WPR, ... of each block, and warp c of a slot
+// takes columns c*128*VPLW + 4*lane + 128*p (p < VPLW) of its rows, so a lane
+// keeps NC = 4*VPLW columns in registers.  Rows of 1024 columns are split
+// over WPR = 2 warps (16 columns per lane); the per-row reductions of the WPR
+// warps meet in shared memory after the block's barrier.
+template <int VPL>
+struct WL {
+    static constexpr int WPR = VPL >= 8 ? 2 : 1;   // warps per row
+    static constexpr int VPLW = VPL / WPR;          // float4 groups per lane
+    static constexpr int NC = 4 * VPLW;             // columns per lane
+};
+
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
 template <typename T, int VPL>
-__global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArgs a) {
-    constexpr int NW = kFwdWarps, NC = 4 * VPL, S = kFwdStages, NT = NW * 32;
+__global__ void __launch_bounds__(kFwdWarps * 32, 3) bs_fwd_cluster_kernel(ClArgs a) {
+    constexpr int NW = kFwdWarps, S = kFwdStages, NT = NW * 32;
+    constexpr int WPR = WL<VPL>::WPR, VPLW = WL<VPL>::VPLW, NC = WL<VPL>::NC, SLOTS = NW / WPR;
     extern __shared__ __align__(128) unsigned char smem[];
-    float2* cp = reinterpret_cast<float2*>(smem + size_t(S) * kStage);   // [kMaxL2] this CTA's column partials
-    float2* cs = cp + kMaxL2;                                             // [kMaxL2] column statistics
+    float2* cs = reinterpret_cast<float2*>(smem + size_t(S) * kStage);   // [kMaxL2] column statistics
     __shared__ __align__(8) uint64_t bars[S];
+    __shared__ float2 s_rp[64][WPR];   // per-row (max, sum) of each warp of the row
     __shared__ int s_nfix;
-    __shared__ int s_fix[kMaxL2];
+    __shared__ int s_fix[kMaxL2 / kC];
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int slot = wid / WPR, cpart = wid % WPR;
+    const int64_t cbase = int64_t(cpart) * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
     const uint32_t rank = cluster_rank();
     ClRing<S> rg = cl_ring_init<S>(a, bars, smem);
@@ -307,27 +323,29 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArg
         int64_t l1, l2;
         window(a.lengths, b, L1, L2, l1, l2);
         const T* sb = reinterpret_cast<const T*>(a.src[0]) + b * L1 * L2;
+        const bool full = l2 == L2;
 
         // ---- pass 1: row statistics, column partials ----
         float Sc[NC];
 #pragma unroll
         for (int e = 0; e < NC; ++e) Sc[e] = 0.0f;
         float A = kNegBig;
-        const bool full = l2 == L2;
+        float2* cp = nullptr;   // merged column partials, in the last pass-1 stage
+        int kcp = -1;
         for (int j = 0; j < rg.nb; ++j, ++k) {
             const bool ok = cl_wait(rg, k, kfail);
             const T* xs = reinterpret_cast<const T*>(rg.stage(k));
             const int rows = rg.rows_in(j);
-            for (int il = wid; ok && il < rows; il += NW) {
+            for (int il = slot; ok && il < rows; il += SLOTS) {
                 const int64_t i = rg.r0 + int64_t(j) * a.R + il;
                 if (i >= l1 || l2 == 0) {
-                    if (lane == 0) a.rstat[b * L1 + i] = make_float2(0.0f, 0.0f);
+                    if (lane == 0) s_rp[il][cpart] = make_float2(kNegBig, 0.0f);
                     continue;
                 }
                 float t[NC];
 #pragma unroll
-                for (int p = 0; p < VPL; ++p) {
-                    const int64_t col = 4 * lane + 128 * p;
+                for (int p = 0; p < VPLW; ++p) {
+                    const int64_t col = cbase + 4 * lane + 128 * p;
                     float v[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
                     if (col < L2) {
                         ld4s(xs + il * L2 + col, v);
@@ -346,55 +364,68 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArg
 #pragma unroll
                 for (int e = 1; e < NC; ++e) mx = fmaxf(mx, t[e]);
                 mx = warp_max<32>(mx);
+                float s = 0.0f;
+                if (mx != -INFINITY) {   // warp-uniform; else every column of this warp's part is masked
 #pragma unroll
-                for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
-                const float s = warp_sum<32>(tree_sum(t));
-                if (lane == 0) a.rstat[b * L1 + i] = make_float2(mx, s > 0.0f ? 1.0f / s : 0.0f);
-                if (mx > A + kRaiseB) {   // warp-uniform
-                    const float sc = exp_shift(A - mx);
+                    for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
+                    s = warp_sum<32>(tree_sum(t));
+                    if (mx > A + kRaiseB) {
+                        const float sc = exp_shift(A - mx);
 #pragma unroll
-                    for (int e = 0; e < NC; ++e) Sc[e] *= sc;
-                    A = mx;
+                        for (int e = 0; e < NC; ++e) Sc[e] *= sc;
+                        A = mx;
+                    }
+                    const float w = exp_shift(mx - A);
+#pragma unroll
+                    for (int e = 0; e < NC; ++e) Sc[e] = fmaf(t[e], w, Sc[e]);
                 }
-                const float w = exp_shift(mx - A);
-#pragma unroll
-                for (int e = 0; e < NC; ++e) Sc[e] = fmaf(t[e], w, Sc[e]);
+                if (lane == 0) s_rp[il][cpart] = make_float2(mx == -INFINITY ? kNegBig : mx, s);
             }
             __syncthreads();
-            if (j == rg.nb - 1) {
-                // merge the warps' partials into cp through the free stage buffer
-                float2* mb = reinterpret_cast<float2*>(rg.stage(k));   // [NW][kMergeCols]
+            // row statistics from the WPR warps of each row
+            if (ok && tid < rows) {
+                const int64_t i = rg.r0 + int64_t(j) * a.R + tid;
+                float2 st = make_float2(0.0f, 0.0f);
+                if (i < l1 && l2 > 0) {
+                    float mm = kNegBig, ss = 0.0f;
 #pragma unroll
-                for (int ch = 0; ch < (VPL + 3) / 4; ++ch) {
-#pragma unroll
-                    for (int p = 4 * ch; p < VPL && p < 4 * ch + 4; ++p) {
-                        const int64_t col = 4 * lane + 128 * p;
-                        if (col < L2) {
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                mb[wid * kMergeCols + 4 * lane + 128 * (p - 4 * ch) + e] = make_float2(A, Sc[4 * p + e]);
-                        }
-                    }
-                    __syncthreads();
-                    const int ncols = int(min(int64_t(kMergeCols), L2 - int64_t(kMergeCols) * ch));
-                    for (int cl = tid; cl < ncols; cl += NT) {
-                        float mm = kNegBig, ss = 0.0f;
-#pragma unroll
-                        for (int w = 0; w < NW; ++w) {
-                            const float2 q = mb[w * kMergeCols + cl];
-                            lse_merge(mm, ss, q.x, q.y);
-                        }
-                        cp[kMergeCols * ch + cl] = make_float2(mm, ss);
-                    }
-                    __syncthreads();
+                    for (int c = 0; c < WPR; ++c) lse_merge(mm, ss, s_rp[tid][c].x, s_rp[tid][c].y);
+                    st = make_float2(mm, ss > 0.0f ? 1.0f / ss : 0.0f);
                 }
-                fence_proxy_async_smem();
-                __syncthreads();
+                a.rstat[b * L1 + i] = st;
             }
-            cl_next(rg, k, kfail);
+            if (j == rg.nb - 1) {
+                // merge the slots' partials into cp (aliasing the stage buffer:
+                // [SLOTS][L2] float2 <= 32 KB); the stage is refilled only after
+                // the cluster has read cp
+                float2* mb = reinterpret_cast<float2*>(rg.stage(k));
+#pragma unroll
+                for (int p = 0; p < VPLW; ++p) {
+                    const int64_t col = cbase + 4 * lane + 128 * p;
+                    if (col < L2) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) mb[slot * L2 + col + e] = make_float2(A, Sc[4 * p + e]);
+                    }
+                }
+                __syncthreads();
+                for (int64_t col = tid; col < L2; col += NT) {
+                    float mm = kNegBig, ss = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < SLOTS; ++q) {
+                        const float2 v = mb[q * L2 + col];
+                        lse_merge(mm, ss, v.x, v.y);
+                    }
+                    mb[col] = make_float2(mm, ss);   // only this thread reads column col
+                }
+                cp = mb;
+                kcp = k;
+            } else {
+                cl_next(rg, k, kfail);
+            }
         }
-        if (rg.nb == 0)
-            for (int64_t col = tid; col < L2; col += NT) cp[col] = make_float2(kNegBig, 0.0f);
+        float2* cpx = cp != nullptr ? cp : reinterpret_cast<float2*>(rg.stage(0));
+        if (rg.nb == 0)   // no rows: neutral partials (no copies are ever in flight)
+            for (int64_t col = tid; col < L2; col += NT) cpx[col] = make_float2(kNegBig, 0.0f);
         if (tid == 0) s_nfix = 0;
         cluster_sync();
 
@@ -402,7 +433,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArg
         for (int64_t col = c0 + tid; col < c1; col += NT) {
             float mm = kNegBig, ss = 0.0f;
             for (uint32_t rr = 0; rr < kC; ++rr) {
-                const float2 q = ld_dsmem2(dsmem(cp + col, rr));
+                const float2 q = ld_dsmem2(dsmem(cpx + col, rr));
                 lse_merge(mm, ss, q.x, q.y);
             }
             float2 st = make_float2(0.0f, 0.0f);
@@ -423,6 +454,11 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArg
             }
         }
         cluster_sync();
+        if (kcp >= 0) {   // cp has been read by the whole cluster: refill its stage
+            fence_proxy_async_smem();
+            __syncthreads();
+            cl_next(rg, kcp, kfail);
+        }
         for (int64_t col = tid; col < L2; col += NT) {
             const uint32_t owner = uint32_t(col / a.cols_per);
             if (owner != rank) cs[col] = ld_dsmem2(dsmem(cs + col, owner));
@@ -434,16 +470,17 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArg
             const bool ok = cl_wait(rg, k, kfail);
             const T* xs = reinterpret_cast<const T*>(rg.stage(k));
             const int rows = rg.rows_in(j);
-            for (int il = wid; ok && il < rows; il += NW) {
+            for (int il = slot; ok && il < rows; il += SLOTS) {
                 const int64_t i = rg.r0 + int64_t(j) * a.R + il;
                 const float2 rs = __ldcg(a.rstat + b * L1 + i);
                 float* orow = a.out + (b * L1 + i) * L2;
+                const bool live = i < l1;
 #pragma unroll
-                for (int p = 0; p < VPL; ++p) {
-                    const int64_t col = 4 * lane + 128 * p;
+                for (int p = 0; p < VPLW; ++p) {
+                    const int64_t col = cbase + 4 * lane + 128 * p;
                     if (col >= L2) continue;
                     float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if (i < l1 && col < l2) {
+                    if (live && col < l2) {
                         float v[4];
                         ld4s(xs + il * L2 + col, v);
                         const float4 c01 = *reinterpret_cast<const float4*>(cs + col);
@@ -470,14 +507,17 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 2) bs_fwd_cluster_kernel(ClArg
 // ---------------------------------------------------------------------------
 template <typename T, typename G, int VPL>
 __global__ void __launch_bounds__(kBwdWarps * 32, 2) bs_bwd_cluster_kernel(ClArgs a) {
-    constexpr int NW = kBwdWarps, NC = 4 * VPL, S = kBwdStages, NT = NW * 32;
+    constexpr int NW = kBwdWarps, S = kBwdStages, NT = NW * 32;
+    constexpr int WPR = WL<VPL>::WPR, VPLW = WL<VPL>::VPLW, NC = WL<VPL>::NC, SLOTS = NW / WPR;
     extern __shared__ __align__(128) unsigned char smem[];
     float2* cs = reinterpret_cast<float2*>(smem + size_t(S) * kStage);   // [kMaxL2] column statistics
-    float* cp = reinterpret_cast<float*>(cs + kMaxL2);                    // [kMaxL2] column partials of q
-    float* cd = cp + kMaxL2;                                              // [kMaxL2] cdot
+    float* cd = reinterpret_cast<float*>(cs + kMaxL2);                    // [kMaxL2] cdot
     __shared__ __align__(8) uint64_t bars[S];
+    __shared__ float s_rp[64][WPR];   // per-row partial sums of the row's warps
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int slot = wid / WPR, cpart = wid % WPR;
+    const int64_t cbase = int64_t(cpart) * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
     const uint32_t rank = cluster_rank();
     ClRing<S> rg = cl_ring_init<S>(a, bars, smem);
@@ -497,19 +537,21 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bs_bwd_cluster_kernel(ClArg
         float C[NC];
 #pragma unroll
         for (int e = 0; e < NC; ++e) C[e] = 0.0f;
+        float* cp = nullptr;
+        int kcp = -1;
         for (int j = 0; j < rg.nb; ++j, ++k) {
             const bool ok = cl_wait(rg, k, kfail);
             const T* xs = reinterpret_cast<const T*>(rg.stage(k));
             const float* gs = reinterpret_cast<const float*>(rg.stage(k) + a.tile_off1);
             const int rows = rg.rows_in(j);
-            for (int il = wid; ok && il < rows; il += NW) {
+            for (int il = slot; ok && il < rows; il += SLOTS) {
                 const int64_t i = rg.r0 + int64_t(j) * a.R + il;
                 float rd = 0.0f;
                 if (i < l1) {
                     const float2 rs = __ldcg(a.rstat + b * L1 + i);
 #pragma unroll
-                    for (int p = 0; p < VPL; ++p) {
-                        const int64_t col = 4 * lane + 128 * p;
+                    for (int p = 0; p < VPLW; ++p) {
+                        const int64_t col = cbase + 4 * lane + 128 * p;
                         if (col < l2) {
                             float v[4], g[4];
                             ld4s(xs + il * L2 + col, v);
@@ -531,42 +573,55 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bs_bwd_cluster_kernel(ClArg
                     }
                 }
                 rd = warp_sum<32>(rd);
-                if (lane == 0) a.rdot[b * L1 + i] = rd;
+                if (lane == 0) s_rp[il][cpart] = rd;
             }
             __syncthreads();
-            if (j == rg.nb - 1) {
-                float* mb = reinterpret_cast<float*>(rg.stage(k));   // [NW][L2], 16 KB at most
+            if (ok && tid < rows) {
+                float rd = 0.0f;
 #pragma unroll
-                for (int p = 0; p < VPL; ++p) {
-                    const int64_t col = 4 * lane + 128 * p;
+                for (int c = 0; c < WPR; ++c) rd += s_rp[tid][c];
+                a.rdot[b * L1 + rg.r0 + int64_t(j) * a.R + tid] = rd;
+            }
+            if (j == rg.nb - 1) {
+                float* mb = reinterpret_cast<float*>(rg.stage(k));   // [SLOTS][L2] <= 16 KB
+#pragma unroll
+                for (int p = 0; p < VPLW; ++p) {
+                    const int64_t col = cbase + 4 * lane + 128 * p;
                     if (col < L2) {
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) mb[wid * L2 + col + e] = C[4 * p + e];
+                        for (int e = 0; e < 4; ++e) mb[slot * L2 + col + e] = C[4 * p + e];
                     }
                 }
                 __syncthreads();
                 for (int64_t col = tid; col < L2; col += NT) {
-                    float s = 0.0f;
+                    float sum = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) s += mb[w * L2 + col];
-                    cp[col] = s;
+                    for (int q = 0; q < SLOTS; ++q) sum += mb[q * L2 + col];
+                    mb[col] = sum;   // only this thread reads column col
                 }
-                fence_proxy_async_smem();
-                __syncthreads();
+                cp = mb;
+                kcp = k;
+            } else {
+                cl_next(rg, k, kfail);
             }
-            cl_next(rg, k, kfail);
         }
+        float* cpx = cp != nullptr ? cp : reinterpret_cast<float*>(rg.stage(0));
         if (rg.nb == 0)
-            for (int64_t col = tid; col < L2; col += NT) cp[col] = 0.0f;
+            for (int64_t col = tid; col < L2; col += NT) cpx[col] = 0.0f;
         cluster_sync();
 
         // ---- column reduction ----
         for (int64_t col = c0 + tid; col < c1; col += NT) {
-            float s = 0.0f;
-            for (uint32_t rr = 0; rr < kC; ++rr) s += ld_dsmem(dsmem(cp + col, rr));
-            cd[col] = s;
+            float sum = 0.0f;
+            for (uint32_t rr = 0; rr < kC; ++rr) sum += ld_dsmem(dsmem(cpx + col, rr));
+            cd[col] = sum;
         }
         cluster_sync();
+        if (kcp >= 0) {
+            fence_proxy_async_smem();
+            __syncthreads();
+            cl_next(rg, kcp, kfail);
+        }
         for (int64_t col = tid; col < L2; col += NT) {
             const uint32_t owner = uint32_t(col / a.cols_per);
             if (owner != rank) cd[col] = ld_dsmem(dsmem(cd + col, owner));
@@ -579,18 +634,19 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bs_bwd_cluster_kernel(ClArg
             const T* xs = reinterpret_cast<const T*>(rg.stage(k));
             const float* gs = reinterpret_cast<const float*>(rg.stage(k) + a.tile_off1);
             const int rows = rg.rows_in(j);
-            for (int il = wid; ok && il < rows; il += NW) {
+            for (int il = slot; ok && il < rows; il += SLOTS) {
                 const int64_t i = rg.r0 + int64_t(j) * a.R + il;
                 const float2 rs = __ldcg(a.rstat + b * L1 + i);
                 const float rd = __ldcg(a.rdot + b * L1 + i);
                 G* grow = gsim + (b * L1 + i) * L2;
+                const bool live = i < l1;
                 float acc = 0.0f;
 #pragma unroll
-                for (int p = 0; p < VPL; ++p) {
-                    const int64_t col = 4 * lane + 128 * p;
+                for (int p = 0; p < VPLW; ++p) {
+                    const int64_t col = cbase + 4 * lane + 128 * p;
                     if (col >= L2) continue;
                     float gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if (i < l1 && col < l2) {
+                    if (live && col < l2) {
                         float v[4], g[4];
                         ld4s(xs + il * L2 + col, v);
                         ld4s(gs + il * L2 + col, g);
@@ -614,10 +670,16 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bs_bwd_cluster_kernel(ClArg
                 }
                 if (a.tau_row != nullptr) {
                     acc = warp_sum<32>(acc);
-                    if (lane == 0) a.tau_row[b * L1 + i] = acc;
+                    if (lane == 0) s_rp[il][cpart] = acc;
                 }
             }
             __syncthreads();
+            if (a.tau_row != nullptr && ok && tid < rows) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int c = 0; c < WPR; ++c) acc += s_rp[tid][c];
+                a.tau_row[b * L1 + rg.r0 + int64_t(j) * a.R + tid] = acc;
+            }
             cl_next(rg, k, kfail);
         }
     }
@@ -650,8 +712,23 @@ int rows_per_block(int64_t row_bytes_total, int nw) {
     return int(std::max<int64_t>(r, 1));
 }
 
-size_t fwd_smem() { return size_t(kFwdStages) * kStage + 2 * kMaxL2 * sizeof(float2); }
-size_t bwd_smem() { return size_t(kBwdStages) * kStage + kMaxL2 * sizeof(float2) + 2 * kMaxL2 * sizeof(float); }
+// DOT_B200_BS_SMEM_PAD_KB adds dynamic shared memory per CTA (tuning runs:
+// fewer resident CTAs, hence fewer problems in flight).
+size_t smem_pad() {
+    static size_t v = [] {
+        const char* e = std::getenv("DOT_B200_BS_SMEM_PAD_KB");
+        const long kb = e ? std::atol(e) : 0;
+        return size_t(kb > 0 && kb < 128 ? kb : 0) << 10;
+    }();
+    return v;
+}
+size_t fwd_smem() { return size_t(kFwdStages) * kStage + kMaxL2 * sizeof(float2) + smem_pad(); }
+size_t bwd_smem() {
+    return size_t(kBwdStages) * kStage + kMaxL2 * sizeof(float2) + kMaxL2 * sizeof(float) + smem_pad();
+}
+
+// Row slots of a CTA (warps / warps per row).
+int slots_for(int64_t L2, int nw) { return vpl_of(L2) >= 8 ? nw / 2 : nw; }
 
 cudaLaunchConfig_t cluster_config(int grid, int threads, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
@@ -689,7 +766,7 @@ ClArgs base_args(const void* sim, int esz, const int32_t* lengths, int64_t B, in
     a.row_bytes[0] = uint32_t(L2 * esz);
     a.nsrc = 1;
     const int64_t row_total = L2 * esz + (with_grad ? L2 * 4 : 0);
-    a.R = rows_per_block(row_total, nw);
+    a.R = rows_per_block(row_total, slots_for(L2, nw));
     if (with_grad) {
         a.nsrc = 2;
         a.row_bytes[1] = uint32_t(L2 * 4);
@@ -784,7 +861,8 @@ bool bsf_supported(int64_t B, int64_t L1, int64_t L2, int dtype, const void* sim
     if (L2 < 4 || L2 > kMaxL2 || L1 < 1 || B < 1) return false;
     if (dtype == DOT_F32 ? (L2 % 4) != 0 : (L2 % 8) != 0) return false;
     const int64_t esz = dtype == DOT_F32 ? 4 : 2;
-    const int R = gout ? rows_per_block(L2 * (esz + 4), kBwdWarps) : rows_per_block(L2 * esz, kFwdWarps);
+    const int R = gout ? rows_per_block(L2 * (esz + 4), slots_for(L2, kBwdWarps))
+                       : rows_per_block(L2 * esz, slots_for(L2, kFwdWarps));
     // the block sequence index of a CTA is 32-bit
     const int64_t nb = ((L1 + kC - 1) / kC + R - 1) / R;
     if (2 * nb * B >= (int64_t(1) << 31)) return false;
