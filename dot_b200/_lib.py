@@ -39,6 +39,9 @@ _SIGS = {
     "dot_sinkhorn_rows": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _i64, _f, _vp, _vp, _vp]),
     "dot_sinkhorn_col_partials_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "dot_sinkhorn_col_partials": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _f, _vp, _vp, _vp, _sz, _vp]),
+    "dot_sinkhorn_col_pairs_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "dot_sinkhorn_col_pairs": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _f, _vp, _vp, _sz, _vp]),
+    "dot_sinkhorn_col_merge": (_i, [_vp, _i, _vp, _i64, _i64, _vp, _vp]),
     "dot_sinkhorn_col_rescale": (_i, [_vp, _vp, _vp, _i64, _vp]),
     "dot_sinkhorn_col_finish": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _vp]),
     "dot_sinkhorn_plan_workspace_bytes": (_sz, [_i64, _i64, _i64]),

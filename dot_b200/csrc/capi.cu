@@ -249,6 +249,40 @@ int dot_sinkhorn_col_partials(const float* X, float score_sign, const float* pot
                             static_cast<cudaStream_t>(stream));
 }
 
+size_t dot_sinkhorn_col_pairs_workspace_bytes(int64_t B, int64_t n, int64_t m) {
+    if (B <= 0 || n <= 0 || m <= 0) return 0;
+    return sk_split_colpairs_ws(B, n, m);
+}
+
+int dot_sinkhorn_col_pairs(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n, int64_t m,
+                           float tau, float* pairs, void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !pot_u || !pairs) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    if ((reinterpret_cast<uintptr_t>(pairs) & 7u) != 0) return fail(DOT_ERR_INVALID, "pairs must be 8-byte aligned");
+    const size_t need = sk_split_colpairs_ws(B, n, m);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    return sk_split_colpairs(X, score_sign * (1.0f / tau), pot_u, B, n, m, reinterpret_cast<float2*>(pairs), workspace,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int dot_sinkhorn_col_merge(const float* pairs, int parts, const float* log_b, int64_t B, int64_t m, float* pot_v,
+                           void* stream) {
+    clear_error();
+    if (B < 0 || m < 0) return fail(DOT_ERR_INVALID, "negative dimension");
+    if (parts < 1) return fail(DOT_ERR_INVALID, "parts must be >= 1");
+    if (B == 0 || m == 0) return DOT_OK;
+    if (!pairs || !pot_v) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    if ((reinterpret_cast<uintptr_t>(pairs) & 7u) != 0) return fail(DOT_ERR_INVALID, "pairs must be 8-byte aligned");
+    return sk_split_pair_merge(reinterpret_cast<const float2*>(pairs), parts, log_b, -logf(float(m)), B, m, pot_v,
+                               static_cast<cudaStream_t>(stream));
+}
+
 int dot_sinkhorn_col_rescale(const float* col_max, float* col_sum, const float* global_max, int64_t count,
                              void* stream) {
     clear_error();

@@ -80,6 +80,11 @@ int sk_split_rows(const float* X, float kinv, const float* la, float la_def, int
 size_t sk_split_colpart_ws(int64_t B, int64_t n, int64_t m);
 int sk_split_colpart(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m,
                      float* col_max, float* col_sum, void* ws, cudaStream_t st);
+size_t sk_split_colpairs_ws(int64_t B, int64_t n, int64_t m);
+int sk_split_colpairs(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m, float2* pairs,
+                      void* ws, cudaStream_t st);
+int sk_split_pair_merge(const float2* pairs, int parts, const float* lb, float lb_def, int64_t B, int64_t m,
+                        float* v2, cudaStream_t st);
 int sk_split_rescale(const float* col_max, float* col_sum, const float* gmax, int64_t count, cudaStream_t st);
 int sk_split_finish(const float* gmax, const float* gsum, const float* lb, float lb_def, int64_t count, float* v2,
                     cudaStream_t st);

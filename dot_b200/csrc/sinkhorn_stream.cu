@@ -219,6 +219,20 @@ __global__ void sk_col_merge_kernel(const float2* __restrict__ part, const float
     else v2[idx] = (lb ? lb[idx] : lb_def) - lse_finish(mm, ss);
 }
 
+// Shard combine in one step: pairs [parts][count] (each shard's column
+// (max, sum) over its rows, gathered from every rank) merged in shard order.
+__global__ void sk_shard_merge_kernel(const float2* __restrict__ pairs, int parts, const float* __restrict__ lb,
+                                      float lb_def, float* __restrict__ v2, int64_t count) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    float mm = kNegBig, ss = 0.0f;
+    for (int p = 0; p < parts; ++p) {
+        const float2 q = pairs[int64_t(p) * count + i];
+        lse_merge(mm, ss, q.x, q.y);
+    }
+    v2[i] = (lb ? lb[i] : lb_def) - lse_finish(mm, ss);
+}
+
 // (max, sum) pairs -> two arrays (the form the shard all-reduces take).
 __global__ void sk_pair_unpack_kernel(const float2* __restrict__ pair, float* __restrict__ max_out,
                                       float* __restrict__ sum_out, int64_t count) {
@@ -793,6 +807,44 @@ int sk_split_colpart(const float* X, float kinv, const float* u2, int64_t B, int
     }
     sk_pair_unpack_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pair, col_max, col_sum, B * m);
     return check_launch("sinkhorn column partials");
+}
+
+size_t sk_split_colpairs_ws(int64_t B, int64_t n, int64_t m) {
+    Carve c(nullptr);
+    const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
+    if (chunks > 1) c.take<float2>(size_t(B * chunks * m));
+    return c.size();
+}
+
+int sk_split_colpairs(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m, float2* pairs,
+                      void* ws, cudaStream_t st) {
+    Carve c(ws);
+    const int64_t rpc = col_rows_per_chunk(n);
+    const int chunks = int(ceil_div(n, rpc));
+    float2* part = chunks > 1 ? c.take<float2>(size_t(B * chunks * m)) : nullptr;
+    SkCtl ctl{nullptr, nullptr, 0.0f, 0};
+    const dim3 col_grid(unsigned(ceil_div(m, kColTile)), unsigned(chunks), unsigned(B));
+    {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st);
+        sk_col_kernel<<<col_grid, kColWarps * 32, 0, st>>>(X, kinv, u2, nullptr, 0.0f, nullptr, part, n, m, rpc,
+                                                           chunks, ctl, pairs);
+    }
+    if (chunks > 1) {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st);
+        sk_col_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(part, nullptr, 0.0f, nullptr, B, m,
+                                                                            chunks, ctl, pairs);
+    }
+    return check_launch("sinkhorn column pairs");
+}
+
+int sk_split_pair_merge(const float2* pairs, int parts, const float* lb, float lb_def, int64_t B, int64_t m,
+                        float* v2, cudaStream_t st) {
+    // the shards' pairs laid out [parts][B*m] are the chunk partials of one
+    // problem: merge them in shard order exactly as the chunk merge does
+    SkCtl ctl{nullptr, nullptr, 0.0f, 0};
+    ProfScope ps(DOT_K_SK_FWD_ITER, st);
+    sk_shard_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pairs, parts, lb, lb_def, v2, B * m);
+    return check_launch("sinkhorn shard merge");
 }
 
 int sk_split_rescale(const float* col_max, float* col_sum, const float* gmax, int64_t count, cudaStream_t st) {

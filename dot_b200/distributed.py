@@ -10,10 +10,13 @@ no multi-GPU path):
   32768 x 32768): rank r holds rows ``shard_range(n_total, r, world)`` of the
   cost.  Per iteration the row half-step is local; the column half-step needs
   LSE over all rows, which is combined from per-rank ``(max, sum)`` partials
-  with two all-reduces -- MAX of the maxima, then SUM of the sums rescaled to
-  the global maximum (:func:`combine_column_partials`).  This is exact (the
-  same combine the single-GPU kernels use across row chunks); the only
-  difference to one GPU is the summation order across ranks.
+  with one all-gather of every rank's ``(max, sum)`` pairs, merged in rank
+  order on every rank (:func:`gather_column_pairs` and
+  ``dot_sinkhorn_col_merge``), so all ranks hold the same ``v``.  This is the
+  combine the single-GPU kernels use across row chunks; the only difference to
+  one GPU is where the row chunks end.  :func:`combine_column_partials` is the
+  two-all-reduce form of the same combine (MAX of the maxima, then SUM of the
+  sums rescaled to the global maximum).
 """
 
 from __future__ import annotations
@@ -54,6 +57,20 @@ def combine_column_partials(col_max: torch.Tensor, col_sum: torch.Tensor,
     return gmax, col_sum
 
 
+def gather_column_pairs(pairs: torch.Tensor, group=None) -> tuple[torch.Tensor, int]:
+    """All-gather this rank's column ``(max, sum)`` pairs ``[B, m, 2]`` into
+    ``[world, B, m, 2]`` in rank order.  Returns ``(gathered, world)``; every
+    rank performs the same single collective."""
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return pairs, 1
+    world = dist.get_world_size(group)
+    flat = pairs.contiguous()
+    # concatenated along dim 0 (the layout every backend accepts), viewed stacked
+    out = flat.new_empty((world * flat.shape[0],) + tuple(flat.shape[1:]))
+    dist.all_gather_into_tensor(out, flat, group=group)
+    return out.view((world,) + tuple(flat.shape)), world
+
+
 def _c_rescale(col_max: torch.Tensor, col_sum: torch.Tensor, gmax: torch.Tensor) -> None:
     lib = _lib.load()
     _lib.check(lib.dot_sinkhorn_col_rescale(_lib.ptr(col_max), _lib.ptr(col_sum), _lib.ptr(gmax), col_max.numel(),
@@ -85,19 +102,17 @@ def sinkhorn_rowshard(C_local: torch.Tensor, reg: float, n_iters: int, n_total: 
     lb = None if log_b is None else log_b.to(device=dev, dtype=torch.float32).contiguous()
     u = torch.zeros((B, n), dtype=torch.float32, device=dev)
     v = torch.zeros((B, m), dtype=torch.float32, device=dev)
-    cmax = torch.empty((B, m), dtype=torch.float32, device=dev)
-    csum = torch.empty((B, m), dtype=torch.float32, device=dev)
-    nb = lib.dot_sinkhorn_col_partials_workspace_bytes(B, n, m)
+    pairs = torch.empty((B, m, 2), dtype=torch.float32, device=dev)
+    nb = lib.dot_sinkhorn_col_pairs_workspace_bytes(B, n, m)
     ws = _lib.workspace(nb, dev)
     for _ in range(int(n_iters)):
         _lib.check(lib.dot_sinkhorn_rows(_lib.ptr(X), float(score_sign), _lib.ptr(la), B, n, m, int(n_total), tau,
                                          _lib.ptr(v), _lib.ptr(u), st), "dot_sinkhorn_rows")
-        _lib.check(lib.dot_sinkhorn_col_partials(_lib.ptr(X), float(score_sign), _lib.ptr(u), B, n, m, tau,
-                                                 _lib.ptr(cmax), _lib.ptr(csum), _lib.ptr(ws), nb, st),
-                   "dot_sinkhorn_col_partials")
-        gmax, gsum = combine_column_partials(cmax, csum, _c_rescale, group=group)
-        _lib.check(lib.dot_sinkhorn_col_finish(_lib.ptr(gmax), _lib.ptr(gsum), _lib.ptr(lb), B, m, _lib.ptr(v), st),
-                   "dot_sinkhorn_col_finish")
+        _lib.check(lib.dot_sinkhorn_col_pairs(_lib.ptr(X), float(score_sign), _lib.ptr(u), B, n, m, tau,
+                                              _lib.ptr(pairs), _lib.ptr(ws), nb, st), "dot_sinkhorn_col_pairs")
+        gathered, parts = gather_column_pairs(pairs, group=group)
+        _lib.check(lib.dot_sinkhorn_col_merge(_lib.ptr(gathered), parts, _lib.ptr(lb), B, m, _lib.ptr(v), st),
+                   "dot_sinkhorn_col_merge")
     out = {"u": u, "v": v, "P": None, "cost": None}
     if want_plan or want_cost:
         P = torch.empty((B, n, m), dtype=torch.float32, device=dev)

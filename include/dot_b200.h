@@ -176,6 +176,20 @@ DOT_API int dot_sinkhorn_col_rescale(const float* col_max, float* col_sum, const
                                      int64_t count, void* stream);
 DOT_API int dot_sinkhorn_col_finish(const float* global_max, const float* global_sum, const float* log_b,
                                     int64_t B, int64_t m, float* pot_v, void* stream);
+/*
+ * One-collective form of the same exchange: each shard writes its column
+ * (max, sum) pairs with dot_sinkhorn_col_pairs (pairs [B,m,2]), the caller
+ * gathers every shard's pairs in shard order into [parts,B,m,2] (e.g. an NCCL
+ * all-gather), and dot_sinkhorn_col_merge merges them in that order and
+ * writes v_j = log_b_j - LSE (log_b NULL: -log(m)).  Every shard computes the
+ * same v bit for bit.  Same combine as above; no counterpart in the reference.
+ */
+DOT_API size_t dot_sinkhorn_col_pairs_workspace_bytes(int64_t B, int64_t n, int64_t m);
+DOT_API int dot_sinkhorn_col_pairs(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n,
+                                   int64_t m, float tau, float* pairs, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+DOT_API int dot_sinkhorn_col_merge(const float* pairs, int parts, const float* log_b, int64_t B, int64_t m,
+                                   float* pot_v, void* stream);
 DOT_API size_t dot_sinkhorn_plan_workspace_bytes(int64_t B, int64_t n, int64_t m);
 DOT_API int dot_sinkhorn_plan(const float* X, float score_sign, const float* pot_u, const float* pot_v, int64_t B,
                               int64_t n, int64_t m, float tau, int out_mode, float* out, float* cost,

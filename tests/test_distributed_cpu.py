@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from dot_b200.distributed import combine_column_partials, shard_range
+from dot_b200.distributed import combine_column_partials, gather_column_pairs, shard_range
 
 
 def test_shard_range_partitions_exactly():
@@ -56,6 +56,50 @@ def _worker(rank, world, port, out):
         out[rank] = float((lse - ref).abs().max())
     finally:
         dist.destroy_process_group()
+
+
+def _merge_cpu(gathered):
+    """Rank-order merge of gathered (max, sum) pairs [world, m, 2] (the
+    arithmetic of dot_sinkhorn_col_merge, in float64 here)."""
+    mm = torch.full(gathered.shape[1:-1], -3.4e38, dtype=torch.float64)
+    ss = torch.zeros_like(mm)
+    for p in gathered.double():
+        mn = torch.maximum(mm, p[..., 0])
+        ss = ss * torch.exp(mm - mn) + p[..., 1] * torch.exp(p[..., 0] - mn)
+        mm = mn
+    return mm + torch.log(ss)
+
+
+def _worker_pairs(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(1)
+        n, m = 41, 13
+        t = torch.randn(n, m, generator=g, dtype=torch.float64) * 30.0
+        lo, hi = shard_range(n, rank, world)
+        local = t[lo:hi]
+        pairs = torch.stack([local.max(0).values, torch.exp(local - local.max(0).values).sum(0)], -1).float()
+        gathered, parts = gather_column_pairs(pairs)
+        assert parts == world and tuple(gathered.shape) == (world, m, 2)
+        lse = _merge_cpu(gathered)
+        out[rank] = (float((lse - torch.logsumexp(t, dim=0)).abs().max()), lse.numpy().tobytes())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_column_pairs_two_ranks_gloo():
+    """One all-gather of (max, sum) pairs, merged in rank order, gives the
+    exact column LSE and the same bits on every rank."""
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker_pairs, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    assert len(out) == world
+    assert max(v[0] for v in out.values()) < 1e-5
+    assert out[0][1] == out[1][1]
 
 
 def test_combine_column_partials_two_ranks_gloo():
