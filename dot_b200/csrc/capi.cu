@@ -169,6 +169,85 @@ int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_a, const
     return sk_stream_fwd(a, workspace, st);
 }
 
+int dot_sinkhorn_fwd_hist(const float* X, float score_sign, const float* log_a, const float* log_b, int64_t B,
+                          int64_t n, int64_t m, float tau, int n_iters, float tol, float* out, float* cost,
+                          float* pot_u, float* pot_v, float* u_hist, float* v_hist, int32_t* status, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (n_iters < 0) return fail(DOT_ERR_INVALID, "n_iters must be >= 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (bad_float(tol) || tol < 0.0f) return fail(DOT_ERR_INVALID, "tol must be finite and >= 0");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !out || !pot_u || !pot_v || !status) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    if (n_iters > 0 && (!u_hist || !v_hist)) return fail(DOT_ERR_INVALID, "null history pointer");
+    const size_t need = sk_stream_fwd_ws(B, n, m, n_iters, tol, cost != nullptr);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    SkFwdArgs a{};
+    a.X = X;
+    a.sign = score_sign;
+    a.tau = tau;
+    a.kinv = score_sign * (1.0f / tau);
+    a.B = B;
+    a.n = n;
+    a.m = m;
+    a.n_iters = n_iters;
+    a.tol = tol;
+    a.out_mode = 0;
+    a.out = out;
+    a.cost = cost;
+    a.u2 = pot_u;
+    a.v2 = pot_v;
+    a.status = status;
+    a.la_def = -logf(float(n));
+    a.lb_def = -logf(float(m));
+    a.la = log_a;
+    a.lb = log_b;
+    a.u_hist = u_hist;
+    a.v_hist = v_hist;
+    return sk_stream_fwd(a, workspace, static_cast<cudaStream_t>(stream));
+}
+
+size_t dot_sinkhorn_bwd_unrolled_workspace_bytes(int64_t B, int64_t n, int64_t m) {
+    if (B <= 0 || n <= 0 || m <= 0) return 0;
+    return sk_unrolled_bwd_ws(B, n, m);
+}
+
+int dot_sinkhorn_bwd_unrolled(const float* X, float score_sign, const float* P, const float* u_hist,
+                              const float* v_hist, const float* grad_P, const float* grad_cost, int64_t B, int64_t n,
+                              int64_t m, float tau, int n_iters, float* grad_X, float* grad_tau, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (n_iters < 0) return fail(DOT_ERR_INVALID, "n_iters must be >= 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !P || !grad_X) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    if (n_iters > 0 && (!u_hist || !v_hist)) return fail(DOT_ERR_INVALID, "null history pointer");
+    const size_t need = sk_unrolled_bwd_ws(B, n, m);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    SkBwdArgs a{};
+    a.X = X;
+    a.sign = score_sign;
+    a.tau = tau;
+    a.P = P;
+    a.gP = grad_P;
+    a.gcost = grad_cost;
+    a.B = B;
+    a.n = n;
+    a.m = m;
+    a.bwd_iters = n_iters;
+    a.gX = grad_X;
+    a.gtau = grad_tau;
+    return sk_unrolled_bwd(a, u_hist, v_hist, workspace, static_cast<cudaStream_t>(stream));
+}
+
 size_t dot_sinkhorn_bwd_workspace_bytes(int64_t B, int64_t n, int64_t m, int bwd_iters) {
     (void)bwd_iters;
     if (B <= 0 || n <= 0 || m <= 0) return 0;

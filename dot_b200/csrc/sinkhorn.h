@@ -27,6 +27,8 @@ struct SkFwdArgs {
     float* u2;         // [B,n] dual potentials u, v (natural log; output)
     float* v2;         // [B,m]
     int32_t* status;   // device int32[4]
+    float* u_hist;     // [n_iters,B,n] u after each iteration, or nullptr
+    float* v_hist;     // [n_iters,B,m]
 };
 
 struct SkBwdArgs {
@@ -73,6 +75,11 @@ size_t sk_stream_fwd_ws(int64_t B, int64_t n, int64_t m, int n_iters, float tol,
 int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 size_t sk_stream_bwd_ws(int64_t B, int64_t n, int64_t m);
 int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
+
+// Unrolled backward through a recorded forward (sinkhorn_unrolled.cu):
+// a.bwd_iters = the number of recorded iterations to differentiate through.
+size_t sk_unrolled_bwd_ws(int64_t B, int64_t n, int64_t m);
+int sk_unrolled_bwd(const SkBwdArgs& a, const float* u_hist, const float* v_hist, void* ws, cudaStream_t st);
 
 // Split half-steps for row-sharded problems (sinkhorn_stream.cu).
 int sk_split_rows(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,

@@ -624,12 +624,24 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
         plan = sk_fused_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
     }
+    const bool hist = a.u_hist != nullptr && a.v_hist != nullptr;
+    auto record = [&](int it) {   // potentials after iteration it (unrolled backward)
+        if (!hist) return;
+        cudaMemcpyAsync(a.u_hist + int64_t(it) * rows, a.u2, sizeof(float) * size_t(rows), cudaMemcpyDeviceToDevice,
+                        st);
+        cudaMemcpyAsync(a.v_hist + int64_t(it) * a.B * a.m, a.v2, sizeof(float) * size_t(a.B * a.m),
+                        cudaMemcpyDeviceToDevice, st);
+    };
     if (fused && a.n_iters > 0) {
         ProfScope ps(DOT_K_SK_FWD_ITER, st, a.n_iters);
-        for (int it = 0; it < a.n_iters; ++it)
-            sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, it == 0, it == a.n_iters - 1, st);
+        for (int it = 0; it < a.n_iters; ++it) {
+            // a copy between two iterations ends the programmatic dependency chain
+            sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, it == 0 || hist, it == a.n_iters - 1, st);
+            record(it);
+        }
     }
     for (int it = 0; it < (fused ? 0 : a.n_iters); ++it) {
+        if (it > 0) record(it - 1);
         ctl.iter = it;
         {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
@@ -647,6 +659,7 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
                                                             chunks, ctl, nullptr);
         }
     }
+    if (!fused && a.n_iters > 0) record(a.n_iters - 1);
     {
         ProfScope ps(DOT_K_SK_FWD_EPI, st);
         sk_status_kernel<<<1, 32, 0, st>>>(w.delta, a.status, a.n_iters, a.tol);
@@ -841,7 +854,6 @@ int sk_split_pair_merge(const float2* pairs, int parts, const float* lb, float l
                         float* v2, cudaStream_t st) {
     // the shards' pairs laid out [parts][B*m] are the chunk partials of one
     // problem: merge them in shard order exactly as the chunk merge does
-    SkCtl ctl{nullptr, nullptr, 0.0f, 0};
     ProfScope ps(DOT_K_SK_FWD_ITER, st);
     sk_shard_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pairs, parts, lb, lb_def, v2, B * m);
     return check_launch("sinkhorn shard merge");

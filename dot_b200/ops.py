@@ -12,8 +12,7 @@ name, argument meaning and return layout, except where noted:
   stats back.
 * ``sinkhorn_dual_forward`` implements ``method=0`` (vanilla) and
   ``schedule=0``; other methods raise ``NotImplementedError``.
-* ``sinkhorn_spectral_preflight`` and ``sinkhorn_with_grads_unrolled`` raise
-  ``NotImplementedError``.
+* ``sinkhorn_spectral_preflight`` raises ``NotImplementedError``.
 
 All ops run on CUDA tensors only and enqueue on the current stream.
 """
@@ -81,6 +80,67 @@ def sinkhorn_forward_raw(X: torch.Tensor, score_sign: float, tau: float, n_iters
     return out, cost, u, v, status
 
 
+def sinkhorn_forward_hist_raw(X: torch.Tensor, score_sign: float, tau: float, n_iters: int,
+                              log_a: Optional[torch.Tensor] = None, log_b: Optional[torch.Tensor] = None,
+                              tol: float = 0.0, want_cost: bool = False):
+    """One call of ``dot_sinkhorn_fwd_hist``: the forward that records the
+    potentials after every iteration for the unrolled backward.
+
+    Returns ``(P, cost_or_None, u, v, status, u_hist [T,B,n], v_hist [T,B,m])``.
+    """
+    _need_cuda(X, "input")
+    if X.dim() != 3:
+        raise ValueError("log_alpha must be 3D [B, n, m]")
+    if not tau > 0.0:
+        raise ValueError("tau must be > 0")
+    if n_iters < 0:
+        raise ValueError("n_iters must be >= 0")
+    X = _f32c(X)
+    B, n, m = X.shape
+    dev = X.device
+    la = _check_marg(log_a, B, n, "log_a", dev)
+    lb = _check_marg(log_b, B, m, "log_b", dev)
+    out = torch.empty((B, n, m), dtype=torch.float32, device=dev)
+    cost = torch.empty((B,), dtype=torch.float32, device=dev) if want_cost else None
+    u = torch.empty((B, n), dtype=torch.float32, device=dev)
+    v = torch.empty((B, m), dtype=torch.float32, device=dev)
+    uh = torch.empty((max(int(n_iters), 1), B, n), dtype=torch.float32, device=dev)
+    vh = torch.empty((max(int(n_iters), 1), B, m), dtype=torch.float32, device=dev)
+    status = torch.zeros((4,), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    nbytes = lib.dot_sinkhorn_fwd_workspace_bytes(B, n, m, int(n_iters), float(tol), 1 if want_cost else 0)
+    ws = _lib.workspace(nbytes, dev)
+    rc = lib.dot_sinkhorn_fwd_hist(_lib.ptr(X), float(score_sign), _lib.ptr(la), _lib.ptr(lb), B, n, m, float(tau),
+                                   int(n_iters), float(tol), _lib.ptr(out), _lib.ptr(cost), _lib.ptr(u), _lib.ptr(v),
+                                   _lib.ptr(uh), _lib.ptr(vh), _lib.ptr(status), _lib.ptr(ws), nbytes,
+                                   _lib.stream_of(X))
+    _lib.check(rc, "dot_sinkhorn_fwd_hist")
+    return out, cost, u, v, status, uh, vh
+
+
+def sinkhorn_backward_unrolled_raw(X: torch.Tensor, score_sign: float, P: torch.Tensor, u_hist: torch.Tensor,
+                                   v_hist: torch.Tensor, grad_P: Optional[torch.Tensor],
+                                   grad_cost: Optional[torch.Tensor], tau: float, n_iters: int,
+                                   want_grad_tau: bool = False):
+    """One call of ``dot_sinkhorn_bwd_unrolled``; returns ``(grad_X, grad_tau_or_None)``."""
+    X = _f32c(X)
+    B, n, m = X.shape
+    dev = X.device
+    gP = None if grad_P is None else _f32c(grad_P)
+    gc = None if grad_cost is None else _f32c(grad_cost.reshape(B))
+    gX = torch.empty((B, n, m), dtype=torch.float32, device=dev)
+    gtau = torch.empty((B,), dtype=torch.float32, device=dev) if want_grad_tau else None
+    lib = _lib.load()
+    nbytes = lib.dot_sinkhorn_bwd_unrolled_workspace_bytes(B, n, m)
+    ws = _lib.workspace(nbytes, dev)
+    rc = lib.dot_sinkhorn_bwd_unrolled(_lib.ptr(X), float(score_sign), _lib.ptr(P.contiguous()),
+                                       _lib.ptr(u_hist), _lib.ptr(v_hist), _lib.ptr(gP), _lib.ptr(gc), B, n, m,
+                                       float(tau), int(n_iters), _lib.ptr(gX), _lib.ptr(gtau), _lib.ptr(ws), nbytes,
+                                       _lib.stream_of(X))
+    _lib.check(rc, "dot_sinkhorn_bwd_unrolled")
+    return gX, gtau
+
+
 def sinkhorn_backward_raw(X: torch.Tensor, score_sign: float, P: torch.Tensor, u: Optional[torch.Tensor],
                           v: Optional[torch.Tensor], grad_P: Optional[torch.Tensor],
                           grad_cost: Optional[torch.Tensor], tau: float, bwd_iters: int,
@@ -144,8 +204,12 @@ def sinkhorn_with_grads_implicit(log_alpha, grad_P, tau: float, n_iters: int, ba
     return [P, g, gt]
 
 
-def sinkhorn_with_grads_unrolled(*args, **kwargs):
-    raise NotImplementedError("dot_b200: the unrolled backward (backward_mode='unrolled') is not implemented")
+def sinkhorn_with_grads_unrolled(log_alpha, grad_P, tau: float, n_iters: int, log_a=None, log_b=None):
+    """``[P, grad_log_alpha, grad_tau]`` through ``n_iters`` unrolled iterations (``registry.cpp:52``)."""
+    P, _, _, _, _, uh, vh = sinkhorn_forward_hist_raw(log_alpha, 1.0, float(tau), int(n_iters), log_a, log_b)
+    g, gt = sinkhorn_backward_unrolled_raw(log_alpha, 1.0, P, uh, vh, grad_P, None, float(tau), int(n_iters),
+                                           want_grad_tau=True)
+    return [P, g, gt]
 
 
 def sinkhorn_spectral_preflight(*args, **kwargs):

@@ -18,10 +18,11 @@ Differences in mechanism (same results):
 * the ``tol`` early stop is decided on the device (no per-iteration host
   sync); ``n_iters_used`` is read back once, and only when ``tol > 0``.
 
-Scope: the vanilla method with the implicit backward.  The reference's own
-CUDA dispatch turns some other method requests into vanilla (:1371-1391);
-those are honoured.  Other methods, schedules, ``n_iters='auto'`` and the
-unrolled backward raise ``NotImplementedError``.  Inputs must be CUDA
+Scope: the vanilla method with the implicit backward (default) or the
+unrolled backward (``backward_mode='unrolled'``: differentiation through the
+recorded iterations).  The reference's own CUDA dispatch turns some other
+method requests into vanilla (:1371-1391); those are honoured.  Other
+methods, schedules and ``n_iters='auto'`` raise ``NotImplementedError``.  Inputs must be CUDA
 tensors: there is no CPU implementation.
 """
 
@@ -98,6 +99,52 @@ class _SinkhornFn(torch.autograd.Function):
             dt, dev = ctx.reg_meta
             greg = gtau.sum().to(device=dev, dtype=dt)
         return (gX if need_x else None), greg, None, None, None, None, None, None, None
+
+
+class _SinkhornUnrolledFn(torch.autograd.Function):
+    """Forward: plan (+ cost) with the potentials of every iteration recorded;
+    backward: differentiation through the recorded iterations
+    (``_SinkhornCudaDualUnrolledFunction``, ``dot/sinkhorn.py:243-311``, whose
+    backward reruns the forward; here the recorded potentials are reused)."""
+
+    @staticmethod
+    def forward(ctx, X, reg, sign: float, n_iters: int, log_a, log_b, tol: float, want_cost: bool):
+        tau = _tau_value(reg)
+        P, cost, _u, _v, status, uh, vh = ops.sinkhorn_forward_hist_raw(X, sign, tau, n_iters, log_a, log_b,
+                                                                         tol=tol, want_cost=want_cost)
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(X, P, uh, vh, status)
+        ctx.tau = tau
+        ctx.sign = sign
+        ctx.n_iters = n_iters
+        ctx.tol = tol
+        ctx.reg_is_tensor = torch.is_tensor(reg)
+        ctx.reg_meta = (reg.dtype, reg.device) if torch.is_tensor(reg) else None
+        ctx.mark_non_differentiable(status)
+        if cost is None:
+            cost = P.new_zeros(0)
+            ctx.mark_non_differentiable(cost)
+        return P, cost, status
+
+    @staticmethod
+    def backward(ctx, grad_P, grad_cost, _grad_status):
+        X, P, uh, vh, status = ctx.saved_tensors
+        if grad_cost is not None and grad_cost.numel() == 0:
+            grad_cost = None
+        need_x = ctx.needs_input_grad[0]
+        need_tau = ctx.reg_is_tensor and ctx.needs_input_grad[1]
+        if (grad_P is None and grad_cost is None) or not (need_x or need_tau):
+            return (None,) * 8
+        # with tol > 0 only the iterations actually run are differentiated
+        # (the reference reruns the forward with n_iters_used, dot/sinkhorn.py:301)
+        used = int(status[0].item()) if ctx.tol > 0 else ctx.n_iters
+        gX, gtau = ops.sinkhorn_backward_unrolled_raw(X, ctx.sign, P, uh, vh, grad_P, grad_cost, ctx.tau, used,
+                                                      want_grad_tau=need_tau)
+        greg = None
+        if need_tau:
+            dt, dev = ctx.reg_meta
+            greg = gtau.sum().to(device=dev, dtype=dt)
+        return (gX if need_x else None), greg, None, None, None, None, None, None
 
 
 def _prepare_marginal(marginal, batch: int, size: int, name: str, device, dtype):
@@ -213,14 +260,15 @@ def sinkhorn(
     _effective_method(method, tau, omega, schedule, reg_start, lr, beta1, beta2, eps_adam, bias_correction, n, m)
     if backward_mode not in ("implicit", "unrolled"):
         raise ValueError("backward_mode must be 'unrolled' or 'implicit'")
-    if backward_mode == "unrolled":
-        raise NotImplementedError("dot_b200: backward_mode='unrolled' is not implemented")
     run_tol = float(tol) if dual else 0.0
     if run_tol < 0:
         raise ValueError("tol must be >= 0")
 
-    P, cost, status = _SinkhornFn.apply(C.to(torch.float32).contiguous() if C.dtype != torch.float32 else C.contiguous(),
-                                        reg, -1.0, n_it, int(backward_iters), log_a, log_b, run_tol, True)
+    Cf = C.to(torch.float32).contiguous() if C.dtype != torch.float32 else C.contiguous()
+    if backward_mode == "unrolled":
+        P, cost, status = _SinkhornUnrolledFn.apply(Cf, reg, -1.0, n_it, log_a, log_b, run_tol, True)
+    else:
+        P, cost, status = _SinkhornFn.apply(Cf, reg, -1.0, n_it, int(backward_iters), log_a, log_b, run_tol, True)
     if dual and run_tol > 0:
         st = status.cpu()
         n_iters_used = int(st[0])
@@ -274,10 +322,11 @@ def sinkhorn_from_scores(
         out = ops.sinkhorn_forward_raw(L.detach(), 1.0, _tau_value(tau), n_it, log_a, log_b, tol=run_tol,
                                        return_log=True)[0]
     else:
-        if backward_mode == "unrolled":
-            raise NotImplementedError("dot_b200: backward_mode='unrolled' is not implemented")
         X = L.to(torch.float32).contiguous() if L.dtype != torch.float32 else L.contiguous()
-        out, _, _ = _SinkhornFn.apply(X, tau, 1.0, n_it, int(backward_iters), log_a, log_b, run_tol, False)
+        if backward_mode == "unrolled":
+            out, _, _ = _SinkhornUnrolledFn.apply(X, tau, 1.0, n_it, log_a, log_b, run_tol, False)
+        else:
+            out, _, _ = _SinkhornFn.apply(X, tau, 1.0, n_it, int(backward_iters), log_a, log_b, run_tol, False)
     return out.squeeze(0) if unbatched else out
 
 

@@ -145,6 +145,34 @@ DOT_API int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P,
                      int bwd_iters, float* grad_X, float* grad_tau, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/*
+ * Forward for the unrolled backward: dot_sinkhorn_fwd (plan, out_mode 0)
+ * that also records the potentials after every iteration, u_hist
+ * [n_iters,B,n] and v_hist [n_iters,B,m].  Workspace as
+ * dot_sinkhorn_fwd_workspace_bytes.  With tol > 0, iterations after the stop
+ * repeat the final potentials; status[0] gives the count to differentiate.
+ * Replaces: sinkhorn_dual_forward_with_intermediates_cuda, reached through
+ * sinkhorn_with_grads_unrolled (src/sinkhorn/registry.cpp:52;
+ * torch_cuda.cpp:717-801, kernels.cu:1445-1507).
+ */
+DOT_API int dot_sinkhorn_fwd_hist(const float* X, float score_sign, const float* log_a, const float* log_b,
+                                  int64_t B, int64_t n, int64_t m, float tau, int n_iters, float tol, float* out,
+                                  float* cost, float* pot_u, float* pot_v, float* u_hist, float* v_hist,
+                                  int32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Unrolled backward: differentiates through the first n_iters recorded
+ * iterations.  Same upstream gradients and outputs as dot_sinkhorn_bwd
+ * (grad_P and/or grad_cost; grad_X, grad_tau).
+ * Replaces: the backward half of sinkhorn_with_grads_unrolled
+ * (src/sinkhorn/registry.cpp:52; torch_cuda.cpp:785; kernels.cu:844-961,1622-1680).
+ */
+DOT_API size_t dot_sinkhorn_bwd_unrolled_workspace_bytes(int64_t B, int64_t n, int64_t m);
+DOT_API int dot_sinkhorn_bwd_unrolled(const float* X, float score_sign, const float* P, const float* u_hist,
+                                      const float* v_hist, const float* grad_P, const float* grad_cost, int64_t B,
+                                      int64_t n, int64_t m, float tau, int n_iters, float* grad_X, float* grad_tau,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Sinkhorn half-steps for problems whose rows are sharded across GPUs       */
 /* ------------------------------------------------------------------------ */

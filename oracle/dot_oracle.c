@@ -90,6 +90,85 @@ void orc_sinkhorn_forward(const float *log_alpha, float *out,
     }
 }
 
+/* Primal Sinkhorn storing every half-step for the unrolled backward:
+ * log_X [B, T+1, n, m] (X_0 = log_alpha / tau, X_{t+1} after the column
+ * normalisation of iteration t) and log_Y [B, T, n, m] (after the row
+ * normalisation of iteration t); P = exp(X_T).
+ * src/sinkhorn/kernels_cpu.cpp:108-165 */
+void orc_sinkhorn_forward_hist(const float *log_alpha, float *P, float *log_X,
+                               float *log_Y, const float *log_a,
+                               const float *log_b, int64_t B, int64_t n,
+                               int64_t m, float tau, int n_iters) {
+    if (!(tau > 0.0f)) return;
+    const int64_t nm = n * m;
+    const float def_a = -logf((float)n);
+    const float def_b = -logf((float)m);
+    for (int64_t b = 0; b < B; ++b) {
+        float *Xb = log_X + b * (int64_t)(n_iters + 1) * nm;
+        float *Yb = log_Y + b * (int64_t)n_iters * nm;
+        for (int64_t e = 0; e < nm; ++e) Xb[e] = log_alpha[b * nm + e] / tau;
+        for (int t = 0; t < n_iters; ++t) {
+            float *Y = Yb + t * nm;
+            float *X1 = Xb + (t + 1) * nm;
+            memcpy(Y, Xb + t * nm, sizeof(float) * (size_t)nm);
+            for (int64_t i = 0; i < n; ++i) {
+                float *row = Y + i * m;
+                float shift = orc_lse(row, m, 1) - (log_a ? log_a[b * n + i] : def_a);
+                for (int64_t j = 0; j < m; ++j) row[j] -= shift;
+            }
+            memcpy(X1, Y, sizeof(float) * (size_t)nm);
+            for (int64_t j = 0; j < m; ++j) {
+                float shift = orc_lse(X1 + j, n, m) - (log_b ? log_b[b * m + j] : def_b);
+                for (int64_t i = 0; i < n; ++i) X1[i * m + j] -= shift;
+            }
+        }
+        const float *XT = Xb + (int64_t)n_iters * nm;
+        for (int64_t e = 0; e < nm; ++e) P[b * nm + e] = orc_exp88(XT[e]);
+    }
+}
+
+/* Unrolled backward through the stored half-steps: Gamma = grad_P * P; for
+ * t = T-1 .. 0, column step Gamma_Y = Gamma - exp(X_{t+1}) * colsum(Gamma),
+ * row step Gamma = Gamma_Y - exp(Y_t) * rowsum(Gamma_Y); then
+ * grad = Gamma / tau, grad_tau = -sum(Gamma * log_alpha) / tau^2.
+ * src/sinkhorn/kernels_cpu.cpp:169-245 */
+void orc_sinkhorn_backward_unrolled(const float *log_alpha, const float *P,
+                                    const float *grad_P, const float *log_X,
+                                    const float *log_Y, float *grad,
+                                    float *grad_tau, int64_t B, int64_t n,
+                                    int64_t m, float tau, int n_iters) {
+    const int64_t nm = n * m;
+    float *Gm = (float *)malloc(sizeof(float) * (size_t)nm);
+    float *GY = (float *)malloc(sizeof(float) * (size_t)nm);
+    for (int64_t b = 0; b < B; ++b) {
+        const float *Xb = log_X + b * (int64_t)(n_iters + 1) * nm;
+        const float *Yb = log_Y + b * (int64_t)n_iters * nm;
+        for (int64_t e = 0; e < nm; ++e) Gm[e] = grad_P[b * nm + e] * P[b * nm + e];
+        for (int t = n_iters - 1; t >= 0; --t) {
+            const float *X1 = Xb + (int64_t)(t + 1) * nm;
+            const float *Y = Yb + (int64_t)t * nm;
+            for (int64_t k = 0; k < m; ++k) {
+                float s = 0.0f;
+                for (int64_t i = 0; i < n; ++i) s += Gm[i * m + k];
+                for (int64_t i = 0; i < n; ++i) GY[i * m + k] = Gm[i * m + k] - orc_exp88(X1[i * m + k]) * s;
+            }
+            for (int64_t i = 0; i < n; ++i) {
+                float ti = 0.0f;
+                for (int64_t k = 0; k < m; ++k) ti += GY[i * m + k];
+                for (int64_t k = 0; k < m; ++k) Gm[i * m + k] = GY[i * m + k] - orc_exp88(Y[i * m + k]) * ti;
+            }
+        }
+        float acc = 0.0f;
+        for (int64_t e = 0; e < nm; ++e) {
+            grad[b * nm + e] = Gm[e] / tau;
+            acc += Gm[e] * log_alpha[b * nm + e];
+        }
+        grad_tau[b] = -acc / (tau * tau);
+    }
+    free(Gm);
+    free(GY);
+}
+
 /* Dual-potential Sinkhorn as the reference's CUDA path runs it:
  * u_i = log_a_i - LSE_j(K_ij + v_j), then v_j = log_b_j - LSE_i(K_ij + u_i),
  * K = log_alpha / tau, u = v = 0 at start, log floor max(sum, 1e-12);

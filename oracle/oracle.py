@@ -73,6 +73,12 @@ def _lib(kind: str) -> ctypes.CDLL:
         f = getattr(lib, p + "bidir_backward")
         f.argtypes = [_fp, _fp, _fp, _fp, _fp, _fp, _fp, _ip, i64, i64, i64, ctypes.c_float]
         f.restype = None
+        f = getattr(lib, p + "sinkhorn_forward_hist")
+        f.argtypes = [_fp, _fp, _fp, _fp, _fp, _fp, i64, i64, i64, ctypes.c_float, ctypes.c_int]
+        f.restype = None
+        f = getattr(lib, p + "sinkhorn_backward_unrolled")
+        f.argtypes = [_fp, _fp, _fp, _fp, _fp, _fp, _fp, i64, i64, i64, ctypes.c_float, ctypes.c_int]
+        f.restype = None
         if kind == "restated":
             f = lib.orc_sinkhorn_dual
             f.argtypes = [_fp, _fp, _fp, i64, i64, i64, ctypes.c_float, ctypes.c_int,
@@ -127,6 +133,37 @@ def sinkhorn_backward_implicit(log_alpha, P, grad_P, tau: float, max_iters: int,
     gtau = np.empty((B,), np.float32)
     fn = getattr(_lib(kind), _PREFIX[kind] + "sinkhorn_backward_implicit")
     fn(_ptr(la), _ptr(p), _ptr(g), _ptr(grad), _ptr(gtau), B, n, m, float(tau), int(max_iters), float(tol))
+    return grad, gtau
+
+
+def sinkhorn_forward_hist(log_alpha, tau: float, n_iters: int, log_a=None, log_b=None,
+                          kind: str = "restated"):
+    """Primal Sinkhorn keeping every half-step: returns ``(P, log_X [B,T+1,n,m],
+    log_Y [B,T,n,m])``.  Reference: ``src/sinkhorn/kernels_cpu.cpp:108-165``."""
+    la = _f32(log_alpha)
+    B, n, m = la.shape
+    T = int(n_iters)
+    P = np.empty_like(la)
+    X = np.empty((B, T + 1, n, m), np.float32)
+    Y = np.empty((B, max(T, 1), n, m), np.float32)
+    la_a = None if log_a is None else _f32(log_a)
+    la_b = None if log_b is None else _f32(log_b)
+    fn = getattr(_lib(kind), _PREFIX[kind] + "sinkhorn_forward_hist")
+    fn(_ptr(la), _ptr(P), _ptr(X), _ptr(Y), _ptr(la_a), _ptr(la_b), B, n, m, float(tau), T)
+    return P, X, Y
+
+
+def sinkhorn_backward_unrolled(log_alpha, P, grad_P, log_X, log_Y, tau: float, n_iters: int,
+                               kind: str = "restated"):
+    """Unrolled backward: returns ``(grad_log_alpha [B,n,m], grad_tau [B])``.
+    Reference: ``src/sinkhorn/kernels_cpu.cpp:169-245``."""
+    la, p, g = _f32(log_alpha), _f32(P), _f32(grad_P)
+    X, Y = _f32(log_X), _f32(log_Y)
+    B, n, m = la.shape
+    grad = np.empty_like(la)
+    gtau = np.empty((B,), np.float32)
+    fn = getattr(_lib(kind), _PREFIX[kind] + "sinkhorn_backward_unrolled")
+    fn(_ptr(la), _ptr(p), _ptr(g), _ptr(X), _ptr(Y), _ptr(grad), _ptr(gtau), B, n, m, float(tau), int(n_iters))
     return grad, gtau
 
 
@@ -198,7 +235,7 @@ def _log_marginal(x, B: int, size: int):
 
 def sinkhorn_api(C, reg: float, n_iters: int, a=None, b=None, backward_iters: int | None = None,
                  g_cost=None, grad_P=None, bwd_tol: float = 0.0, kind: str = "restated",
-                 with_grad: bool = True):
+                 with_grad: bool = True, backward_mode: str = "implicit"):
     """``dot.sinkhorn(C, reg, n_iters, a=a, b=b)`` on the reference's CPU path.
 
     Returns a dict with ``P`` [B,n,m], ``cost`` [B] and, when ``with_grad``,
@@ -212,7 +249,9 @@ def sinkhorn_api(C, reg: float, n_iters: int, a=None, b=None, backward_iters: in
     (:1703) whose autograd gives ``grad_P += g*C`` and ``dC += g*P``; the
     negation gives ``dC -= grad_log_alpha``.  ``bwd_tol`` is the adjoint
     early-exit threshold: the reference CPU op uses 1e-6, its CUDA op runs all
-    ``backward_iters`` sweeps (``bwd_tol=0``).
+    ``backward_iters`` sweeps (``bwd_tol=0``).  ``backward_mode='unrolled'``
+    follows ``_SinkhornUnrolledFunction`` (:45-96): the backward differentiates
+    through the ``n_iters`` stored iterations (``torch_cpu.cpp:188-259``).
     """
     C = _f32(C)
     B, n, m = C.shape
@@ -228,8 +267,12 @@ def sinkhorn_api(C, reg: float, n_iters: int, a=None, b=None, backward_iters: in
     G = (g[:, None, None] * C).astype(np.float32)
     if grad_P is not None:
         G = (G + _f32(grad_P)).astype(np.float32)
-    bi = n_iters if backward_iters is None else backward_iters
-    gla, gtau = sinkhorn_backward_implicit(log_alpha, P, G, reg, bi, tol=bwd_tol, kind=kind)
+    if backward_mode == "unrolled":
+        _, X, Y = sinkhorn_forward_hist(log_alpha, reg, n_iters, la, lb, kind=kind)
+        gla, gtau = sinkhorn_backward_unrolled(log_alpha, P, G, X, Y, reg, n_iters, kind=kind)
+    else:
+        bi = n_iters if backward_iters is None else backward_iters
+        gla, gtau = sinkhorn_backward_implicit(log_alpha, P, G, reg, bi, tol=bwd_tol, kind=kind)
     dC = (g[:, None, None] * P - gla).astype(np.float32)
     out.update(dC=dC, dreg=np.float32(gtau.sum(dtype=np.float64)), grad_log_alpha=gla, grad_tau=gtau)
     return out

@@ -33,6 +33,22 @@ void ref_sinkhorn_backward_implicit(const float* log_alpha, const float* P,
                                                   max_iters, tol);
 }
 
+// src/sinkhorn/kernels_cpu.h: sinkhorn_forward_with_intermediates_cpu
+void ref_sinkhorn_forward_hist(const float* log_alpha, float* P, float* log_X, float* log_Y,
+                               const float* log_a, const float* log_b, int B, int n, int m,
+                               float tau, int n_iters) {
+    dot::sinkhorn::sinkhorn_forward_with_intermediates_cpu(log_alpha, P, log_X, log_Y, log_a, log_b,
+                                                           B, n, m, tau, n_iters);
+}
+
+// src/sinkhorn/kernels_cpu.h: sinkhorn_backward_unrolled_cpu
+void ref_sinkhorn_backward_unrolled(const float* log_alpha, const float* P, const float* grad_P,
+                                    const float* log_X, const float* log_Y, float* grad,
+                                    float* grad_tau, int B, int n, int m, float tau, int n_iters) {
+    dot::sinkhorn::sinkhorn_backward_unrolled_cpu(log_alpha, P, grad_P, log_X, log_Y, nullptr, nullptr,
+                                                  grad, grad_tau, B, n, m, tau, n_iters);
+}
+
 // src/bidirectional_softmax/kernels_cpu.h: bidirectional_softmax_forward_cpu
 void ref_bidir_forward(const float* sim, float* out, float* row_sm, float* col_sm,
                        const int32_t* lengths, int B, int L1, int L2, float T) {

@@ -78,12 +78,14 @@ def dirichlet(B, n, seed):
     return torch.distributions.Dirichlet(torch.ones(n)).sample((B,)).float()
 
 def run_sinkhorn(name, C, reg, n_iters, a=None, b=None, reg_tensor=False, plan_weight=None,
-                 cost_weight=None, backward_iters=None):
+                 cost_weight=None, backward_iters=None, backward_mode=None):
     Cg = C.clone().requires_grad_(True)
     r = torch.tensor(float(reg), requires_grad=True) if reg_tensor else float(reg)
     kw = {}
     if backward_iters is not None:
         kw["backward_iters"] = backward_iters
+    if backward_mode is not None:
+        kw["backward_mode"] = backward_mode
     res = dot.sinkhorn(Cg, reg=r, n_iters=n_iters, a=a, b=b, **kw)
     cw = torch.ones_like(res.cost) if cost_weight is None else cost_weight
     loss = (res.cost * cw).sum()
@@ -96,6 +98,8 @@ def run_sinkhorn(name, C, reg, n_iters, a=None, b=None, reg_tensor=False, plan_w
                n_iters_used=np.int64(res.n_iters_used), converged=np.bool_(res.converged))
     if backward_iters is not None:
         out["backward_iters"] = np.int64(backward_iters)
+    if backward_mode is not None:
+        out["backward_mode"] = np.array(backward_mode)
     if a is not None: out["a"] = a.numpy()
     if b is not None: out["b"] = b.numpy()
     if plan_weight is not None: out["plan_weight"] = plan_weight.numpy()
@@ -134,6 +138,17 @@ run_sinkhorn("bwditers", torch.rand(2, 24, 24, generator=g), 0.2, 30, backward_i
 g = gen(10)
 run_sinkhorn("marg1d", torch.rand(3, 16, 8, generator=g), 0.4, 25,
              torch.softmax(torch.randn(16, generator=g), -1), torch.softmax(torch.randn(8, generator=g), -1))
+
+# unrolled backward (backward_mode='unrolled'): plan and cost in the loss,
+# differentiable reg; and non-uniform marginals
+g = gen(12)
+run_sinkhorn("unrolled", torch.rand(2, 20, 24, generator=g), 0.2, 30, reg_tensor=True,
+             plan_weight=torch.randn(2, 20, 24, generator=g), cost_weight=torch.tensor([1.0, -0.5]),
+             backward_mode="unrolled")
+g = gen(13)
+run_sinkhorn("unrolled_marg", torch.rand(2, 16, 12, generator=g), 0.3, 25,
+             torch.softmax(torch.randn(2, 16, generator=g), -1), torch.softmax(torch.randn(2, 12, generator=g), -1),
+             backward_mode="unrolled")
 
 # sinkhorn_from_scores (plan and log-plan)
 g = gen(11)

@@ -82,5 +82,11 @@ def test_modules_keep_their_settings():
 def test_out_of_scope_entry_points_raise():
     with pytest.raises(NotImplementedError):
         dot.spectral_preflight(torch.rand(1, 4, 4), 0.1)
-    with pytest.raises(NotImplementedError):
-        dot._ops.sinkhorn_with_grads_unrolled(None, None, 1.0, 5)
+
+
+def test_unrolled_op_rejects_cpu_tensors():
+    # implemented on the GPU only: no CPU fallback
+    with pytest.raises(RuntimeError, match="CUDA"):
+        dot._ops.sinkhorn_with_grads_unrolled(torch.rand(1, 4, 4), torch.rand(1, 4, 4), 1.0, 5)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        dot.sinkhorn(torch.rand(1, 4, 4), reg=0.5, n_iters=5, backward_mode="unrolled")

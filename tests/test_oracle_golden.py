@@ -20,7 +20,8 @@ def test_oracle_matches_reference_golden_sinkhorn(path):
     d = U.load(path)
     r = O.sinkhorn_api(d["C"], float(d["reg"]), int(d["n_iters"]), d.get("a"), d.get("b"),
                        backward_iters=int(d["backward_iters"]) if "backward_iters" in d else None,
-                       g_cost=d["cost_weight"], grad_P=d.get("plan_weight"), bwd_tol=1e-6)
+                       g_cost=d["cost_weight"], grad_P=d.get("plan_weight"), bwd_tol=1e-6,
+                       backward_mode=str(d["backward_mode"]) if "backward_mode" in d else "implicit")
     # the reference's CPU path, restated: plan and gradients bit-identical
     assert np.array_equal(r["P"], d["P"])
     assert np.array_equal(r["dC"], d["dC"])

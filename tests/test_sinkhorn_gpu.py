@@ -20,12 +20,14 @@ DEV = "cuda"
 
 
 def run_api(C, reg, n_iters, a=None, b=None, backward_iters=None, cost_weight=None, plan_weight=None,
-            reg_tensor=False, tol=0.0):
+            reg_tensor=False, tol=0.0, backward_mode=None):
     Cg = torch.as_tensor(C).to(DEV).clone().requires_grad_(True)
     r = torch.tensor(float(reg), device=DEV, requires_grad=True) if reg_tensor else float(reg)
     kw = {}
     if backward_iters is not None:
         kw["backward_iters"] = backward_iters
+    if backward_mode is not None:
+        kw["backward_mode"] = backward_mode
     res = dot.sinkhorn(Cg, reg=r, n_iters=n_iters, a=None if a is None else torch.as_tensor(a).to(DEV),
                        b=None if b is None else torch.as_tensor(b).to(DEV), tol=tol, **kw)
     cw = torch.ones_like(res.cost) if cost_weight is None else torch.as_tensor(cost_weight).to(DEV)
@@ -49,7 +51,8 @@ def test_golden_sinkhorn(path):
     d = U.load(path)
     r = run_api(d["C"], float(d["reg"]), int(d["n_iters"]), d.get("a"), d.get("b"),
                 backward_iters=int(d["backward_iters"]) if "backward_iters" in d else None,
-                cost_weight=d["cost_weight"], plan_weight=d.get("plan_weight"), reg_tensor="dreg" in d)
+                cost_weight=d["cost_weight"], plan_weight=d.get("plan_weight"), reg_tensor="dreg" in d,
+                backward_mode=str(d["backward_mode"]) if "backward_mode" in d else None)
     U.assert_normwise(r["P"], d["P"], U.PLAN_RTOL, "plan")
     U.assert_rel(r["cost"], d["cost"], U.COST_RTOL, "cost", atol=1e-9)
     U.assert_normwise(r["dC"], d["dC"], U.GRAD_RTOL, "dC")
@@ -390,3 +393,78 @@ def test_cfg4_and_cfg1_full_size_against_oracle_sample():
     r1 = run_api(C1, 1.0, 100)
     U.assert_normwise(r1["P"], ref["P"], U.PLAN_RTOL, "cfg1 plan")
     U.assert_normwise(r1["dC"], ref["dC"], U.GRAD_RTOL, "cfg1 dC")
+
+
+# ---------------------------------------------------------------------------
+# unrolled backward (backward_mode='unrolled')
+# ---------------------------------------------------------------------------
+
+UNROLLED_SHAPES = [
+    # (B, n, m, reg, T, marginals)
+    (2, 17, 33, 0.2, 12, True),
+    (2, 64, 64, 1.0, 30, False),      # resident-sized shape: the recording forward streams
+    (1, 600, 40, 0.3, 8, False),      # tall: column sums over several row chunks
+    (1, 20, 1100, 0.5, 5, False),     # wide: two-pass forward
+    (3, 5, 7, 0.7, 0, False),         # no iterations: Gamma = G * P
+]
+
+
+@pytest.mark.parametrize("B,n,m,reg,T,marg", UNROLLED_SHAPES, ids=lambda v: str(v))
+def test_unrolled_backward_matches_oracle(B, n, m, reg, T, marg):
+    g = U.gen(7000 + n * 3 + m)
+    C = torch.rand(B, n, m, generator=g)
+    a = b = None
+    if marg:
+        a = U.dirichlet(B, n, 17) + 1e-3
+        a = a / a.sum(-1, keepdim=True)
+        b = U.dirichlet(B, m, 18) + 1e-3
+        b = b / b.sum(-1, keepdim=True)
+    W = torch.randn(B, n, m, generator=g)
+    cw = torch.randn(B, generator=g)
+    ref = O.sinkhorn_api(C.numpy(), reg, T, None if a is None else a.numpy(), None if b is None else b.numpy(),
+                         g_cost=cw.numpy(), grad_P=W.numpy(), backward_mode="unrolled")
+    r = run_api(C, reg, T, a, b, cost_weight=cw, plan_weight=W, reg_tensor=True, backward_mode="unrolled")
+    U.assert_normwise(r["P"], ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_rel(r["cost"], ref["cost"], U.COST_RTOL, "cost", atol=1e-9)
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
+    assert r["dreg"] == pytest.approx(float(ref["dreg"]), rel=U.GRAD_RTOL, abs=1e-6)
+
+
+def test_unrolled_with_tol_differentiates_the_iterations_run():
+    C = torch.rand(2, 40, 48, generator=U.gen(71))
+    r = run_api(C, 0.5, 200, tol=1e-4, backward_mode="unrolled")
+    used = r["res"].n_iters_used
+    assert 0 < used < 200
+    ref = O.sinkhorn_api(C.numpy(), 0.5, used, backward_mode="unrolled")
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
+
+
+def test_unrolled_from_scores_and_reference_op():
+    g = U.gen(72)
+    la = torch.randn(2, 10, 14, generator=g)
+    w = torch.randn(2, 10, 14, generator=g)
+    lag = la.to(DEV).requires_grad_(True)
+    P = dot.sinkhorn_from_scores(lag, tau=0.5, n_iters=30, backward_mode="unrolled", tol=0)
+    (P * w.to(DEV)).sum().backward()
+    Pr, X, Y = O.sinkhorn_forward_hist(la.numpy(), 0.5, 30)
+    gref, gtref = O.sinkhorn_backward_unrolled(la.numpy(), Pr, w.numpy(), X, Y, 0.5, 30)
+    U.assert_normwise(P.detach(), Pr, U.PLAN_RTOL, "plan")
+    U.assert_normwise(lag.grad, gref, U.GRAD_RTOL, "dlog_alpha")
+    P2, g2, gt2 = ops.sinkhorn_with_grads_unrolled(la.to(DEV), w.to(DEV), 0.5, 30)
+    U.assert_normwise(g2, gref, U.GRAD_RTOL, "op grad")
+    assert np.allclose(U.to_np(gt2), gtref, rtol=U.GRAD_RTOL, atol=1e-6)
+
+
+def test_unrolled_dual_and_full_agree():
+    """The reference's own check (tests/test_sinkhorn.py:806-823): dual and
+    full-matrix formulations agree for the unrolled backward."""
+    torch.manual_seed(0)
+    c1 = torch.rand(1, 48, 64, device=DEV, requires_grad=True)
+    c2 = c1.detach().clone().requires_grad_(True)
+    d = dot.sinkhorn(c1, reg=0.1, n_iters=30, tol=0, dual=True, backward_mode="unrolled")
+    f = dot.sinkhorn(c2, reg=0.1, n_iters=30, tol=0, dual=False, backward_mode="unrolled")
+    d.cost.sum().backward()
+    f.cost.sum().backward()
+    assert d.n_iters_used == 30 and f.n_iters_used == 30
+    assert torch.allclose(d.transport_plan, f.transport_plan, atol=1e-5)
+    assert torch.allclose(c1.grad, c2.grad, atol=1e-4)
