@@ -306,8 +306,8 @@ def test_marginals_without_grad_and_errors():
         dot.sinkhorn(cost, reg=0.0)
     with pytest.raises(ValueError):
         dot.sinkhorn(cost, a=torch.full((2, 5), 0.3, device=DEV))
-    with pytest.raises(NotImplementedError):
-        dot.sinkhorn(cost, backward_mode="unrolled")
+    with pytest.raises(ValueError):
+        dot.sinkhorn(cost, backward_mode="exact")
 
 
 def test_bf16_and_fp64_inputs_follow_reference_casts():
