@@ -355,7 +355,8 @@ def run_ours(args, cfg: dict) -> None:
 
     if rank == 0:
         peaks = measured_peaks()
-        roof = roofline(cfg, prof, peaks, args.steps)
+        roof = roofline(cfg, prof, peaks, args.steps,
+                        elems_local=(C_dev.numel() if cfg["kind"] != "bidir" else None))
         line = {
             "metric": METRIC if cfg["kind"] != "bidir" else "bidirectional softmax fwd+bwd elements/s",
             "value": value,
@@ -394,7 +395,7 @@ def run_ours(args, cfg: dict) -> None:
         dist.destroy_process_group()
 
 
-def roofline(cfg: dict, prof: dict, peaks: dict, steps: int) -> dict:
+def roofline(cfg: dict, prof: dict, peaks: dict, steps: int, elems_local: int | None = None) -> dict:
     """Dominant kernel class: algorithmic bytes / measured kernel time.
 
     Sinkhorn: every sweep kernel (fused forward iteration, fused adjoint
@@ -408,6 +409,8 @@ def roofline(cfg: dict, prof: dict, peaks: dict, steps: int) -> dict:
     """
     B, n, m = cfg["B"], cfg["n"], cfg["m"]
     elems = B * n * m
+    if elems_local is None:
+        elems_local = elems
     cands = [(v["ms"], k, v) for k, v in prof.items() if v["launches"] and v["ms"] > 0]
     if not cands:
         return {"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": None,
@@ -416,12 +419,13 @@ def roofline(cfg: dict, prof: dict, peaks: dict, steps: int) -> dict:
     ms, k, v = cands[0]
     avg_ms = v["ms"] / v["launches"]
     if k in ("sk_fwd_iter", "sk_bwd_iter"):
-        # two-pass path (m > 1024 or m % 4 != 0): row + column launch (+ a merge
-        # launch, which moves no matrix bytes, when n spans several chunks)
-        fused = m <= 1024 and m % 4 == 0
-        per_iter = 1 if fused else (3 if n > 1024 else 2)
-        sweeps = v["launches"] * (1 if fused else 2) // per_iter
-        total_bytes = 4 * elems * sweeps
+        # matrix sweeps per iteration: one for the fused (m <= 1024) and the
+        # wide-row cluster (8192 <= m <= 65536) kernels, two (row, then
+        # column) for the general two-pass path; the merge launches of the
+        # two-pass and row-shard paths move no matrix bytes
+        single = (m <= 1024 and m % 4 == 0) or (8192 <= m <= 65536 and m % 32 == 0)
+        sweeps = cfg["iters"] * steps * (1 if single else 2)
+        total_bytes = 4 * elems_local * sweeps
         bytes_per_launch = total_bytes / v["launches"]
     elif k == "sk_resident":
         total_bytes = 20 * elems * steps   # fwd: read C, write P; bwd: read P, read C, write grad
@@ -579,12 +583,16 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work per baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--iters", type=int, default=None, help="override the config's iteration count (profiling)")
+    ap.add_argument("--rows", type=int, default=None, help="override the config's row count n (profiling)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     cfg["name"] = args.config
     if args.iters is not None and "iters" in cfg:
         cfg["iters"] = args.iters
         cfg["desc"] += f" (run with {args.iters} iterations)"
+    if args.rows is not None:
+        cfg["n"] = args.rows
+        cfg["desc"] += f" (run with {args.rows} rows)"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

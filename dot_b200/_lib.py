@@ -44,6 +44,8 @@ _SIGS = {
     "dot_sinkhorn_bwd_unrolled_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "dot_sinkhorn_bwd_unrolled": (_i, [_vp, _f, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i, _vp, _vp, _vp,
                                        _sz, _vp]),
+    "dot_sinkhorn_rows_colpairs_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "dot_sinkhorn_rows_colpairs": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _i64, _f, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dot_sinkhorn_col_pairs_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "dot_sinkhorn_col_pairs": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _f, _vp, _vp, _sz, _vp]),
     "dot_sinkhorn_col_merge": (_i, [_vp, _i, _vp, _i64, _i64, _vp, _vp]),

@@ -328,6 +328,39 @@ int dot_sinkhorn_col_partials(const float* X, float score_sign, const float* pot
                             static_cast<cudaStream_t>(stream));
 }
 
+size_t dot_sinkhorn_rows_colpairs_workspace_bytes(int64_t B, int64_t n, int64_t m) {
+    if (B <= 0 || n <= 0 || m <= 0) return 0;
+    const size_t a = sk_split_colpairs_ws(B, n, m);
+    const size_t b = (m >= 8192 && m <= 65536 && (m % 32) == 0) ? sk_wide_ws(B, n, m) : 0;
+    return a > b ? a : b;
+}
+
+int dot_sinkhorn_rows_colpairs(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n, int64_t m,
+                               int64_t n_total, float tau, const float* pot_v, float* pot_u, float* pairs,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    int rc = check_dims(B, n, m);
+    if (rc) return rc;
+    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
+    if (n_total < n) return fail(DOT_ERR_INVALID, "n_total must be >= the shard's row count");
+    if (B == 0 || n == 0 || m == 0) return DOT_OK;
+    if (!X || !pot_v || !pot_u || !pairs) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    if ((reinterpret_cast<uintptr_t>(pairs) & 7u) != 0) return fail(DOT_ERR_INVALID, "pairs must be 8-byte aligned");
+    const size_t need = dot_sinkhorn_rows_colpairs_workspace_bytes(B, n, m);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const float kinv = score_sign * (1.0f / tau);
+    const float la_def = -logf(float(n_total));
+    if (sk_wide_supported(B, n, m, X))
+        return sk_wide_rows_pairs(X, kinv, log_a, la_def, B, n, m, pot_v, pot_u, reinterpret_cast<float2*>(pairs),
+                                  workspace, st);
+    rc = sk_split_rows(X, kinv, log_a, la_def, B, n, m, pot_v, pot_u, st);
+    if (rc != DOT_OK) return rc;
+    return sk_split_colpairs(X, kinv, pot_u, B, n, m, reinterpret_cast<float2*>(pairs), workspace, st);
+}
+
 size_t dot_sinkhorn_col_pairs_workspace_bytes(int64_t B, int64_t n, int64_t m) {
     if (B <= 0 || n <= 0 || m <= 0) return 0;
     return sk_split_colpairs_ws(B, n, m);

@@ -76,6 +76,16 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 size_t sk_stream_bwd_ws(int64_t B, int64_t n, int64_t m);
 int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
 
+// Fused single-pass iterations for wide rows on thread-block clusters
+// (sinkhorn_wide.cu): 8192 <= m <= 65536, m % 32 == 0, tol == 0.
+bool sk_wide_supported(int64_t B, int64_t n, int64_t m, const void* X);
+size_t sk_wide_ws(int64_t B, int64_t n, int64_t m);
+int sk_wide_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
+// Row shard: u for the shard's rows from the given v, and the shard's column
+// (max, sum) pairs [B, m] over those rows with the new u, in one pass.
+int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
+                       const float* v2, float* u2, float2* pairs, void* ws, cudaStream_t st);
+
 // Unrolled backward through a recorded forward (sinkhorn_unrolled.cu):
 // a.bwd_iters = the number of recorded iterations to differentiate through.
 size_t sk_unrolled_bwd_ws(int64_t B, int64_t n, int64_t m);

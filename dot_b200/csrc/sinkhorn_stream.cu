@@ -579,6 +579,7 @@ struct SkFwdWs {
     float* delta;
     float* cost_row;
     int32_t* cnt;
+    char* wide;       // wide-row cluster kernels' scratch
 };
 
 // Fused kernels are used when the shape allows it; the workspace covers
@@ -593,6 +594,8 @@ static SkFwdWs carve_fwd(Carve& c, int64_t B, int64_t n, int64_t m, int n_iters,
     w.delta = tol > 0.0f ? c.take<float>(size_t(n_iters > 0 ? n_iters : 1)) : nullptr;
     w.cost_row = want_cost ? c.take<float>(size_t(B * n)) : nullptr;
     w.cnt = c.take<int32_t>(size_t(B));
+    const bool wide_shape = m >= 8192 && m <= 65536 && (m % 32) == 0 && tol == 0.0f;
+    w.wide = wide_shape ? c.take<char>(sk_wide_ws(B, n, m)) : nullptr;
     return w;
 }
 
@@ -624,6 +627,11 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
         plan = sk_fused_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
     }
+    const bool wide = !fused && a.tol == 0.0f && w.wide != nullptr && sk_wide_supported(a.B, a.n, a.m, a.X);
+    if (wide) {
+        int rc = sk_wide_fwd(a, w.wide, st);
+        if (rc != DOT_OK) return rc;
+    }
     const bool hist = a.u_hist != nullptr && a.v_hist != nullptr;
     auto record = [&](int it) {   // potentials after iteration it (unrolled backward)
         if (!hist) return;
@@ -640,7 +648,7 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
             record(it);
         }
     }
-    for (int it = 0; it < (fused ? 0 : a.n_iters); ++it) {
+    for (int it = 0; it < (fused || wide ? 0 : a.n_iters); ++it) {
         if (it > 0) record(it - 1);
         ctl.iter = it;
         {
@@ -659,7 +667,7 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
                                                             chunks, ctl, nullptr);
         }
     }
-    if (!fused && a.n_iters > 0) record(a.n_iters - 1);
+    if (!fused && !wide && a.n_iters > 0) record(a.n_iters - 1);
     {
         ProfScope ps(DOT_K_SK_FWD_EPI, st);
         sk_status_kernel<<<1, 32, 0, st>>>(w.delta, a.status, a.n_iters, a.tol);

@@ -103,13 +103,13 @@ def sinkhorn_rowshard(C_local: torch.Tensor, reg: float, n_iters: int, n_total: 
     u = torch.zeros((B, n), dtype=torch.float32, device=dev)
     v = torch.zeros((B, m), dtype=torch.float32, device=dev)
     pairs = torch.empty((B, m, 2), dtype=torch.float32, device=dev)
-    nb = lib.dot_sinkhorn_col_pairs_workspace_bytes(B, n, m)
+    nb = lib.dot_sinkhorn_rows_colpairs_workspace_bytes(B, n, m)
     ws = _lib.workspace(nb, dev)
     for _ in range(int(n_iters)):
-        _lib.check(lib.dot_sinkhorn_rows(_lib.ptr(X), float(score_sign), _lib.ptr(la), B, n, m, int(n_total), tau,
-                                         _lib.ptr(v), _lib.ptr(u), st), "dot_sinkhorn_rows")
-        _lib.check(lib.dot_sinkhorn_col_pairs(_lib.ptr(X), float(score_sign), _lib.ptr(u), B, n, m, tau,
-                                              _lib.ptr(pairs), _lib.ptr(ws), nb, st), "dot_sinkhorn_col_pairs")
+        # row half-step and this shard's column pairs (one pass for wide rows)
+        _lib.check(lib.dot_sinkhorn_rows_colpairs(_lib.ptr(X), float(score_sign), _lib.ptr(la), B, n, m,
+                                                  int(n_total), tau, _lib.ptr(v), _lib.ptr(u), _lib.ptr(pairs),
+                                                  _lib.ptr(ws), nb, st), "dot_sinkhorn_rows_colpairs")
         gathered, parts = gather_column_pairs(pairs, group=group)
         _lib.check(lib.dot_sinkhorn_col_merge(_lib.ptr(gathered), parts, _lib.ptr(lb), B, m, _lib.ptr(v), st),
                    "dot_sinkhorn_col_merge")

@@ -212,6 +212,16 @@ DOT_API int dot_sinkhorn_col_finish(const float* global_max, const float* global
  * writes v_j = log_b_j - LSE (log_b NULL: -log(m)).  Every shard computes the
  * same v bit for bit.  Same combine as above; no counterpart in the reference.
  */
+/*
+ * dot_sinkhorn_rows followed by dot_sinkhorn_col_pairs in one call; for wide
+ * rows (8192 <= m <= 65536, m % 32 == 0) a single pass over the shard on
+ * thread-block clusters (the matrix is read once per iteration instead of
+ * twice).  No counterpart in the reference (it has no multi-GPU path).
+ */
+DOT_API size_t dot_sinkhorn_rows_colpairs_workspace_bytes(int64_t B, int64_t n, int64_t m);
+DOT_API int dot_sinkhorn_rows_colpairs(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n,
+                                       int64_t m, int64_t n_total, float tau, const float* pot_v, float* pot_u,
+                                       float* pairs, void* workspace, size_t workspace_bytes, void* stream);
 DOT_API size_t dot_sinkhorn_col_pairs_workspace_bytes(int64_t B, int64_t n, int64_t m);
 DOT_API int dot_sinkhorn_col_pairs(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n,
                                    int64_t m, float tau, float* pairs, void* workspace, size_t workspace_bytes,

@@ -17,7 +17,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, shape=(2, 1030, 2000)):
     import datetime
 
     import torch.distributed as dist
@@ -33,7 +33,8 @@ def _worker(rank, world, port, out):
                             device_id=torch.device("cuda", rank))
     try:
         g = torch.Generator().manual_seed(0)
-        B, n, m, reg, T = 2, 1030, 2000, 0.05, 30
+        B, n, m = shape
+        reg, T = 0.05, 30
         C = torch.rand(B, n, m, generator=g)
         lo, hi = shard_range(n, rank, world)
         res = sinkhorn_rowshard(C[:, lo:hi].cuda(), reg, T, n_total=n)
@@ -55,6 +56,21 @@ def test_rowshard_two_gpus_matches_single_gpu():
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    assert len(out) == world
+    for rank, (dP, dv, dc) in out.items():
+        assert dP < 1e-5, (rank, dP)
+        assert dv < 1e-4, (rank, dv)
+        assert dc < 1e-5, (rank, dc)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_rowshard_wide_rows_two_gpus_matches_single_gpu():
+    """Shards of wide rows take the single-pass cluster kernel per iteration."""
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), out, (1, 514, 8192)), nprocs=world, join=True,
+                       start_method="spawn")
     assert len(out) == world
     for rank, (dP, dv, dc) in out.items():
         assert dP < 1e-5, (rank, dP)

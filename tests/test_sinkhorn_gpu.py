@@ -468,3 +468,53 @@ def test_unrolled_dual_and_full_agree():
     assert d.n_iters_used == 30 and f.n_iters_used == 30
     assert torch.allclose(d.transport_plan, f.transport_plan, atol=1e-5)
     assert torch.allclose(c1.grad, c2.grad, atol=1e-4)
+
+
+# ---------------------------------------------------------------------------
+# wide rows (8192 <= m <= 65536): single-pass iterations on thread-block clusters
+# ---------------------------------------------------------------------------
+
+WIDE_SHAPES = [
+    # (B, n, m, reg, T, marginals)
+    (1, 70, 8192, 0.1, 6, False),       # fewer row batches than clusters
+    (3, 50, 8224, 0.2, 5, False),       # partial column slices; problems change inside a cluster's range
+    (1, 300, 16384, 0.05, 10, True),    # non-uniform marginals
+]
+
+
+@pytest.mark.parametrize("B,n,m,reg,T,marg", WIDE_SHAPES, ids=lambda v: str(v))
+def test_wide_rows_forward_matches_oracle(B, n, m, reg, T, marg):
+    g = U.gen(9000 + n + m)
+    C = torch.rand(B, n, m, generator=g)
+    a = b = None
+    if marg:
+        a = U.dirichlet(B, n, 31) + 1e-3
+        a = a / a.sum(-1, keepdim=True)
+        b = U.dirichlet(B, m, 32) + 1e-3
+        b = b / b.sum(-1, keepdim=True)
+    ref = O.sinkhorn_api(C.numpy(), reg, T, None if a is None else a.numpy(), None if b is None else b.numpy(),
+                         with_grad=False)
+    res = dot.sinkhorn(C.to(DEV), reg=reg, n_iters=T, a=None if a is None else a.to(DEV),
+                       b=None if b is None else b.to(DEV), tol=0)
+    U.assert_normwise(res.transport_plan, ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_rel(res.cost, ref["cost"], U.COST_RTOL, "cost", atol=1e-9)
+    # after the last column update the column marginals hold
+    bm = torch.full((B, m), 1.0 / m) if b is None else b
+    assert torch.allclose(res.transport_plan.sum(-2).cpu(), bm, rtol=1e-4, atol=0)
+
+
+def test_wide_rows_unrolled_backward():
+    C = torch.rand(1, 40, 8192, generator=U.gen(9100))
+    W = torch.randn(1, 40, 8192, generator=U.gen(9101))
+    ref = O.sinkhorn_api(C.numpy(), 0.3, 4, grad_P=W.numpy(), backward_mode="unrolled")
+    r = run_api(C, 0.3, 4, plan_weight=W, backward_mode="unrolled")
+    U.assert_normwise(r["P"], ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
+
+
+def test_wide_rows_implicit_backward():
+    C = torch.rand(2, 30, 8192, generator=U.gen(9200))
+    ref = O.sinkhorn_api(C.numpy(), 0.2, 5, bwd_tol=0.0)
+    r = run_api(C, 0.2, 5)
+    U.assert_normwise(r["P"], ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
