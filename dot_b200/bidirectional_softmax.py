@@ -32,8 +32,9 @@ class _BidirectionalSoftmaxFn(torch.autograd.Function):
     def backward(ctx, grad_output: torch.Tensor):
         sim, lengths, rs, cs = ctx.saved_tensors
         gdt = torch.bfloat16 if sim.dtype == torch.bfloat16 else None
+        # tau is a plain float here (no gradient), so its gradient is not computed
         grad_sim, _ = ops.bidirectional_softmax_backward(sim, None, grad_output, rs, cs, ctx.tau, lengths,
-                                                         grad_dtype=gdt)
+                                                         grad_dtype=gdt, want_grad_tau=False)
         return grad_sim, None, None
 
 

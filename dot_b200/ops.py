@@ -255,12 +255,14 @@ def bidirectional_softmax(sim: torch.Tensor, tau: float, lengths: torch.Tensor):
 
 def bidirectional_softmax_backward(sim: torch.Tensor, output: torch.Tensor, grad_output: torch.Tensor,
                                    row_stats: torch.Tensor, col_stats: torch.Tensor, tau: float,
-                                   lengths: torch.Tensor, grad_dtype: Optional[torch.dtype] = None):
+                                   lengths: torch.Tensor, grad_dtype: Optional[torch.dtype] = None,
+                                   want_grad_tau: bool = True):
     """``[grad_sim, grad_tau]`` (``src/bidirectional_softmax/registry.cpp:34``).
 
     ``output`` is accepted for signature parity and not read: the kernels
     recompute it from ``sim`` and the stats.  ``grad_sim`` is float32, or
-    bfloat16 when ``grad_dtype=torch.bfloat16``.
+    bfloat16 when ``grad_dtype=torch.bfloat16``.  ``want_grad_tau=False``
+    skips the temperature gradient (returned as None).
     """
     _need_cuda(sim, "sim")
     s, dt = _bs_dtype(sim)
@@ -270,7 +272,7 @@ def bidirectional_softmax_backward(sim: torch.Tensor, output: torch.Tensor, grad
     g = _f32c(grad_output)
     gdt = torch.bfloat16 if grad_dtype == torch.bfloat16 else torch.float32
     gsim = torch.empty((B, L1, L2), dtype=gdt, device=dev)
-    gtau = torch.empty((B,), dtype=torch.float32, device=dev)
+    gtau = torch.empty((B,), dtype=torch.float32, device=dev) if want_grad_tau else None
     lib = _lib.load()
     nbytes = lib.dot_bidir_bwd_workspace_bytes(B, L1, L2)
     ws = _lib.workspace(nbytes, dev)
