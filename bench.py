@@ -440,10 +440,26 @@ def roofline(cfg: dict, prof: dict, peaks: dict, steps: int, elems_local: int | 
         bytes_per_launch = 8 * elems
     achieved = total_bytes / (v["ms"] / 1e3) / 1e9
     peak = peaks["hbm_gbs"]
-    return {"bound": "hbm", "kernel_class": k, "achieved": achieved, "peak": peak, "unit": "GB/s",
-            "frac": achieved / peak, "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
-            "launches": v["launches"], "algorithmic_bytes_per_launch": bytes_per_launch,
-            "traffic": traffic_from_profiles(k, cfg.get("name", ""))}
+    traffic = traffic_from_profiles(k, cfg.get("name", ""))
+    if traffic is not None and k in ("sk_fwd_iter", "sk_bwd_iter"):
+        # the captured figure is one full single-GPU sweep launch; average it
+        # over this run's launches (row-shard merge launches move no matrix
+        # bytes) and scale it to this rank's rows
+        traffic *= (elems_local / elems) * (sweeps / v["launches"])
+    out = {"bound": "hbm", "kernel_class": k, "achieved": achieved, "peak": peak, "unit": "GB/s",
+           "frac": achieved / peak, "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
+           "launches": v["launches"], "algorithmic_bytes_per_launch": bytes_per_launch,
+           "traffic": traffic}
+    fw, bw = prof.get("sk_fwd_iter"), prof.get("sk_bwd_iter")
+    if k in ("sk_fwd_iter", "sk_bwd_iter") and fw and bw and fw["ms"] > 0 and bw["ms"] > 0:
+        # forward and adjoint iteration sweeps together (each streams the
+        # matrix once per iteration on the single-pass paths)
+        single = (m <= 1024 and m % 4 == 0) or (8192 <= m <= 65536 and m % 32 == 0)
+        nsweep = (cfg["iters"] + cfg.get("bwd_iters", cfg["iters"])) * steps * (1 if single else 2)
+        fb = 4 * elems_local * nsweep / ((fw["ms"] + bw["ms"]) / 1e3) / 1e9
+        out["fwd_bwd"] = {"achieved": fb, "frac": fb / peak, "unit": "GB/s",
+                          "ms": fw["ms"] + bw["ms"], "sweeps": nsweep}
+    return out
 
 
 def traffic_from_profiles(kclass: str, workload: str):

@@ -23,6 +23,7 @@
 namespace dotb {
 
 constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
+constexpr float kLn2 = 0.6931471805599453f;     // ln(2)
 constexpr float kSumFloor = 1.0e-12f;
 constexpr float kNegBig = -FLT_MAX;
 

@@ -313,11 +313,18 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             for (int e = 0; e < NC; ++e) mx = fmaxf(mx, t[e]);
             // row LSE, max pass then sum pass (the reference's two-pass order)
             mx = warp_max<32>(mx);
+            // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e
+            // rounded; cr = mx*log2e - mL exactly (FMA remainder), so every
+            // term carries the common factor 2^cr, taken out of the row LSE
+            // and out of the column weight below
+            const float mxc = fmaxf(mx, -1.0e37f);   // a row of -inf terms keeps mL finite
+            const float mL = mxc * kLog2e;
+            const float cr = fmaf(mxc, kLog2e, -mL);
 #pragma unroll
-            for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);   // t now holds E_ij
+            for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));   // t now holds E_ij * 2^cr
             const float s = warp_sum<32>(tree_sum(t));
             const int64_t grow = grow0 + i;
-            const float unew = lar[q] - lse_finish(mx, s);
+            const float unew = lar[q] - (mx + (logf(fmaxf(s, kSumFloor)) - cr * kLn2));
             if (lane == 0) {
                 if (tolmode) dmax = fmaxf(dmax, fabsf(unew - __ldcg(a.u2 + grow)));
                 a.u2[grow] = unew;
@@ -329,7 +336,7 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
                 for (int e = 0; e < NC; ++e) cS[e] *= sc;
                 A = ai;
             }
-            const float w = exp_shift(ai - A);
+            const float w = ex2(fmaf(ai - A, kLog2e, -cr));   // exp(ai - A) / 2^cr
 #pragma unroll
             for (int e = 0; e < NC; ++e) cS[e] = fmaf(t[e], w, cS[e]);
         };
