@@ -102,6 +102,21 @@ __device__ __forceinline__ float tree_sum(const float (&x)[N]) {
     }
 }
 
+// Max of N registers as a balanced tree (max is exact: any order gives the
+// same value).
+template <int N>
+__device__ __forceinline__ float tree_max(const float (&x)[N]) {
+    if constexpr (N == 1) {
+        return x[0];
+    } else {
+        float h[(N + 1) / 2];
+#pragma unroll
+        for (int k = 0; k < N / 2; ++k) h[k] = fmaxf(x[2 * k], x[2 * k + 1]);
+        if constexpr (N % 2 == 1) h[N / 2] = x[N - 1];
+        return tree_max<(N + 1) / 2>(h);
+    }
+}
+
 // Online update of a (max, sum) partial with a group of K new values
 // (-INFINITY marks an empty slot).
 template <int K>

@@ -261,8 +261,8 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
     float dmax = 0.0f;
     int cur = -1;
 
+    int b = rg.g0 / c.s.nblk, jb = rg.g0 - b * c.s.nblk;   // advanced per block, no division
     for (int g = rg.g0; g < rg.g1; ++g) {
-        const int b = g / c.s.nblk, jb = g - b * c.s.nblk;
         if (b != cur) {   // first block of a problem in this range
             cur = b;
 #pragma unroll
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             for (int e = 0; e < NC; ++e) cS[e] = 0.0f;
             A = kNegBig;
         }
-        const int rj = rg.rows_in(g);
+        const int rj = int(min(int64_t(R), n - int64_t(jb) * R));
         const int64_t grow0 = int64_t(b) * n + int64_t(jb) * R;   // global row of the block's row 0
         float lar[RPW];
 #pragma unroll
@@ -415,6 +415,10 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             __syncthreads();
         }
         if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
+        if (++jb == c.s.nblk) {
+            jb = 0;
+            ++b;
+        }
     }
 
     if (tolmode) {
@@ -452,8 +456,8 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_bw
     float mr[NC], acc[NC];
     int cur = -1;
 
+    int b = rg.g0 / c.s.nblk, jb = rg.g0 - b * c.s.nblk;   // advanced per block, no division
     for (int g = rg.g0; g < rg.g1; ++g) {
-        const int b = g / c.s.nblk, jb = g - b * c.s.nblk;
         if (b != cur) {
             cur = b;
 #pragma unroll
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_bw
 #pragma unroll
             for (int e = 0; e < NC; ++e) acc[e] = 0.0f;
         }
-        const int rj = rg.rows_in(g);
+        const int rj = int(min(int64_t(R), n - int64_t(jb) * R));
         const int64_t grow0 = int64_t(b) * n + int64_t(jb) * R;
         float2 ri[RPW];   // row invariants, loaded before waiting on the block
 #pragma unroll
@@ -550,6 +554,10 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_bw
             __syncthreads();
         }
         if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
+        if (++jb == c.s.nblk) {
+            jb = 0;
+            ++b;
+        }
     }
 }
 

@@ -7,19 +7,25 @@
 // A row does not fit one CTA's registers, so a thread-block cluster of kWC
 // CTAs shares every row: CTA r of a cluster owns columns [r*mc, (r+1)*mc),
 // mc = m / kWC, and keeps v and its columns' running partials in registers
-// (thread t: columns 4t + 2048q, q < NQ).  The clusters split the B*nbat row
-// batches (kWR rows each) into equal contiguous ranges.  Per batch, every CTA
-//   pass A   streams its slice of the batch's rows into shared memory (1-D
-//            bulk copies on a 3-stage mbarrier ring), forms t = K + v, a
-//            warp-wide max, E = exp(t - max) (written back in place) and the
-//            warp sums, merges its warps into one (max, sum) per row and
-//            stores that pair into every CTA of the cluster (distributed
-//            shared memory), then arrives on the cluster barrier;
-//   pass B   of the previous batch runs while the barrier completes: the
-//            column partials S_j += E_ij * exp(max_i + u_i - A) (one FFMA per
-//            element, A a warp-wide reference, as in sinkhorn_fused.cu);
-//   merge    after the barrier, each CTA combines the kWC pairs of every row
-//            in rank order (all CTAs get the same LSE) into u_i.
+// (thread t: columns 4t + 4Tq, q < NQ, T threads).  The clusters split the
+// B*nbat row batches into equal contiguous ranges.
+// Per batch g (the rows of one stage, R <= 4), every warp of every CTA
+//   pass A   waits for the batch's slice rows (1-D bulk copies on a 3-stage
+//            mbarrier ring), forms t = K + v over its columns, a warp max,
+//            E = exp(t - max) (written back in place) and the warp sum, and
+//            stores that (max, sum) pair into every CTA of the cluster with
+//            st.async, whose bytes complete a transaction on the receiver's
+//            mbarrier (a 4-slot ring of exchange buffers);
+//   u        of the previous batch g-1: waits for that batch's pairs from all
+//            kWC x W warps of the cluster (they had this batch's pass A to
+//            arrive) and merges them itself (every warp gets the same LSE);
+//   pass B   of batch g-1: column partials S_j += E_ij * exp(max_i + u_i - A)
+//            (one FFMA per element, A a warp-wide reference, as in
+//            sinkhorn_fused.cu); the last warp done with a stage refills it.
+// No barrier joins the warps inside the loop.  A sender reuses a slot only
+// after every warp of the cluster has consumed the slot's previous batch:
+// sending batch g follows the sender's own u of batch g-2, which needed
+// batch g-2's pairs from every warp, each sent after that warp's u of g-4.
 // When its range leaves a problem, a CTA publishes its columns' partials;
 // the CTA that arrives last among the same-rank CTAs of every cluster that
 // touched the problem merges that column slice in cluster order (atomic
@@ -29,6 +35,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <string>
 
 #include "common.cuh"
 #include "internal.h"
@@ -40,21 +47,23 @@ namespace dotb {
 namespace {
 
 constexpr int kWC = 8;                 // CTAs per cluster
-constexpr int kWS = 3;                 // ring stages
 constexpr int kWMaxR = 4;              // rows per batch (at most)
+constexpr int kWX = 4;                 // row-pair exchange slots (batches in flight between CTAs)
 
-// CTA shapes: (A) 512 threads, 64 KB stages, one CTA per SM; (B) 256
-// threads, 32 KB stages, two CTAs per SM (one CTA computes while the other
-// waits at its cluster barrier; clusters also pack onto more SMs).
-template <int T_, int STAGE_, int MINB_>
+// CTA shapes: threads, stage bytes, CTAs per SM, stages.  A batch is the
+// rows one stage holds; its exponentials stay in the stage until the column
+// update, so deep stages (few batches, little per-batch work) pay best.
+template <int T_, int STAGE_, int MINB_, int S_>
 struct WCfg {
     static constexpr int T = T_;
     static constexpr int W = T_ / 32;
     static constexpr int STAGE = STAGE_;
     static constexpr int MINB = MINB_;
+    static constexpr int S = S_;
 };
-using WideA = WCfg<512, 65536, 1>;
-using WideB = WCfg<256, 32768, 2>;
+using WideA = WCfg<512, 65536, 1, 3>;   // 512 threads, one CTA per SM (slices up to 8192 columns)
+using WideB = WCfg<256, 32768, 2, 3>;   // 256 threads, two CTAs per SM (slices up to 4096 columns)
+enum WideShape { kShapeA = 0, kShapeB = 1 };
 constexpr int kWFix = 1024;            // exactly recomputed columns per slice merge (cap)
 constexpr float kRaiseW = 60.0f;
 constexpr float kTinyW = 8.077935669463161e-28f;   // 2^-90
@@ -71,12 +80,6 @@ __device__ __forceinline__ uint32_t w_cid() {
 }
 __device__ __forceinline__ void w_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void w_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-__device__ __forceinline__ void w_st_remote(const void* local, uint32_t rank, float2 v) {
-    uint32_t a;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(local)), "r"(rank));
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v.x), "f"(v.y) : "memory");
-}
-
 struct WideArgs {
     const float* X;
     float kinv;
@@ -96,6 +99,7 @@ struct WideArgs {
     int32_t* cnt;       // [B][kWC] arrival counters, zero between launches
     float2* pairs;      // row-shard mode: merged column pairs [B][m]; nullptr: write v
     int32_t* err;       // bounded-wait expiry word
+    int wmode;          // barrier wait form (mbar_wait_mode)
 };
 
 __host__ __device__ __forceinline__ int w_q(const WideArgs& a, int k) { return int(int64_t(k) * a.TB / a.G); }
@@ -121,13 +125,17 @@ __device__ float w_exact_column(const float* X, const float* u2, float kinv, int
 
 template <class CFG, int NQ, bool FULL>
 __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a) {
-    constexpr int NC = 4 * NQ, kWT = CFG::T, kWW = CFG::W, kWStage = CFG::STAGE;
+    constexpr int NC = 4 * NQ, kWT = CFG::T, kWW = CFG::W, kWStage = CFG::STAGE, kWS = CFG::S;
+    constexpr int kP = kWC * kWW;   // pairs per row of a batch: one per warp of the cluster
+    constexpr int kPL = kP / 32;    // pairs per lane in the merge
+    static_assert(kP % 32 == 0, "warps per cluster must be a multiple of 32");
     extern __shared__ __align__(128) unsigned char smem[];
-    float2* xch = reinterpret_cast<float2*>(smem + size_t(kWS) * kWStage);   // [2][kWC][kWMaxR]
-    __shared__ __align__(8) uint64_t bars[kWS];
-    __shared__ float2 s_wp[kWW][kWMaxR];   // warp (max, sum) per row
-    __shared__ float s_u[2][kWMaxR];       // u of the rows of a batch, by batch parity
-    __shared__ int s_flag, s_nfix;
+    float2* xch = reinterpret_cast<float2*>(smem + size_t(kWS) * kWStage);   // [kWX][R][kP]
+    __shared__ __align__(8) uint64_t full[kWS];   // a stage's rows have landed (bulk-copy bytes)
+    __shared__ __align__(8) uint64_t xbar[kWX];   // a batch's row pairs from every warp of the cluster have landed
+    __shared__ unsigned s_rel[kWS];               // warps done with a stage (wrapping counter)
+    __shared__ int s_flag, s_nfix, s_next, s_kfail;
+    __shared__ volatile int s_abort;              // a bounded wait expired: stop copying and waiting
     __shared__ int s_fix[kWFix];
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -136,7 +144,11 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
     const int64_t cbase = int64_t(rank) * mc;
     const int g0 = w_q(a, int(cid)), g1 = w_q(a, int(cid) + 1);
     auto live = [&](int q) -> bool { return FULL || (4 * tid + 4 * kWT * q) < mc; };
-    auto stage = [&](int g) -> float* { return reinterpret_cast<float*>(smem + size_t((g - g0) % kWS) * kWStage); };
+    auto sidx = [&](int g) -> int { return (g - g0) % kWS; };
+    auto sphase = [&](int g) -> uint32_t { return uint32_t(((g - g0) / kWS) & 1); };
+    auto stage = [&](int g) -> float* { return reinterpret_cast<float*>(smem + size_t(sidx(g)) * kWStage); };
+    auto xidx = [&](int g) -> int { return (g - g0) % kWX; };
+    auto xphase = [&](int g) -> uint32_t { return uint32_t(((g - g0) / kWX) & 1); };
     auto rows_of = [&](int g) -> int {
         const int jb = g % a.nbat;
         return int(min(int64_t(a.R), n - int64_t(jb) * a.R));
@@ -145,25 +157,50 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
         const int b = g / a.nbat, jb = g - b * a.nbat;
         const int rows = rows_of(g);
         const uint32_t bytes = uint32_t(mc) * 4u;
-        uint64_t* bb = &bars[(g - g0) % kWS];
+        uint64_t* bb = &full[sidx(g)];
         mbar_arrive_expect_tx(bb, bytes * uint32_t(rows));
         const float* src = a.X + (int64_t(b) * n + int64_t(jb) * a.R) * m + cbase;
         for (int r = 0; r < rows; ++r) bulk_g2s(stage(g) + int64_t(r) * mc, src + int64_t(r) * m, bytes, bb);
+        s_next = g + 1;
+    };
+    auto wait_full = [&](int g) -> bool {
+        if (s_abort) return false;
+        const bool r = mbar_wait_mode(&full[sidx(g)], sphase(g), a.wmode, false, a.err);
+        if (!r) s_abort = 1;
+        return r;
+    };
+    auto wait_pairs = [&](int g) -> bool {
+        if (s_abort) return false;
+        const bool r = mbar_wait_mode(&xbar[xidx(g)], xphase(g), a.wmode, true, a.err);
+        if (!r) s_abort = 1;
+        return r;
     };
 
     if (tid == 0) {
 #pragma unroll
-        for (int k = 0; k < kWS; ++k) mbar_init(&bars[k], 1);
+        for (int k = 0; k < kWS; ++k) {
+            mbar_init(&full[k], 1);
+            s_rel[k] = 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kWX; ++k) mbar_init(&xbar[k], 1);
+        s_abort = 0;
+        s_nfix = 0;
+        s_next = g0;
+        s_kfail = g1;
         mbar_fence_init();
     }
     __syncthreads();
+    w_arrive();   // every CTA of the cluster has initialised its barriers before a pair is sent to it
+    w_wait();
     if (tid == 0)
         for (int g = g0; g < g1 && g < g0 + kWS; ++g) issue(g);
 
     float vr[NC], cS[NC];
-    float A = kNegBig;              // warp-wide column reference
-    float tmc[kWMaxR], tmp[kWMaxR]; // warp row maxima: current batch, pending batch
-    int cur = -1, pend = -1, kfail = -1;
+    float A = kNegBig;               // warp-wide column reference
+    float tmc[kWMaxR], tmp[kWMaxR];  // warp row maxima: current batch, pending batch
+    float uw[kWMaxR];                // u of the pending batch's rows
+    int cur = -1, pend = -1;
 
     auto load_v = [&](int b) {
 #pragma unroll
@@ -181,35 +218,74 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
         A = kNegBig;
     };
 
-    // column update of a batch whose E and u are ready; frees its stage
-    auto pass_b = [&](int gp) {
-        const float* es = stage(gp);
-        const int rows = rows_of(gp);
-        if (kfail < 0) {
-            for (int ir = 0; ir < rows; ++ir) {
-                const float ai = tmp[ir] + s_u[gp & 1][ir];   // warp-uniform
-                if (ai > A + kRaiseW) {
-                    const float sc = exp_shift(A - ai);
+    // u of batch gp's rows from the kP pairs of each row (every warp of the
+    // cluster sent one): max over the lanes, then the rescaled sums added in
+    // a fixed order, so every warp of every CTA gets the same value.  Warp 0
+    // writes it out, before its CTA's flush arrival.
+    auto take_u = [&](int gp, int rp, int64_t grow0) {
+        wait_pairs(gp);
+        const float2* xs = xch + xidx(gp) * a.R * kP;
 #pragma unroll
-                    for (int e = 0; e < NC; ++e) cS[e] *= sc;
-                    A = ai;
+        for (int ir = 0; ir < kWMaxR; ++ir) {
+            if (ir < rp) {
+                float2 q[kPL];
+                float ml = kNegBig;
+#pragma unroll
+                for (int k = 0; k < kPL; ++k) {
+                    q[k] = xs[ir * kP + lane + 32 * k];
+                    ml = fmaxf(ml, q[k].x);
                 }
-                const float w = exp_shift(ai - A);
+                const float mm = warp_max<32>(ml);
+                float sl = 0.0f;
 #pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    if (live(q)) {
-                        const float4 e4 = *reinterpret_cast<const float4*>(es + int64_t(ir) * mc + 4 * tid + 4 * kWT * q);
-                        cS[4 * q + 0] = fmaf(e4.x, w, cS[4 * q + 0]);
-                        cS[4 * q + 1] = fmaf(e4.y, w, cS[4 * q + 1]);
-                        cS[4 * q + 2] = fmaf(e4.z, w, cS[4 * q + 2]);
-                        cS[4 * q + 3] = fmaf(e4.w, w, cS[4 * q + 3]);
+                for (int k = 0; k < kPL; ++k) sl = fmaf(q[k].y, exp_shift(q[k].x - mm), sl);
+                const float ss = warp_sum<32>(sl);
+                const int64_t grow = grow0 + ir;
+                uw[ir] = (a.la ? __ldg(a.la + grow) : a.la_def) - lse_finish(mm, ss);
+                if (wid == 0 && lane == 0) a.u2[grow] = uw[ir];
+            }
+        }
+    };
+
+    // column update of batch gp (E in its stage, u in uw); the last warp
+    // done with the stage refills it
+    auto pass_b = [&](int gp, int rows) {
+        const float* es = stage(gp);
+        if (!s_abort) {
+#pragma unroll
+            for (int ir = 0; ir < kWMaxR; ++ir) {
+                if (ir < rows) {
+                    const float ai = tmp[ir] + uw[ir];   // warp-uniform
+                    if (ai > A + kRaiseW) {
+                        const float sc = exp_shift(A - ai);
+#pragma unroll
+                        for (int e = 0; e < NC; ++e) cS[e] *= sc;
+                        A = ai;
+                    }
+                    const float w = exp_shift(ai - A);
+#pragma unroll
+                    for (int q = 0; q < NQ; ++q) {
+                        if (live(q)) {
+                            const float4 e4 =
+                                *reinterpret_cast<const float4*>(es + ir * int(mc) + 4 * tid + 4 * kWT * q);
+                            cS[4 * q + 0] = fmaf(e4.x, w, cS[4 * q + 0]);
+                            cS[4 * q + 1] = fmaf(e4.y, w, cS[4 * q + 1]);
+                            cS[4 * q + 2] = fmaf(e4.z, w, cS[4 * q + 2]);
+                            cS[4 * q + 3] = fmaf(e4.w, w, cS[4 * q + 3]);
+                        }
                     }
                 }
             }
         }
-        fence_proxy_async_smem();   // E was written with generic stores; the stage is refilled by a bulk copy
-        __syncthreads();
-        if (tid == 0 && kfail < 0 && gp + kWS < g1) issue(gp + kWS);
+        fence_proxy_async_smem();   // this thread's E stores before the stage's bulk-copy refill
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicInc(&s_rel[sidx(gp)], unsigned(kWW - 1)) == unsigned(kWW - 1)) {
+                __threadfence_block();
+                if (gp + kWS < g1 && !s_abort) issue(gp + kWS);
+            }
+        }
     };
 
     // publish this CTA's column partials of problem b; the last same-rank
@@ -264,102 +340,106 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
         __syncthreads();
     };
 
+    // Warps run decoupled: each waits for its stage, sends its own row pairs
+    // and takes u itself; they meet only at problem boundaries (flush).
+    // batch coordinates advance incrementally (no division per batch)
+    int b = g0 / a.nbat, jb = g0 - b * a.nbat;
+    int prows = 0;
+    int64_t pgrow0 = 0;
     for (int g = g0; g < g1; ++g) {
-        const int b = g / a.nbat, jb = g - b * a.nbat;
         if (b != cur) {
-            if (pend >= 0) {
-                pass_b(pend);
+            if (pend >= 0) {   // finish the previous problem's last batch
+                take_u(pend, prows, pgrow0);
+                pass_b(pend, prows);
                 pend = -1;
             }
             if (cur >= 0) flush(cur);
             cur = b;
             load_v(b);
         }
-        const int rows = rows_of(g);
-        const bool ok = kfail < 0 && __syncthreads_and(mbar_wait_sleep(&bars[(g - g0) % kWS],
-                                                                       uint32_t(((g - g0) / kWS) & 1), a.err));
-        if (kfail < 0 && !ok) kfail = g;
+        const int rows = min(a.R, int(n - int64_t(jb) * a.R));
+        const int64_t grow0 = int64_t(b) * n + int64_t(jb) * a.R;
+        if (tid == 0) mbar_arrive_expect_tx(&xbar[xidx(g)], uint32_t(rows * kP) * uint32_t(sizeof(float2)));
+        const bool ok = __all_sync(0xffffffffu, wait_full(g));
+        if (!ok && lane == 0) atomicMin(&s_kfail, g);
 
-        // ---- pass A: row partials of this CTA's columns ----
+        // ---- pass A: row partials of this warp's columns; E written in place ----
         float* xs = stage(g);
-        for (int ir = 0; ir < rows; ++ir) {
-            float mx = kNegBig, s = 0.0f;
-            if (ok) {
-                float t[NC];
 #pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    if (live(q)) {
-                        const float4 x = *reinterpret_cast<const float4*>(xs + int64_t(ir) * mc + 4 * tid + 4 * kWT * q);
-                        t[4 * q + 0] = kplus(x.x, a.kinv, vr[4 * q + 0]);
-                        t[4 * q + 1] = kplus(x.y, a.kinv, vr[4 * q + 1]);
-                        t[4 * q + 2] = kplus(x.z, a.kinv, vr[4 * q + 2]);
-                        t[4 * q + 3] = kplus(x.w, a.kinv, vr[4 * q + 3]);
-                    } else {
-                        t[4 * q + 0] = t[4 * q + 1] = t[4 * q + 2] = t[4 * q + 3] = -INFINITY;
+        for (int ir = 0; ir < kWMaxR; ++ir) {
+            if (ir < rows) {
+                float mx = kNegBig, s = 0.0f;
+                if (ok) {
+                    float t[NC];
+#pragma unroll
+                    for (int q = 0; q < NQ; ++q) {
+                        if (live(q)) {
+                            const float4 x =
+                                *reinterpret_cast<const float4*>(xs + ir * int(mc) + 4 * tid + 4 * kWT * q);
+                            t[4 * q + 0] = kplus(x.x, a.kinv, vr[4 * q + 0]);
+                            t[4 * q + 1] = kplus(x.y, a.kinv, vr[4 * q + 1]);
+                            t[4 * q + 2] = kplus(x.z, a.kinv, vr[4 * q + 2]);
+                            t[4 * q + 3] = kplus(x.w, a.kinv, vr[4 * q + 3]);
+                        } else {
+                            t[4 * q + 0] = t[4 * q + 1] = t[4 * q + 2] = t[4 * q + 3] = -INFINITY;
+                        }
+                    }
+                    mx = warp_max<32>(fmaxf(mx, tree_max(t)));
+#pragma unroll
+                    for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
+                    s = warp_sum<32>(tree_sum(t));
+#pragma unroll
+                    for (int q = 0; q < NQ; ++q) {
+                        if (live(q))
+                            *reinterpret_cast<float4*>(xs + ir * int(mc) + 4 * tid + 4 * kWT * q) =
+                                make_float4(t[4 * q + 0], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
                     }
                 }
-#pragma unroll
-                for (int e = 0; e < NC; ++e) mx = fmaxf(mx, t[e]);
-                mx = warp_max<32>(mx);
-#pragma unroll
-                for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
-                s = warp_sum<32>(tree_sum(t));
-#pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    if (live(q))
-                        *reinterpret_cast<float4*>(xs + int64_t(ir) * mc + 4 * tid + 4 * kWT * q) =
-                            make_float4(t[4 * q + 0], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+                tmc[ir] = mx;
+                if (lane < kWC) {   // this warp's pair of row ir to CTA `lane` of the cluster
+                    const float2* dst = xch + (xidx(g) * a.R + ir) * kP + int(rank) * kWW + wid;
+                    st_async_f2(cluster_map(dst, uint32_t(lane)), cluster_map(&xbar[xidx(g)], uint32_t(lane)),
+                                make_float2(mx, s));
                 }
             }
-            tmc[ir] = mx;
-            if (lane == 0) s_wp[wid][ir] = make_float2(mx, s);
         }
-        __syncthreads();
-        if (tid < rows * kWC) {   // this CTA's (max, sum) of each row, to every CTA of the cluster
-            const int ir = tid / kWC, peer = tid % kWC;
-            float mm = kNegBig, ss = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kWW; ++w) lse_merge(mm, ss, s_wp[w][ir].x, s_wp[w][ir].y);
-            w_st_remote(xch + ((g & 1) * kWC + rank) * kWMaxR + ir, uint32_t(peer), make_float2(mm, ss));
+        if (pend >= 0) {   // its pairs had this batch's pass A to arrive
+            take_u(pend, prows, pgrow0);
+            pass_b(pend, prows);
         }
-        w_arrive();
-        if (pend >= 0) pass_b(pend);   // overlaps the exchange
-        w_wait();
-
-        // ---- merge: u of this batch's rows (identical in every CTA) ----
-        if (tid < rows) {
-            float mm = kNegBig, ss = 0.0f;
-#pragma unroll
-            for (int r = 0; r < kWC; ++r) {
-                const float2 q = xch[((g & 1) * kWC + r) * kWMaxR + tid];
-                lse_merge(mm, ss, q.x, q.y);
-            }
-            const int64_t grow = int64_t(b) * n + int64_t(jb) * a.R + tid;
-            const float unew = (a.la ? a.la[grow] : a.la_def) - lse_finish(mm, ss);
-            s_u[g & 1][tid] = unew;
-            a.u2[grow] = unew;   // every rank writes the same value: ordered before its own arrival
-        }
-        __syncthreads();
 #pragma unroll
         for (int ir = 0; ir < kWMaxR; ++ir) tmp[ir] = tmc[ir];
         pend = g;
+        prows = rows;
+        pgrow0 = grow0;
+        if (++jb == a.nbat) {
+            jb = 0;
+            ++b;
+        }
     }
-    if (pend >= 0) pass_b(pend);
+    if (pend >= 0) {
+        take_u(pend, prows, pgrow0);
+        pass_b(pend, prows);
+    }
     if (cur >= 0) flush(cur);
-    if (kfail >= 0 && tid == 0)   // copies still in flight after a failed wait
-        for (int g = kfail; g < g1 && g < kfail + kWS; ++g)
-            mbar_wait_sleep(&bars[(g - g0) % kWS], uint32_t(((g - g0) / kWS) & 1), nullptr);
+    __syncthreads();
+    if (tid == 0)   // copies still in flight after a failed wait
+        for (int g = s_kfail; g < s_next && g < s_kfail + kWS; ++g)
+            mbar_wait_sleep(&full[sidx(g)], sphase(g), nullptr);
+    w_arrive();   // no CTA leaves while a peer may still store into its shared memory
+    w_wait();
 }
 
+// Stages plus the pair-exchange slots for batches of R rows.
 template <class CFG>
-size_t wide_smem() { return size_t(kWS) * CFG::STAGE + 2 * kWC * kWMaxR * sizeof(float2); }
+size_t wide_smem(int R) { return size_t(CFG::S) * CFG::STAGE + size_t(kWX) * R * kWC * CFG::W * sizeof(float2); }
 
 template <class CFG>
-cudaLaunchConfig_t wide_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr) {
+cudaLaunchConfig_t wide_config(int grid, int R, cudaStream_t st, cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid));
     cfg.blockDim = dim3(CFG::T);
-    cfg.dynamicSmemBytes = wide_smem<CFG>();
+    cfg.dynamicSmemBytes = wide_smem<CFG>(R);
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kWC;
@@ -370,89 +450,98 @@ cudaLaunchConfig_t wide_config(int grid, cudaStream_t st, cudaLaunchAttribute* a
     return cfg;
 }
 
-// DOT_B200_WIDE_CTAS=1 or 2 selects the CTA shape (tuning runs); 2 by
-// default where the slice fits it (mc <= 4096), else 1.
-int wide_ctas_pref() {
+// DOT_B200_WIDE_SHAPE = a | b selects the CTA shape (tuning runs; b only
+// where the slice fits it, mc <= 4096).  Default: b for mc <= 4096, else a.
+int wide_shape(int64_t mc) {
+    static int pref = [] {
+        const char* e = std::getenv("DOT_B200_WIDE_SHAPE");
+        if (e == nullptr) return -1;
+        const std::string v(e);
+        return v == "a" ? int(kShapeA) : v == "b" ? int(kShapeB) : -1;
+    }();
+    if (pref == kShapeA) return pref;
+    if (pref == kShapeB && mc <= 4096) return pref;
+    return mc <= 4096 ? kShapeB : kShapeA;
+}
+
+// DOT_B200_WIDE_WAIT = 0 | 1 | 2 selects the barrier wait form (tuning runs).
+int wide_wait_mode() {
     static int v = [] {
-        const char* e = std::getenv("DOT_B200_WIDE_CTAS");
-        const int x = e ? std::atoi(e) : 2;
-        return x == 1 ? 1 : 2;
+        const char* e = std::getenv("DOT_B200_WIDE_WAIT");
+        const int x = e ? std::atoi(e) : 0;
+        return (x >= 0 && x <= 2) ? x : 0;
     }();
     return v;
 }
-bool use_b(int64_t mc) { return wide_ctas_pref() == 2 && mc <= 4096; }
 
 template <class CFG>
 int nq_of(int64_t mc) {
     const int64_t per = 4 * CFG::T;
-    return mc <= per ? 1 : mc <= 2 * per ? 2 : mc <= 4 * per ? 4 : 8;
+    return mc <= per ? 1 : mc <= 2 * per ? 2 : 4;
 }
 
 template <class CFG, int NQ>
 void launch_nq(const WideArgs& a, cudaStream_t st) {
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = wide_config<CFG>(a.G * kWC, st, attr);
+    cudaLaunchConfig_t cfg = wide_config<CFG>(a.G * kWC, a.R, st, attr);
     if (a.mc == 4 * CFG::T * NQ) cudaLaunchKernelEx(&cfg, skw_iter_kernel<CFG, NQ, true>, a);
     else cudaLaunchKernelEx(&cfg, skw_iter_kernel<CFG, NQ, false>, a);
 }
 
-template <class CFG, int NQ>
-void set_attr_nq() {
-    cudaFuncSetAttribute(skw_iter_kernel<CFG, NQ, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         int(wide_smem<CFG>()));
-    cudaFuncSetAttribute(skw_iter_kernel<CFG, NQ, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         int(wide_smem<CFG>()));
-}
-
-void launch_any(const WideArgs& a, cudaStream_t st) {
-    if (use_b(a.mc)) {
-        switch (nq_of<WideB>(a.mc)) {
-            case 1: launch_nq<WideB, 1>(a, st); break;
-            case 2: launch_nq<WideB, 2>(a, st); break;
-            default: launch_nq<WideB, 4>(a, st); break;
-        }
-    } else {
-        switch (nq_of<WideA>(a.mc)) {
-            case 1: launch_nq<WideA, 1>(a, st); break;
-            case 2: launch_nq<WideA, 2>(a, st); break;
-            default: launch_nq<WideA, 4>(a, st); break;
-        }
+template <class CFG>
+void launch_cfg(const WideArgs& a, cudaStream_t st) {
+    switch (nq_of<CFG>(a.mc)) {
+        case 1: launch_nq<CFG, 1>(a, st); break;
+        case 2: launch_nq<CFG, 2>(a, st); break;
+        default: launch_nq<CFG, 4>(a, st); break;
     }
 }
 
-int max_clusters(bool b_shape) {
-    static int cached[2][64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int k = b_shape ? 1 : 0;
-    if (dev >= 0 && dev < 64 && cached[k][dev] > 0) return cached[k][dev];
-    set_attr_nq<WideA, 1>();
-    set_attr_nq<WideA, 2>();
-    set_attr_nq<WideA, 4>();
-    set_attr_nq<WideB, 1>();
-    set_attr_nq<WideB, 2>();
-    set_attr_nq<WideB, 4>();
+template <class CFG>
+void set_attr_cfg() {
+    const int bytes = int(wide_smem<CFG>(kWMaxR));
+    cudaFuncSetAttribute(skw_iter_kernel<CFG, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(skw_iter_kernel<CFG, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(skw_iter_kernel<CFG, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(skw_iter_kernel<CFG, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(skw_iter_kernel<CFG, 4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(skw_iter_kernel<CFG, 4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+template <class CFG>
+int occupancy_clusters(int R) {
     cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = wide_config<CFG>(kWC, R, nullptr, attr);
     int ncl = 0;
-    cudaError_t e;
-    if (b_shape) {
-        cudaLaunchConfig_t cfg = wide_config<WideB>(kWC, nullptr, attr);
-        e = cudaOccupancyMaxActiveClusters(&ncl, skw_iter_kernel<WideB, 4, true>, &cfg);
-    } else {
-        cudaLaunchConfig_t cfg = wide_config<WideA>(kWC, nullptr, attr);
-        e = cudaOccupancyMaxActiveClusters(&ncl, skw_iter_kernel<WideA, 2, true>, &cfg);
-    }
-    if (e != cudaSuccess || ncl < 1) {
+    if (cudaOccupancyMaxActiveClusters(&ncl, skw_iter_kernel<CFG, 4, true>, &cfg) != cudaSuccess || ncl < 1) {
         cudaGetLastError();
         ncl = 1;
     }
-    if (dev >= 0 && dev < 64) cached[k][dev] = ncl;
+    return ncl;
+}
+
+void launch_any(const WideArgs& a, cudaStream_t st) {
+    if (wide_shape(a.mc) == kShapeA) launch_cfg<WideA>(a, st);
+    else launch_cfg<WideB>(a, st);
+}
+
+// Resident clusters of the shape with R-row batches on this device (cached
+// per device).
+int max_clusters(int shape, int R) {
+    static int cached[2][kWMaxR + 1][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[shape][R][dev] > 0) return cached[shape][R][dev];
+    set_attr_cfg<WideA>();
+    set_attr_cfg<WideB>();
+    const int ncl = shape == kShapeA ? occupancy_clusters<WideA>(R) : occupancy_clusters<WideB>(R);
+    if (dev >= 0 && dev < 64) cached[shape][R][dev] = ncl;
     return ncl;
 }
 
 // Rows per batch: as many rows of the CTA's slice as one stage holds (<= 4).
 int wide_rows(int64_t mc) {
-    const int64_t stage = use_b(mc) ? WideB::STAGE : WideA::STAGE;
+    const int64_t stage = wide_shape(mc) == kShapeA ? WideA::STAGE : WideB::STAGE;
     return int(std::max<int64_t>(1, std::min<int64_t>(kWMaxR, stage / (mc * 4))));
 }
 
@@ -467,7 +556,7 @@ WidePlan wide_plan(int64_t B, int64_t n, int64_t m) {
     p.R = wide_rows(p.mc);
     p.nbat = int((n + p.R - 1) / p.R);
     p.TB = int(B * p.nbat);
-    p.G = int(std::min<int64_t>(max_clusters(use_b(p.mc)), p.TB));
+    p.G = int(std::min<int64_t>(max_clusters(wide_shape(p.mc), p.R), p.TB));
     WideArgs tmp{};
     tmp.TB = p.TB;
     tmp.G = p.G;
@@ -534,6 +623,7 @@ int sk_wide_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     w.maxseg = int(wide_seg_bound(a.B, a.n, a.m));
     w.pairs = nullptr;
     w.err = a.status + 3;
+    w.wmode = wide_wait_mode();
     const int64_t rows = a.B * a.n;
     const bool hist = a.u_hist != nullptr && a.v_hist != nullptr;
     ProfScope ps(DOT_K_SK_FWD_ITER, st, a.n_iters);
@@ -578,6 +668,7 @@ int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def
     w.maxseg = int(wide_seg_bound(B, n, m));
     w.pairs = pairs;
     w.err = nullptr;
+    w.wmode = wide_wait_mode();
     ProfScope ps(DOT_K_SK_FWD_ITER, st);
     launch_any(w, st);
     return check_launch("sinkhorn rows + column pairs (wide rows)");
