@@ -64,6 +64,13 @@ struct WCfg {
 using WideA = WCfg<512, 65536, 1, 3>;   // 512 threads, one CTA per SM (slices up to 8192 columns)
 using WideB = WCfg<256, 32768, 2, 3>;   // 256 threads, two CTAs per SM (slices up to 4096 columns)
 enum WideShape { kShapeA = 0, kShapeB = 1 };
+// Rows per batch for a shape and NQ (slices of at most 4*T*NQ columns): the
+// rows of a full slice one stage holds, at most kWMaxR.
+template <class CFG, int NQ>
+__host__ __device__ constexpr int wide_rows_of() {
+    return CFG::STAGE / (16 * CFG::T * NQ) < 1 ? 1
+         : CFG::STAGE / (16 * CFG::T * NQ) > kWMaxR ? kWMaxR : CFG::STAGE / (16 * CFG::T * NQ);
+}
 constexpr int kWFix = 1024;            // exactly recomputed columns per slice merge (cap)
 constexpr float kRaiseW = 60.0f;
 constexpr float kTinyW = 8.077935669463161e-28f;   // 2^-90
@@ -126,6 +133,7 @@ __device__ float w_exact_column(const float* X, const float* u2, float kinv, int
 template <class CFG, int NQ, bool FULL>
 __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a) {
     constexpr int NC = 4 * NQ, kWT = CFG::T, kWW = CFG::W, kWStage = CFG::STAGE, kWS = CFG::S;
+    constexpr int RM = wide_rows_of<CFG, NQ>();   // rows per batch (the host passes a.R == RM)
     constexpr int kP = kWC * kWW;   // pairs per row of a batch: one per warp of the cluster
     constexpr int kPL = kP / 32;    // pairs per lane in the merge
     static_assert(kP % 32 == 0, "warps per cluster must be a multiple of 32");
@@ -133,6 +141,8 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
     float2* xch = reinterpret_cast<float2*>(smem + size_t(kWS) * kWStage);   // [kWX][R][kP]
     __shared__ __align__(8) uint64_t full[kWS];   // a stage's rows have landed (bulk-copy bytes)
     __shared__ __align__(8) uint64_t xbar[kWX];   // a batch's row pairs from every warp of the cluster have landed
+    __shared__ __align__(8) uint64_t ubar[kWX];   // a batch's u is in s_uv
+    __shared__ float s_uv[kWX][kWMaxR];
     __shared__ unsigned s_rel[kWS];               // warps done with a stage (wrapping counter)
     __shared__ int s_flag, s_nfix, s_next, s_kfail;
     __shared__ volatile int s_abort;              // a bounded wait expired: stop copying and waiting
@@ -183,7 +193,10 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
             s_rel[k] = 0u;
         }
 #pragma unroll
-        for (int k = 0; k < kWX; ++k) mbar_init(&xbar[k], 1);
+        for (int k = 0; k < kWX; ++k) {
+            mbar_init(&xbar[k], 1);
+            mbar_init(&ubar[k], 1);
+        }
         s_abort = 0;
         s_nfix = 0;
         s_next = g0;
@@ -198,8 +211,9 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
 
     float vr[NC], cS[NC];
     float A = kNegBig;               // warp-wide column reference
-    float tmc[kWMaxR], tmp[kWMaxR];  // warp row maxima: current batch, pending batch
-    float uw[kWMaxR];                // u of the pending batch's rows
+    float tmc[RM], tmp[RM];  // warp row maxima: current batch, pending batch
+    float crc[RM], crp[RM];  // their rounding remainders (mx*log2e - round(mx*log2e))
+    float uw[RM];            // u of the pending batch's rows
     int cur = -1, pend = -1;
 
     auto load_v = [&](int b) {
@@ -219,32 +233,44 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
     };
 
     // u of batch gp's rows from the kP pairs of each row (every warp of the
-    // cluster sent one): max over the lanes, then the rescaled sums added in
-    // a fixed order, so every warp of every CTA gets the same value.  Warp 0
-    // writes it out, before its CTA's flush arrival.
+    // cluster sent one), merged by one warp of the CTA (rotating with gp): max
+    // over the lanes, then the rescaled sums added in a fixed order, so every
+    // CTA gets the same value.  It is published in s_uv behind ubar; the
+    // merging warp writes it out before its CTA's flush arrival.
     auto take_u = [&](int gp, int rp, int64_t grow0) {
-        wait_pairs(gp);
-        const float2* xs = xch + xidx(gp) * a.R * kP;
+        const int slot = xidx(gp);
+        if (wid == (gp - g0) % kWW) {
+            wait_pairs(gp);
+            const float2* xs = xch + slot * a.R * kP;
 #pragma unroll
-        for (int ir = 0; ir < kWMaxR; ++ir) {
-            if (ir < rp) {
-                float2 q[kPL];
-                float ml = kNegBig;
+            for (int ir = 0; ir < RM; ++ir) {
+                if (ir < rp) {
+                    float2 q[kPL];
+                    float ml = kNegBig;
 #pragma unroll
-                for (int k = 0; k < kPL; ++k) {
-                    q[k] = xs[ir * kP + lane + 32 * k];
-                    ml = fmaxf(ml, q[k].x);
+                    for (int k = 0; k < kPL; ++k) {
+                        q[k] = xs[ir * kP + lane + 32 * k];
+                        ml = fmaxf(ml, q[k].x);
+                    }
+                    const float mm = warp_max<32>(ml);
+                    float sl = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < kPL; ++k) sl = fmaf(q[k].y, exp_shift(q[k].x - mm), sl);
+                    const float ss = warp_sum<32>(sl);
+                    if (lane == 0) {
+                        const int64_t grow = grow0 + ir;
+                        const float u = (a.la ? __ldg(a.la + grow) : a.la_def) - lse_finish(mm, ss);
+                        s_uv[slot][ir] = u;
+                        a.u2[grow] = u;
+                    }
                 }
-                const float mm = warp_max<32>(ml);
-                float sl = 0.0f;
-#pragma unroll
-                for (int k = 0; k < kPL; ++k) sl = fmaf(q[k].y, exp_shift(q[k].x - mm), sl);
-                const float ss = warp_sum<32>(sl);
-                const int64_t grow = grow0 + ir;
-                uw[ir] = (a.la ? __ldg(a.la + grow) : a.la_def) - lse_finish(mm, ss);
-                if (wid == 0 && lane == 0) a.u2[grow] = uw[ir];
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ubar[slot]);
         }
+        if (!s_abort && !mbar_wait_mode(&ubar[slot], xphase(gp), a.wmode, false, a.err)) s_abort = 1;
+#pragma unroll
+        for (int ir = 0; ir < RM; ++ir) uw[ir] = s_uv[slot][ir];
     };
 
     // column update of batch gp (E in its stage, u in uw); the last warp
@@ -253,7 +279,7 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
         const float* es = stage(gp);
         if (!s_abort) {
 #pragma unroll
-            for (int ir = 0; ir < kWMaxR; ++ir) {
+            for (int ir = 0; ir < RM; ++ir) {
                 if (ir < rows) {
                     const float ai = tmp[ir] + uw[ir];   // warp-uniform
                     if (ai > A + kRaiseW) {
@@ -262,7 +288,7 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
                         for (int e = 0; e < NC; ++e) cS[e] *= sc;
                         A = ai;
                     }
-                    const float w = exp_shift(ai - A);
+                    const float w = ex2(fmaf(ai - A, kLog2e, -crp[ir]));   // exp(ai - A) / 2^cr
 #pragma unroll
                     for (int q = 0; q < NQ; ++q) {
                         if (live(q)) {
@@ -366,9 +392,10 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
         // ---- pass A: row partials of this warp's columns; E written in place ----
         float* xs = stage(g);
 #pragma unroll
-        for (int ir = 0; ir < kWMaxR; ++ir) {
+        for (int ir = 0; ir < RM; ++ir) {
             if (ir < rows) {
                 float mx = kNegBig, s = 0.0f;
+                crc[ir] = 0.0f;
                 if (ok) {
                     float t[NC];
 #pragma unroll
@@ -385,9 +412,16 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
                         }
                     }
                     mx = warp_max<32>(fmaxf(mx, tree_max(t)));
+                    // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e
+                    // rounded; every term carries 2^cr, cr = mx*log2e - mL exactly
+                    // (FMA remainder), taken out of the sum here and out of the
+                    // column weight in pass B
+                    const float mxc = fmaxf(mx, -1.0e37f);   // a row of -inf terms keeps mL finite
+                    const float mL = mxc * kLog2e;
+                    crc[ir] = fmaf(mxc, kLog2e, -mL);
 #pragma unroll
-                    for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
-                    s = warp_sum<32>(tree_sum(t));
+                    for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));
+                    s = warp_sum<32>(tree_sum(t)) * ex2(-crc[ir]);
 #pragma unroll
                     for (int q = 0; q < NQ; ++q) {
                         if (live(q))
@@ -408,7 +442,10 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
             pass_b(pend, prows);
         }
 #pragma unroll
-        for (int ir = 0; ir < kWMaxR; ++ir) tmp[ir] = tmc[ir];
+        for (int ir = 0; ir < RM; ++ir) {
+            tmp[ir] = tmc[ir];
+            crp[ir] = crc[ir];
+        }
         pend = g;
         prows = rows;
         pgrow0 = grow0;
@@ -539,10 +576,14 @@ int max_clusters(int shape, int R) {
     return ncl;
 }
 
-// Rows per batch: as many rows of the CTA's slice as one stage holds (<= 4).
+// Rows per batch of the shape for slices of mc columns (wide_rows_of).
 int wide_rows(int64_t mc) {
-    const int64_t stage = wide_shape(mc) == kShapeA ? WideA::STAGE : WideB::STAGE;
-    return int(std::max<int64_t>(1, std::min<int64_t>(kWMaxR, stage / (mc * 4))));
+    if (wide_shape(mc) == kShapeA) {
+        const int q = nq_of<WideA>(mc);
+        return q == 1 ? wide_rows_of<WideA, 1>() : q == 2 ? wide_rows_of<WideA, 2>() : wide_rows_of<WideA, 4>();
+    }
+    const int q = nq_of<WideB>(mc);
+    return q == 1 ? wide_rows_of<WideB, 1>() : q == 2 ? wide_rows_of<WideB, 2>() : wide_rows_of<WideB, 4>();
 }
 
 struct WidePlan {
