@@ -434,7 +434,7 @@ int bs_bwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int
 
 }  // namespace
 
-// fused passes (bidir_fused.cu) for L2 <= 1024, L2 % 4 == 0
+// streaming sweeps (bidir_stream.cu) for L2 <= 1024, L2 % 4 == 0
 bool bsf_supported(int64_t B, int64_t L1, int64_t L2, int dtype, const void* sim, const void* gout, const void* dst,
                    int dst_dtype);
 size_t bsf_fwd_ws(int64_t B, int64_t L1, int64_t L2);
