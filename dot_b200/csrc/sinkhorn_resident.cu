@@ -148,6 +148,17 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
 
     for (int64_t j = tid; j < C::CW; j += C::T) S.v[j] = 0.0f;
     if (!load_tile(S.tile, a.X + b * n * m, n, m, &bar, err)) return;
+    // the tile holds K = X * kinv from here on (rounded once, as the reference
+    // materialises log_K); the cost epilogue re-reads X
+    for (int64_t q = tid; q < (n * m) >> 2; q += C::T) {
+        float4 x = reinterpret_cast<float4*>(S.tile)[q];
+        x.x = __fmul_rn(x.x, a.kinv);
+        x.y = __fmul_rn(x.y, a.kinv);
+        x.z = __fmul_rn(x.z, a.kinv);
+        x.w = __fmul_rn(x.w, a.kinv);
+        reinterpret_cast<float4*>(S.tile)[q] = x;
+    }
+    __syncthreads();
 
     auto colof = [&](int p) { return 4 * gl + 4 * LPR * p; };
     const int nslots = int((n + C::ROWS_PER_SLOT - 1) / C::ROWS_PER_SLOT);
@@ -177,28 +188,28 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
             for (int p = 0; p < VPL; ++p) {
                 const int col = colof(p);
                 if (rok && col < m) {
-                    const float4 x = *reinterpret_cast<const float4*>(S.tile + i * m + col);
-                    t[4 * p + 0] = kplus(x.x, a.kinv, vr[4 * p + 0]);
-                    t[4 * p + 1] = kplus(x.y, a.kinv, vr[4 * p + 1]);
-                    t[4 * p + 2] = kplus(x.z, a.kinv, vr[4 * p + 2]);
-                    t[4 * p + 3] = kplus(x.w, a.kinv, vr[4 * p + 3]);
+                    const float4 k4 = *reinterpret_cast<const float4*>(S.tile + i * m + col);
+                    t[4 * p + 0] = __fadd_rn(k4.x, vr[4 * p + 0]);
+                    t[4 * p + 1] = __fadd_rn(k4.y, vr[4 * p + 1]);
+                    t[4 * p + 2] = __fadd_rn(k4.z, vr[4 * p + 2]);
+                    t[4 * p + 3] = __fadd_rn(k4.w, vr[4 * p + 3]);
                 } else {
                     t[4 * p + 0] = t[4 * p + 1] = t[4 * p + 2] = t[4 * p + 3] = -INFINITY;
                 }
             }
+            mx = group_max<LPR>(fmaxf(mx, tree_max(t)));
+            // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e rounded;
+            // every term carries 2^cr, cr = mx*log2e - mL exactly (FMA
+            // remainder), taken out of the row LSE and the column weight
+            const float mxc = fmaxf(mx, -1.0e37f);   // a row of -inf terms keeps mL finite
+            const float mL = mxc * kLog2e;
+            const float cr = fmaf(mxc, kLog2e, -mL);
 #pragma unroll
-            for (int e = 0; e < NC; ++e) mx = fmaxf(mx, t[e]);
-            mx = group_max<LPR>(mx);
-            float s = 0.0f;
-#pragma unroll
-            for (int e = 0; e < NC; ++e) {
-                t[e] = exp_shift(t[e] - mx);
-                s += t[e];
-            }
-            s = group_sum<LPR>(s);
+            for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));
+            const float s = group_sum<LPR>(tree_sum(t));
             float ai = -INFINITY;
             if (rok) {
-                const float unew = (la ? la[i] : a.la_def) - lse_finish(mx, s);
+                const float unew = (la ? la[i] : a.la_def) - (mx + (logf(fmaxf(s, kSumFloor)) - cr * kLn2));
                 if (gl == 0) S.u[i] = unew;
                 ai = mx + unew;
             }
@@ -209,7 +220,7 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
                 for (int e = 0; e < NC; ++e) cs[e] *= sc;
                 A = amax;
             }
-            const float w = exp_shift(ai - A);
+            const float w = ex2(fmaf(ai - A, kLog2e, -cr));   // exp(ai - A) / 2^cr
 #pragma unroll
             for (int e = 0; e < NC; ++e) cs[e] = fmaf(t[e], w, cs[e]);
         }
@@ -247,10 +258,10 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
         for (int k = wid; k < nfix; k += W) {   // exact column LSE from the resident tile
             const int64_t j = S.fix[k];
             float mx = kNegBig;
-            for (int64_t i = lane; i < n; i += 32) mx = fmaxf(mx, kplus(S.tile[i * m + j], a.kinv, S.u[i]));
+            for (int64_t i = lane; i < n; i += 32) mx = fmaxf(mx, __fadd_rn(S.tile[i * m + j], S.u[i]));
             mx = warp_max<32>(mx);
             float sm = 0.0f;
-            for (int64_t i = lane; i < n; i += 32) sm += exp_shift(kplus(S.tile[i * m + j], a.kinv, S.u[i]) - mx);
+            for (int64_t i = lane; i < n; i += 32) sm += exp_shift(__fadd_rn(S.tile[i * m + j], S.u[i]) - mx);
             sm = warp_sum<32>(sm);
             if (lane == 0) S.v[j] = (lb ? lb[j] : a.lb_def) - lse_finish(mx, sm);
         }
@@ -265,20 +276,24 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
     __syncthreads();
     float acc = 0.0f;
     float* outb = a.out + b * n * m;
+    const float4* xg = reinterpret_cast<const float4*>(a.X + b * n * m);
     const int64_t nm4 = (n * m) >> 2;
     for (int64_t q = tid; q < nm4; q += C::T) {
         const int64_t e0 = q * 4;
         const int64_t i = e0 / m, j = e0 - i * m;
-        const float4 x = *reinterpret_cast<const float4*>(S.tile + e0);
+        const float4 k4 = *reinterpret_cast<const float4*>(S.tile + e0);
         const float uu = S.u[i];
-        const float t0 = __fadd_rn(kplus(x.x, a.kinv, uu), S.v[j + 0]);
-        const float t1 = __fadd_rn(kplus(x.y, a.kinv, uu), S.v[j + 1]);
-        const float t2 = __fadd_rn(kplus(x.z, a.kinv, uu), S.v[j + 2]);
-        const float t3 = __fadd_rn(kplus(x.w, a.kinv, uu), S.v[j + 3]);
+        const float t0 = __fadd_rn(__fadd_rn(k4.x, uu), S.v[j + 0]);
+        const float t1 = __fadd_rn(__fadd_rn(k4.y, uu), S.v[j + 1]);
+        const float t2 = __fadd_rn(__fadd_rn(k4.z, uu), S.v[j + 2]);
+        const float t3 = __fadd_rn(__fadd_rn(k4.w, uu), S.v[j + 3]);
         float4 o;
         if (a.out_mode == 0) {
             o = make_float4(safe_expf(t0), safe_expf(t1), safe_expf(t2), safe_expf(t3));
-            acc += o.x * x.x + o.y * x.y + o.z * x.z + o.w * x.w;
+            if (a.cost != nullptr) {
+                const float4 x = __ldg(xg + q);
+                acc += o.x * x.x + o.y * x.y + o.z * x.z + o.w * x.w;
+            }
         } else {
             o = make_float4(t0, t1, t2, t3);
         }
@@ -332,7 +347,7 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int
     };
 
     // ---- invariants: row (sum_k P G, sum_k P), column (sum_i P G, sum_i P)
-    float rPG[MAXSLOTS], rP[MAXSLOTS];
+    float rPG[MAXSLOTS], rP[MAXSLOTS];   // rP: 1 / max(sum_k P, 1e-12)
     float cPG[NC], cP[NC];
 #pragma unroll
     for (int e = 0; e < NC; ++e) { cPG[e] = 0.0f; cP[e] = 0.0f; }
@@ -361,7 +376,7 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int
             }
         }
         rPG[sl] = group_sum<LPR>(spg);
-        rP[sl] = group_sum<LPR>(sp);
+        rP[sl] = 1.0f / fmaxf(group_sum<LPR>(sp), kSumFloor);   // reciprocal of the row denominator
     }
     // column invariants: reduce over groups, then over warps through S.part
     float* cinv_pg = S.part;
@@ -398,7 +413,7 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int
         float s = 0.0f;
 #pragma unroll
         for (int w = 0; w < W; ++w) s += cinv_pg[w * C::CW + j];
-        s_cp[j] = s;
+        s_cp[j] = 1.0f / fmaxf(s, kSumFloor);   // reciprocal of the column denominator
     }
     __syncthreads();
 
@@ -434,11 +449,11 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int
                     pv[4 * p + 0] = pv[4 * p + 1] = pv[4 * p + 2] = pv[4 * p + 3] = 0.0f;
                 }
             }
-            float s = 0.0f;
+            float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four independent chains
 #pragma unroll
-            for (int e = 0; e < NC; ++e) s += pv[e] * mr[e];
-            s = group_sum<LPR>(s);
-            const float l = rok ? (rPG[sl] - s) / fmaxf(rP[sl], kSumFloor) : 0.0f;
+            for (int e = 0; e < NC; ++e) sq[e & 3] = fmaf(pv[e], mr[e], sq[e & 3]);
+            const float s = group_sum<LPR>((sq[0] + sq[1]) + (sq[2] + sq[3]));
+            const float l = rok ? (rPG[sl] - s) * rP[sl] : 0.0f;
             if (rok && gl == 0) lam[i] = l;
 #pragma unroll
             for (int e = 0; e < NC; ++e) acc[e] += pv[e] * l;
@@ -456,7 +471,7 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int
             float s = 0.0f;
 #pragma unroll
             for (int w = 0; w < W; ++w) s += S.part[w * C::CW + j];
-            mu[j] = (s_cpg[j] - s) / fmaxf(s_cp[j], kSumFloor);
+            mu[j] = (s_cpg[j] - s) * s_cp[j];
         }
         __syncthreads();
     }
