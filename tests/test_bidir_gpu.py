@@ -69,8 +69,8 @@ CASES = [
     (2, 129, 127, 0.05, None),
     (1, 1300, 40, 0.2, [[1250, 33]]),   # tall: column statistics span several row chunks
     (2, 64, 1024, 0.1, None),
-    # cluster path (L2 <= 1024, L2 % 4 == 0): fewer rows than CTAs per cluster,
-    # ragged and empty windows, more problems than resident clusters
+    # streaming path (L2 <= 1024, L2 % 4 == 0): fewer rows than row slots,
+    # ragged and empty windows, more problems than resident CTAs
     (5, 3, 64, 0.5, None),
     (4, 37, 256, 0.2, [[37, 256], [30, 200], [1, 8], [0, 0]]),
     (300, 16, 96, 0.3, None),
@@ -98,7 +98,7 @@ def test_oracle_and_fp64_parity(B, L1, L2, tau, lengths):
 
 @pytest.mark.parametrize("B,L1,L2,lengths", [(3, 45, 136, [[45, 136], [20, 64], [45, 7]]), (2, 9, 1024, None)])
 def test_bf16_input_against_oracle(B, L1, L2, lengths):
-    """bf16 input on the cluster path: the oracle runs on the same bf16 values
+    """bf16 input on the streaming path: the oracle runs on the same bf16 values
     upcast to fp32 (the reference's own cast); the bf16 gradient is compared
     within one bf16 rounding."""
     g = U.gen(L1 * 11 + L2)
@@ -152,6 +152,28 @@ def test_cfg3_full_size(dtype):
         else:
             ref_bf = torch.from_numpy(ref["grad"]).bfloat16().float()
             U.assert_normwise(s.grad[bi:bi + 1].float(), ref_bf, 1e-2, f"grad[{bi}]")
+
+
+def test_multi_chunk_ragged():
+    """Ragged windows on rows split over two warps (L2 = 1024), 14 problems
+    spread over the persistent CTAs' ranges (problems shared by several CTAs
+    and merged by the last to arrive): a sample of them against the oracle."""
+    B = 14
+    g = U.gen(14)
+    sim = torch.randn(B, 1024, 1024, generator=g)
+    go = torch.randn(B, 1024, 1024, generator=g)
+    rng = np.random.default_rng(14)
+    ln = np.stack([rng.integers(1, 1025, B), rng.integers(1, 1025, B)], 1).astype(np.int32)
+    ln[3] = [1024, 1024]
+    out, grad = run(sim, 0.1, ln, go)
+    for bi in (0, 5, 6, 11, 12, 13):
+        ref = O.bidir_api(sim[bi:bi + 1].numpy(), 0.1, ln[bi:bi + 1], go[bi:bi + 1].numpy())
+        assert np.abs(U.to_np(out[bi:bi + 1]) - ref["out"]).max() <= OUT_ATOL
+        U.assert_normwise(out[bi:bi + 1], ref["out"], U.PLAN_RTOL, f"out[{bi}]")
+        U.assert_normwise(grad[bi:bi + 1], ref["grad"], U.GRAD_RTOL, f"grad[{bi}]")
+        l1, l2 = ln[bi]
+        assert (out[bi, l1:, :] == 0).all() and (out[bi, :, l2:] == 0).all()
+        assert (grad[bi, l1:, :] == 0).all() and (grad[bi, :, l2:] == 0).all()
 
 
 def test_deterministic_bitwise():
