@@ -31,6 +31,8 @@
 // values bit for bit.  Each sweep reads its inputs once (the output sweeps
 // re-read sim: 1.5x / 1.67x the compulsory bytes of the two directions) and
 // runs at streaming bandwidth instead of holding whole problems in flight.
+// The second sweep of a direction is a programmatic dependent launch: it sets
+// up and starts copying sim while the first finishes.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -266,6 +268,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
     if (tid == 0) s_nfix = 0;
+    pdl_launch_dependents();   // the second sweep may start its copies of the read-only input
     const Ring rg = ring_start(a, bars, smem);
     const T* simT = reinterpret_cast<const T*>(a.sim);
 
@@ -433,6 +436,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
     const Ring rg = ring_start(a, bars, smem);
+    pdl_wait();   // the first sweep's statistics / dots are complete and visible
     int64_t l1 = 0, l2 = 0;
     int b = rg.g0 / a.s.nblk, jb = rg.g0 - b * a.s.nblk;
     int cur = -1;
@@ -501,6 +505,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
+    pdl_launch_dependents();   // the second sweep may start its copies of the read-only input
     const Ring rg = ring_start(a, bars, smem);
 
     float Sd[NC];
@@ -621,6 +626,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
     const Ring rg = ring_start(a, bars, smem);
+    pdl_wait();   // the first sweep's statistics / dots are complete and visible
     int64_t l1 = 0, l2 = 0;
     int b = rg.g0 / a.s.nblk, jb = rg.g0 - b * a.s.nblk;
     int cur = -1;
@@ -838,6 +844,24 @@ SweepArgs sweep_args(const void* sim, int esz, const int32_t* lengths, int64_t B
     return a;
 }
 
+// Launch of a second sweep with programmatic dependent launch: its CTAs may
+// start (barrier set-up, first copies of the read-only input) while the first
+// sweep finishes; they wait for it before reading its results.
+template <typename K, typename... Args>
+void launch_dependent(K kernel, int grid, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(kT);
+    cfg.dynamicSmemBytes = sweep_smem();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename T, int VPL>
 int fwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int64_t L2, float tau, float* out,
              float2* rstat, float2* cstat, void* ws, cudaStream_t st) {
@@ -856,7 +880,7 @@ int fwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int64_
     cudaFuncSetAttribute(bs2_out_kernel<T, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sweep_smem()));
     ProfScope ps(DOT_K_BS_FWD, st, 2);
     bs2_stats_kernel<T, VPL><<<unsigned(a.s.G), kT, sweep_smem(), st>>>(a);
-    bs2_out_kernel<T, VPL><<<unsigned(a.s.G), kT, sweep_smem(), st>>>(a);
+    launch_dependent(bs2_out_kernel<T, VPL>, a.s.G, st, a);
     return check_launch("bidirectional softmax forward");
 }
 
@@ -882,7 +906,7 @@ int bwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int64_
     {
         ProfScope ps(DOT_K_BS_BWD, st, 2);
         bs2_dots_kernel<T, VPL><<<unsigned(a.s.G), kT, sweep_smem(), st>>>(a);
-        bs2_grad_kernel<T, G, VPL><<<unsigned(a.s.G), kT, sweep_smem(), st>>>(a, gsim);
+        launch_dependent(bs2_grad_kernel<T, G, VPL>, a.s.G, st, a, gsim);
     }
     if (gtau != nullptr) {
         ProfScope ps(DOT_K_BS_BWD, st);
