@@ -32,7 +32,9 @@
 // re-read sim: 1.5x / 1.67x the compulsory bytes of the two directions) and
 // runs at streaming bandwidth instead of holding whole problems in flight.
 // The second sweep of a direction is a programmatic dependent launch: it sets
-// up and starts copying sim while the first finishes.
+// up and starts copying sim while the first finishes.  The output and dot
+// sweeps need only row * col, which they take from one exponential,
+// exp(2v - rmax - cmax); the gradient sweep uses row and col apart.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -330,16 +332,21 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
             const float mx = warp_max<32>(tree_max(t));
             float s = 0.0f;
             if (mx != -INFINITY) {   // warp-uniform; else every column of this warp's part is masked
+                // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e rounded;
+                // every term carries 2^cr, cr = mx*log2e - mL exactly (FMA
+                // remainder), taken out of the row sum and the column weight
+                const float mL = mx * kLog2e;
+                const float cr = fmaf(mx, kLog2e, -mL);
 #pragma unroll
-                for (int e = 0; e < NC; ++e) t[e] = exp_shift(t[e] - mx);
-                s = warp_sum<32>(tree_sum(t));
+                for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));
+                s = warp_sum<32>(tree_sum(t)) * ex2(-cr);
                 if (mx > A + kRaiseB) {
                     const float sc = exp_shift(A - mx);
 #pragma unroll
                     for (int e = 0; e < NC; ++e) Sc[e] *= sc;
                     A = mx;
                 }
-                const float w = exp_shift(mx - A);
+                const float w = ex2(fmaf(mx - A, kLog2e, -cr));   // exp(mx - A) / 2^cr
 #pragma unroll
                 for (int e = 0; e < NC; ++e) Sc[e] = fmaf(t[e], w, Sc[e]);
             }
@@ -429,7 +436,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
     constexpr int WPR = W::WPR, VPLW = W::VPLW, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's column statistics
+    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's columns: (cmax * log2 e, 1/sum)
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int slot = wid / WPR, cpart = wid % WPR;
@@ -445,7 +452,10 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
         if (b != cur) {   // the barrier below orders these writes before their reads
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
-            for (int64_t col = tid; col < L2; col += kT) s_cs[col] = __ldg(a.cstat + int64_t(b) * L2 + col);
+            for (int64_t col = tid; col < L2; col += kT) {
+                const float2 c = __ldg(a.cstat + int64_t(b) * L2 + col);
+                s_cs[col] = make_float2(c.x * kLog2e, c.y);
+            }
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
         const bool ok = rg.wait(g);
@@ -460,6 +470,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
             float* orow = a.out + row * L2;
             const bool live = i < l1;
             const float2 rs = live ? __ldg(a.rstat + row) : make_float2(0.0f, 0.0f);
+            const float rmL = rs.x * kLog2e;
 #pragma unroll
             for (int p = 0; p < VPLW; ++p) {
                 const int64_t col = cbase + 4 * lane + 128 * p;
@@ -472,8 +483,17 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
                         ld_cs4(s_cs + col, cs);
                         const bool whole = col + 3 < l2;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            if (whole || col + e < l2) o[e] = bs_vals(__fmul_rn(v[e], a.invT), rs, cs[e]).out;
+                        for (int e = 0; e < 4; ++e) {
+                            if (whole || col + e < l2) {
+                                // row * col = exp(2v - rmax - cmax) * rinv * cinv: one
+                                // exponential (the gradient sweep needs row and col
+                                // apart and keeps bs_vals)
+                                const float val = __fmul_rn(v[e], a.invT);
+                                const float rc = ex2(fmaf(val, 2.0f * kLog2e, -rmL) - cs[e].x) * rs.y * cs[e].y;
+                                const float x = 1e-9f + rc;
+                                o[e] = fminf(x * rsqrt_approx(x), 1.0f);
+                            }
+                        }
                     }
                     st4g(orow + col, o);
                 }
@@ -497,7 +517,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     constexpr int WPR = W::WPR, VPLW = W::VPLW, NC = W::NC, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's column statistics
+    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's columns: (cmax * log2 e, 1/sum)
     __shared__ float s_rd[kMaxR][WPR];               // per-row q sums of the row's warps
     __shared__ int s_flag;
 
@@ -517,7 +537,10 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
         if (b != cur) {   // the barrier below orders these writes before their reads
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
-            for (int64_t col = tid; col < L2; col += kT) s_cs[col] = __ldg(a.cstat + int64_t(b) * L2 + col);
+            for (int64_t col = tid; col < L2; col += kT) {
+                const float2 c = __ldg(a.cstat + int64_t(b) * L2 + col);
+                s_cs[col] = make_float2(c.x * kLog2e, c.y);
+            }
 #pragma unroll
             for (int e = 0; e < NC; ++e) Sd[e] = 0.0f;
         }
@@ -534,6 +557,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
             float rd = 0.0f;
             if (i < l1) {   // warp-uniform
                 const float2 rs = __ldg(a.rstat + int64_t(b) * L1 + i);
+                const float rmL = rs.x * kLog2e;
 #pragma unroll
                 for (int p = 0; p < VPLW; ++p) {
                     const int64_t col = cbase + 4 * lane + 128 * p;
@@ -547,8 +571,13 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             if (whole || col + e < l2) {
-                                const BsVals q = bs_vals(__fmul_rn(v[e], a.invT), rs, cs[e]);
-                                const float qq = (gv[e] * 0.5f) * q.iout * q.rc;
+                                // q needs row * col only: exp(2v - rmax - cmax) *
+                                // rinv * cinv, one exponential
+                                const float val = __fmul_rn(v[e], a.invT);
+                                const float rc =
+                                    ex2(fmaf(val, 2.0f * kLog2e, -rmL) - cs[e].x) * rs.y * cs[e].y;
+                                const float iout = fmaxf(rsqrt_approx(1e-9f + rc), 1.0f);
+                                const float qq = (gv[e] * 0.5f) * iout * rc;
                                 rd += qq;
                                 Sd[4 * p + e] += qq;
                             }

@@ -338,21 +338,51 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
         __syncthreads();
         if (s_flag == 0) return;
         __threadfence();
-        for (int64_t lc = tid; lc < mc; lc += kWT) {
-            float mm = kNegBig, ss = 0.0f;
-            for (int sg = 0; sg < nseg; ++sg) {
-                const float2 pp = __ldcg(a.part + (int64_t(b) * a.maxseg + sg) * m + cbase + lc);
-                lse_merge(mm, ss, pp.x, pp.y);
+        // the slice's columns over the segments in order: max pass, then the
+        // rescaled sums (one exponential per partial); four columns per thread
+        // at a time, so four independent chains are in flight
+        const float2* pb = a.part + int64_t(b) * a.maxseg * m + cbase;
+        constexpr int kCols = 4;
+        for (int64_t lc0 = tid; lc0 < mc; lc0 += kCols * kWT) {
+            float mm[kCols], ss[kCols];
+#pragma unroll
+            for (int c = 0; c < kCols; ++c) {
+                mm[c] = kNegBig;
+                ss[c] = 0.0f;
             }
-            const int64_t col = cbase + lc;
-            if (a.pairs != nullptr) {
-                a.pairs[int64_t(b) * m + col] = make_float2(mm, ss);
-            } else if (ss < kTinyW) {
-                const int k = atomicAdd(&s_nfix, 1);
-                if (k < kWFix) s_fix[k] = int(lc);
-                else a.v2[int64_t(b) * m + col] = (a.lb ? a.lb[int64_t(b) * m + col] : a.lb_def) - lse_finish(mm, ss);
-            } else {
-                a.v2[int64_t(b) * m + col] = (a.lb ? a.lb[int64_t(b) * m + col] : a.lb_def) - lse_finish(mm, ss);
+            for (int sg = 0; sg < nseg; ++sg) {
+#pragma unroll
+                for (int c = 0; c < kCols; ++c) {
+                    const int64_t lc = lc0 + int64_t(c) * kWT;
+                    if (lc < mc) mm[c] = fmaxf(mm[c], __ldcg(pb + int64_t(sg) * m + lc).x);
+                }
+            }
+            for (int sg = 0; sg < nseg; ++sg) {
+#pragma unroll
+                for (int c = 0; c < kCols; ++c) {
+                    const int64_t lc = lc0 + int64_t(c) * kWT;
+                    if (lc < mc) {
+                        const float2 pp = __ldcg(pb + int64_t(sg) * m + lc);
+                        ss[c] = fmaf(pp.y, exp_shift(pp.x - mm[c]), ss[c]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < kCols; ++c) {
+                const int64_t lc = lc0 + int64_t(c) * kWT;
+                if (lc >= mc) continue;
+                const int64_t col = cbase + lc;
+                if (a.pairs != nullptr) {
+                    a.pairs[int64_t(b) * m + col] = make_float2(mm[c], ss[c]);
+                } else if (ss[c] < kTinyW) {
+                    const int k = atomicAdd(&s_nfix, 1);
+                    if (k < kWFix) s_fix[k] = int(lc);
+                    else a.v2[int64_t(b) * m + col] = (a.lb ? a.lb[int64_t(b) * m + col] : a.lb_def) -
+                                                      lse_finish(mm[c], ss[c]);
+                } else {
+                    a.v2[int64_t(b) * m + col] = (a.lb ? a.lb[int64_t(b) * m + col] : a.lb_def) -
+                                                 lse_finish(mm[c], ss[c]);
+                }
             }
         }
         if (tid == 0) a.cnt[int64_t(b) * kWC + rank] = 0;
