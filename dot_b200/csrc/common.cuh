@@ -34,6 +34,16 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// ln(x) from the SFU's base-2 log (lg2.approx, absolute error about 2^-22 in
+// log2 over the normal range), for a row sum in [1, m]: the sum of a row's
+// exp(t - max), whose largest term is 1.  Accurate log-sum-exps elsewhere use
+// lse_finish.
+__device__ __forceinline__ float fast_log(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y * 0.6931471805599453f;
+}
+
 // exp(d) for a shifted difference d <= 0 inside a log-sum-exp.
 __device__ __forceinline__ float exp_shift(float d) { return ex2(d * kLog2e); }
 

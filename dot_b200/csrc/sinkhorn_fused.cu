@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));   // t now holds E_ij * 2^cr
             const float s = warp_sum<32>(tree_sum(t));
             const int64_t grow = grow0 + i;
-            const float unew = lar[q] - (mx + (logf(fmaxf(s, kSumFloor)) - cr * kLn2));
+            const float unew = lar[q] - (mx + (fast_log(fmaxf(s, kSumFloor)) - cr * kLn2));
             if (lane == 0) {
                 if (tolmode) dmax = fmaxf(dmax, fabsf(unew - __ldcg(a.u2 + grow)));
                 a.u2[grow] = unew;

@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
             const float s = group_sum<LPR>(tree_sum(t));
             float ai = -INFINITY;
             if (rok) {
-                const float unew = (la ? la[i] : a.la_def) - (mx + (logf(fmaxf(s, kSumFloor)) - cr * kLn2));
+                const float unew = (la ? la[i] : a.la_def) - (mx + (fast_log(fmaxf(s, kSumFloor)) - cr * kLn2));
                 if (gl == 0) S.u[i] = unew;
                 ai = mx + unew;
             }
