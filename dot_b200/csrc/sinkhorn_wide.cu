@@ -132,6 +132,7 @@ __device__ float w_exact_column(const float* X, const float* u2, float kinv, int
 
 template <class CFG, int NQ, bool FULL>
 __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a) {
+    pdl_launch_dependents();   // the next iteration may set up while this one runs
     constexpr int NC = 4 * NQ, kWT = CFG::T, kWW = CFG::W, kWStage = CFG::STAGE, kWS = CFG::S;
     constexpr int RM = wide_rows_of<CFG, NQ>();   // rows per batch (the host passes a.R == RM)
     constexpr int kP = kWC * kWW;   // pairs per row of a batch: one per warp of the cluster
@@ -208,6 +209,10 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
     w_wait();
     if (tid == 0)
         for (int g = g0; g < g1 && g < g0 + kWS; ++g) issue(g);
+    // programmatic dependent launch: the set-up and first copies of the
+    // (read-only) matrix above may overlap the previous kernel; v, u and the
+    // merge buffers are touched only after it has completed
+    pdl_wait();
 
     float vr[NC], cS[NC];
     float A = kNegBig;               // warp-wide column reference
@@ -502,7 +507,7 @@ template <class CFG>
 size_t wide_smem(int R) { return size_t(CFG::S) * CFG::STAGE + size_t(kWX) * R * kWC * CFG::W * sizeof(float2); }
 
 template <class CFG>
-cudaLaunchConfig_t wide_config(int grid, int R, cudaStream_t st, cudaLaunchAttribute* attr) {
+cudaLaunchConfig_t wide_config(int grid, int R, cudaStream_t st, cudaLaunchAttribute* attr, bool pdl = false) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid));
     cfg.blockDim = dim3(CFG::T);
@@ -514,6 +519,11 @@ cudaLaunchConfig_t wide_config(int grid, int R, cudaStream_t st, cudaLaunchAttri
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (pdl) {   // attr holds two entries
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
+    }
     return cfg;
 }
 
@@ -549,8 +559,8 @@ int nq_of(int64_t mc) {
 
 template <class CFG, int NQ>
 void launch_nq(const WideArgs& a, cudaStream_t st) {
-    cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = wide_config<CFG>(a.G * kWC, a.R, st, attr);
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = wide_config<CFG>(a.G * kWC, a.R, st, attr, true);
     if (a.mc == 4 * CFG::T * NQ) cudaLaunchKernelEx(&cfg, skw_iter_kernel<CFG, NQ, true>, a);
     else cudaLaunchKernelEx(&cfg, skw_iter_kernel<CFG, NQ, false>, a);
 }
