@@ -404,7 +404,7 @@ def run_ours(args, cfg: dict) -> None:
                        "per_rank_batch": cfg["B"],
                        "l2": "inputs larger than L2 (126 MB)" if units_per_step(cfg) // max(cfg.get("iters", 1), 1) * 4
                        > 126e6 else "small working set: L2-resident by design (on-chip solver)",
-                       "parallelism": (f"rows sharded x{world}, NCCL all-reduce of column (max,sum) partials "
+                       "parallelism": (f"rows sharded x{world}, NCCL all-gather of column (max, sum) pairs "
                                        "per iteration" if rowshard else
                                        f"batch-independent x{world} (no collective)")},
             "e2e": {"value": e2e_value, "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
