@@ -27,16 +27,14 @@
 //           gradient sweep: the same ring again, elementwise; per-row partials
 //           of sum grad * sim / T for the temperature gradient.
 // The statistics are (max, 1/sum); every sweep recomputes row, col and out
-// from sim and the statistics (the forms below agree to a few ulps), so
-// nothing of full size is stored between sweeps.  Each sweep reads its inputs
-// once (the output sweeps
+// from sim with the same expressions, so the backward sees the forward's
+// values bit for bit.  Each sweep reads its inputs once (the output sweeps
 // re-read sim: 1.5x / 1.67x the compulsory bytes of the two directions) and
 // runs at streaming bandwidth instead of holding whole problems in flight.
 // The second sweep of a direction is a programmatic dependent launch: it sets
 // up and starts copying sim while the first finishes.  The output and dot
 // sweeps need only row * col, which they take from one exponential,
-// exp(2v - rmax - cmax); the gradient sweep forms row and col apart, each
-// from one FFMA and one exponential.
+// exp(2v - rmax - cmax); the gradient sweep uses row and col apart.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -120,18 +118,29 @@ __device__ __forceinline__ void window(const int32_t* lengths, int64_t b, int64_
     l2 = min(max(int64_t(__ldg(lengths + 2 * b + 1)), int64_t(0)), L2);
 }
 
-// Per-element values from the statistics (max, 1/sum), with v = sim/T rounded
-// and the maxima pre-scaled by log2 e:
-//   row = 2^(v*log2e - rmax*log2e) * rinv, col likewise, rc = row * col,
-//   out = min(sqrt(1e-9 + rc), 1), iout = 1 / out,
-// the output and dot sweeps taking rc from one exponential,
-// 2^(2v*log2e - (rmax + cmax)*log2e) * rinv * cinv.  sqrt and 1/sqrt come
-// from one rsqrt (SFU, ~2^-22 relative).  The column value's numerator and its
-// share of the column sum (accumulated from the row exponentials) can differ
-// by an ulp, so rc may exceed 1 by rounding where one element dominates its
-// row and column; out is capped at 1, its exact-arithmetic bound.
-// out >= sqrt(1e-9) > 1e-9, so the reference's guard dp = 0 for out <= 1e-9
-// never applies.
+// Per-element values from the statistics, the same expressions in every sweep:
+//   row = exp(v - rmax) * rinv, col = exp(v - cmax) * cinv, rc = row * col,
+//   out = min(sqrt(1e-9 + rc), 1), iout = 1 / out.
+// sqrt and 1/sqrt come from one rsqrt (SFU, ~2^-22 relative).  The column
+// value's numerator exp(v - A) and its share of the column sum (accumulated
+// as E*w) can differ by an ulp, so rc may exceed 1 by rounding where one
+// element dominates its row and column; out is capped at 1, its
+// exact-arithmetic bound.  out >= sqrt(1e-9) > 1e-9, so the reference's guard
+// dp = 0 for out <= 1e-9 never applies.
+struct BsVals {
+    float row, col, rc, out, iout;
+};
+__device__ __forceinline__ BsVals bs_vals(float v, float2 rs, float2 cs) {
+    BsVals q;
+    q.row = exp_shift(v - rs.x) * rs.y;
+    q.col = exp_shift(v - cs.x) * cs.y;
+    q.rc = q.row * q.col;
+    const float x = 1e-9f + q.rc;
+    const float r = rsqrt_approx(x);
+    q.out = fminf(x * r, 1.0f);
+    q.iout = fmaxf(r, 1.0f);
+    return q;
+}
 
 // Exact column softmax statistics (max, 1/sum) over rows [0, l1) -- one warp.
 template <typename T>
@@ -477,7 +486,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
                         for (int e = 0; e < 4; ++e) {
                             if (whole || col + e < l2) {
                                 // row * col = exp(2v - rmax - cmax) * rinv * cinv: one
-                                // exponential
+                                // exponential (the gradient sweep needs row and col
+                                // apart and keeps bs_vals)
                                 const float val = __fmul_rn(v[e], a.invT);
                                 const float rc = ex2(fmaf(val, 2.0f * kLog2e, -rmL) - cs[e].x) * rs.y * cs[e].y;
                                 const float x = 1e-9f + rc;
@@ -637,7 +647,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
     constexpr int WPR = W::WPR, VPLW = W::VPLW, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's columns: (cmax * log2 e, 1/sum)
+    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's column statistics
     __shared__ float s_tp[kMaxR][WPR];               // per-row tau partials of the row's warps
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -654,10 +664,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
         if (b != cur) {   // the barrier below orders these writes before their reads
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
-            for (int64_t col = tid; col < L2; col += kT) {
-                const float2 c = __ldg(a.cstat + int64_t(b) * L2 + col);
-                s_cs[col] = make_float2(c.x * kLog2e, c.y);
-            }
+            for (int64_t col = tid; col < L2; col += kT) s_cs[col] = __ldg(a.cstat + int64_t(b) * L2 + col);
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
         const bool ok = rg.wait(g);
@@ -675,7 +682,6 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
             const bool live = i < l1;
             const float2 rs = live ? __ldg(a.rstat + row) : make_float2(0.0f, 0.0f);
             const float rd = live ? __ldg(a.rdot + row) : 0.0f;
-            const float rmL = rs.x * kLog2e;
             float acc = 0.0f;
 #pragma unroll
             for (int p = 0; p < VPLW; ++p) {
@@ -694,14 +700,9 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             if (whole || col + e < l2) {
-                                // row and col, each from one FFMA and one exponential
-                                const float val = __fmul_rn(v[e], a.invT);
-                                const float rw = ex2(fmaf(val, kLog2e, -rmL)) * rs.y;
-                                const float cl = ex2(fmaf(val, kLog2e, -cs[e].x)) * cs[e].y;
-                                const float rc = rw * cl;
-                                const float iout = fmaxf(rsqrt_approx(1e-9f + rc), 1.0f);
-                                const float qq = (gv[e] * 0.5f) * iout * rc;
-                                gr[e] = (2.0f * qq - rd * rw - cd[e] * cl) * a.invT;
+                                const BsVals q = bs_vals(__fmul_rn(v[e], a.invT), rs, cs[e]);
+                                const float qq = (gv[e] * 0.5f) * q.iout * q.rc;
+                                gr[e] = (2.0f * qq - rd * q.row - cd[e] * q.col) * a.invT;
                                 acc = fmaf(gr[e], v[e] * a.invT, acc);
                             }
                         }
