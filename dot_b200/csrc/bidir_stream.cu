@@ -26,15 +26,16 @@
 //           sums (rdot) and column partials (cdot, merged as above).
 //           gradient sweep: the same ring again, elementwise; per-row partials
 //           of sum grad * sim / T for the temperature gradient.
-// The statistics are (max, 1/sum); every sweep recomputes row, col and out
-// from sim with the same expressions, so the backward sees the forward's
-// values bit for bit.  Each sweep reads its inputs once (the output sweeps
-// re-read sim: 1.5x / 1.67x the compulsory bytes of the two directions) and
-// runs at streaming bandwidth instead of holding whole problems in flight.
-// The second sweep of a direction is a programmatic dependent launch: it sets
-// up and starts copying sim while the first finishes.  The output and dot
-// sweeps need only row * col, which they take from one exponential,
-// exp(2v - rmax - cmax); the gradient sweep uses row and col apart.
+// The statistics are (max, 1/sum); every sweep recomputes its values from
+// sim.  The output and dot sweeps need only row * col, which they take from
+// one exponential, exp(2v - rmax - cmax), with the same expression, so the dot
+// sweep sees the forward's out bit for bit; the gradient sweep needs row and
+// col apart and forms row * col from them (within a few ulp of the other
+// form).  Each sweep reads its inputs once (the output sweeps re-read sim:
+// 1.5x / 1.67x the compulsory bytes of the two directions) and runs at
+// streaming bandwidth instead of holding whole problems in flight.  The
+// second sweep of a direction is a programmatic dependent launch: it sets up
+// and starts copying sim while the first finishes.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -118,7 +119,7 @@ __device__ __forceinline__ void window(const int32_t* lengths, int64_t b, int64_
     l2 = min(max(int64_t(__ldg(lengths + 2 * b + 1)), int64_t(0)), L2);
 }
 
-// Per-element values from the statistics, the same expressions in every sweep:
+// Per-element values from the statistics (the gradient sweep):
 //   row = exp(v - rmax) * rinv, col = exp(v - cmax) * cinv, rc = row * col,
 //   out = min(sqrt(1e-9 + rc), 1), iout = 1 / out.
 // sqrt and 1/sqrt come from one rsqrt (SFU, ~2^-22 relative).  The column
