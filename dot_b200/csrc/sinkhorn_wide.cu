@@ -29,9 +29,12 @@
 // When its range leaves a problem, a CTA publishes its columns' partials;
 // the CTA that arrives last among the same-rank CTAs of every cluster that
 // touched the problem merges that column slice in cluster order (atomic
-// arrival counter, no waiting) and writes v -- or, for a row shard of a
-// larger problem, the merged (max, sum) pairs for the cross-GPU combine.
-// Columns whose merged sum is too small to trust are recomputed exactly.
+// arrival counter, no waiting) and writes v.  Columns whose merged sum is
+// too small to trust are recomputed exactly.  For a row shard of a larger
+// problem the kernel only publishes the partials: skw_pairs_merge_kernel
+// (every SM, one thread per column, the same arithmetic in the same order)
+// merges them into the (max, sum) pairs of the cross-GPU combine, so no
+// single CTA per slice runs the merge after the rest of the grid is done.
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -334,6 +337,7 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
                     mypart[4 * tid + 4 * kWT * q + e] = make_float2(A - vr[4 * q + e], cS[4 * q + e]);
             }
         }
+        if (a.pairs != nullptr) return;   // skw_pairs_merge_kernel merges them
         __threadfence();
         __syncthreads();
         if (tid == 0) {
@@ -377,9 +381,7 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
                 const int64_t lc = lc0 + int64_t(c) * kWT;
                 if (lc >= mc) continue;
                 const int64_t col = cbase + lc;
-                if (a.pairs != nullptr) {
-                    a.pairs[int64_t(b) * m + col] = make_float2(mm[c], ss[c]);
-                } else if (ss[c] < kTinyW) {
+                if (ss[c] < kTinyW) {
                     const int k = atomicAdd(&s_nfix, 1);
                     if (k < kWFix) s_fix[k] = int(lc);
                     else a.v2[int64_t(b) * m + col] = (a.lb ? a.lb[int64_t(b) * m + col] : a.lb_def) -
@@ -500,6 +502,44 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
             mbar_wait_sleep(&full[sidx(g)], sphase(g), nullptr);
     w_arrive();   // no CTA leaves while a peer may still store into its shared memory
     w_wait();
+}
+
+// Row-shard mode: merge the published column partials of every problem over
+// the clusters that touched it, in cluster order (max pass, then the
+// rescaled sums -- the arithmetic of the in-kernel slice merge), into the
+// (max, sum) pairs [B][m].  One thread per column; segment loads are issued
+// eight at a time so a thread waits on L2 about nseg/4 times in all.
+constexpr int kMT = 128;   // threads per merge CTA
+constexpr int kMU = 8;     // segment loads in flight per thread
+__global__ void __launch_bounds__(kMT) skw_pairs_merge_kernel(WideArgs a, int64_t B) {
+    pdl_launch_dependents();
+    pdl_wait();   // the iteration kernel's partials are complete and visible
+    const int64_t idx = int64_t(blockIdx.x) * kMT + threadIdx.x;
+    if (idx >= B * a.m) return;
+    const int b = int(idx / a.m);
+    const int64_t col = idx - int64_t(b) * a.m;
+    const int kfirst = w_owner(a, b * a.nbat);
+    const int nseg = w_owner(a, (b + 1) * a.nbat - 1) - kfirst + 1;
+    const float2* pc = a.part + int64_t(b) * a.maxseg * a.m + col;
+    float mm = kNegBig;
+    for (int s0 = 0; s0 < nseg; s0 += kMU) {
+        float x[kMU];
+#pragma unroll
+        for (int k = 0; k < kMU; ++k) x[k] = s0 + k < nseg ? __ldcg(&pc[int64_t(s0 + k) * a.m].x) : kNegBig;
+#pragma unroll
+        for (int k = 0; k < kMU; ++k) mm = fmaxf(mm, x[k]);
+    }
+    float ss = 0.0f;
+    for (int s0 = 0; s0 < nseg; s0 += kMU) {
+        float2 pp[kMU];
+#pragma unroll
+        for (int k = 0; k < kMU; ++k)
+            pp[k] = s0 + k < nseg ? __ldcg(pc + int64_t(s0 + k) * a.m) : make_float2(kNegBig, 0.0f);
+#pragma unroll
+        for (int k = 0; k < kMU; ++k)
+            if (s0 + k < nseg) ss = fmaf(pp[k].y, exp_shift(pp[k].x - mm), ss);
+    }
+    a.pairs[int64_t(b) * a.m + col] = make_float2(mm, ss);
 }
 
 // Stages plus the pair-exchange slots for batches of R rows.
@@ -729,8 +769,7 @@ int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def
     Carve c(ws);
     WideArgs w{};
     w.part = c.take<float2>(size_t(B * wide_seg_bound(B, n, m) * m));
-    w.cnt = c.take<int32_t>(size_t(B * kWC));
-    cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(B * kWC), st);
+    w.cnt = c.take<int32_t>(size_t(B * kWC));   // unused: no arrival counting in this mode
     w.X = X;
     w.kinv = kinv;
     w.la = la;
@@ -752,6 +791,17 @@ int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def
     w.wmode = wide_wait_mode();
     ProfScope ps(DOT_K_SK_FWD_ITER, st);
     launch_any(w, st);
+    // the pair merge starts (PDL) while the iteration kernel drains
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned((B * m + kMT - 1) / kMT));
+    cfg.blockDim = dim3(kMT);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, skw_pairs_merge_kernel, w, B);
     return check_launch("sinkhorn rows + column pairs (wide rows)");
 }
 
