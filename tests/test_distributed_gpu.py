@@ -1,5 +1,6 @@
 """Row-sharded Sinkhorn over NCCL (2 ranks, one GPU each) against the
-single-GPU forward on the same problem.  Needs >= 2 GPUs; skipped otherwise."""
+single-GPU forward on the same problem (skipped with fewer than 2 GPUs), and
+the same loop on one GPU without a process group."""
 
 import os
 import socket
