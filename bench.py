@@ -24,6 +24,15 @@ resident in HBM; ``e2e`` re-times the same step from pinned host memory
 step's loss inside the timed region; the next step's inputs are copied on a
 second stream while the current step computes).
 
+Extra keys of the default (cfg2) line: ``configs`` (N=1) -- every other
+BASELINE configuration with its time per step, throughput, dominant-kernel
+roofline and CPU baseline; ``rowshard_cfg5`` -- configs[4] (32768 x 32768,
+reg 0.01) forward at 100 iterations, on one GPU at N=1 and rows sharded over
+the N GPUs (library-owned NCCL all-gather per iteration) at N>1;
+``batchshard_cfg4`` -- configs[3] with its 4096 problems split over the N
+GPUs.  The last two are strong scaling and give the 1/2/4/8-GPU curve of the
+sharded configurations when the driver runs the bench at several N.
+
 ``--impl reference`` times the reference's own CPU implementation of the path
 (its kernels_cpu.cpp compiled from source into oracle/_ref by oracle/Makefile;
 the C restatement in oracle/ if that library is absent) on all host threads,
@@ -46,6 +55,8 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "Sinkhorn fwd+bwd cost-elem-iters/s per GPU; achieved HBM GB/s vs peak"
+METRIC_FWD = "Sinkhorn fwd cost-elem-iters/s (forward only); achieved HBM GB/s vs peak"
+METRIC_BS = "bidirectional softmax fwd+bwd elements/s; achieved HBM GB/s vs peak"
 
 CONFIGS = {
     "cfg1": dict(kind="sinkhorn", B=8, n=64, m=64, reg=1.0, iters=100, cost="uniform", marg="uniform",
@@ -222,73 +233,99 @@ class ClockSampler:
 # our arm
 # ---------------------------------------------------------------------------
 
-def run_ours(args, cfg: dict) -> None:
-    import torch
-    import torch.distributed as dist
-
-    import dot
-    from dot_b200 import _lib
-
-    rank, local_rank, world = env_rank()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    rowshard = cfg["kind"] == "sinkhorn_fwd" and world > 1
-    if cfg.get("cost") == "sqdist3u":
-        # one problem (cfg5): the same seeded points on every rank; each rank
-        # builds the cost rows it owns on its GPU (row sharding for world > 1)
-        from dot_b200.distributed import shard_range
-
-        g = torch.Generator(device="cpu")
-        g.manual_seed(1234)
-        x = torch.rand(cfg["B"], cfg["n"], 3, generator=g)
-        y = torch.rand(cfg["B"], cfg["m"], 3, generator=g)
-        lo, hi = shard_range(cfg["n"], rank, world) if rowshard else (0, cfg["n"])
-        C_gpu = torch.cdist(x[:, lo:hi].to(dev), y.to(dev)).square().contiguous()
-        inputs = {"C": C_gpu.cpu()}
-        del C_gpu
-    else:
-        inputs = make_inputs(cfg, seed=1234 + rank)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
+def metric_of(cfg: dict) -> str:
     if cfg["kind"] == "bidir":
-        S_host = inputs["S"].pin_memory()
-        G_host = inputs["G"].pin_memory()
-        S_dev = S_host.to(dev)
-        G_dev = G_host.to(dev)
+        return METRIC_BS
+    return METRIC_FWD if cfg["kind"] == "sinkhorn_fwd" else METRIC
 
-        def step(S, G):
-            s = S.detach().requires_grad_(True)
-            out = dot.bidirectional_softmax(s, tau=cfg["tau"])
-            out.backward(G)
-            return out
 
-        host_in = (S_host, G_host)
+def unit_of(cfg: dict) -> str:
+    return "elements/s" if cfg["kind"] == "bidir" else "cost-elem-iters/s"
 
-        def step_on(bufs):
-            return step(*bufs).sum()
 
-        step_dev = lambda: step(S_dev, G_dev)  # noqa: E731
-        h2d = S_host.numel() * S_host.element_size() + G_host.numel() * 4
+def config_dict(cfg: dict, world: int) -> dict:
+    """The ``config`` object of a bench line; both arms print the same one."""
+    rowshard = cfg["kind"] == "sinkhorn_fwd" and world > 1
+    d = {"workload": cfg["desc"], **{k: cfg[k] for k in ("B", "n", "m") if k in cfg}}
+    if cfg["kind"] == "bidir":
+        d.update({"tau": cfg["tau"], "dtype": cfg.get("dtype", "f32")})
     else:
+        d.update({"reg": cfg["reg"], "n_iters": cfg["iters"], "tol": 0})
+        if cfg["kind"] == "sinkhorn":
+            d["backward_iters"] = cfg["iters"]
+    d["per_rank_batch"] = cfg["B"]
+    big = cfg["B"] * cfg["n"] * cfg["m"] * 4 > 126e6
+    d["l2"] = ("inputs larger than L2 (126 MB)" if big else
+               "small working set: L2-resident by design (on-chip solver)")
+    d["parallelism"] = (f"rows sharded x{world}, NCCL all-gather of column (max, sum) pairs per iteration"
+                        if rowshard else f"batch-independent x{world} (no collective)")
+    return d
+
+
+class Workload:
+    """Device-resident inputs and the step function of one configuration on
+    this rank.  ``rowshard``: configs[4] (one problem) with its rows split
+    over the ranks; ``batch_split``: the batch split over the ranks (strong
+    scaling through ``sinkhorn_batchshard``); otherwise every rank runs the
+    whole workload on its own inputs (weak scaling)."""
+
+    def __init__(self, cfg: dict, rank: int, world: int, dev, batch_split: bool = False):
+        import torch
+
+        import dot
+        from dot_b200.distributed import shard_range, sinkhorn_batchshard, sinkhorn_rowshard
+
+        self.cfg = cfg
+        self.rowshard = cfg["kind"] == "sinkhorn_fwd" and world > 1
+        if cfg.get("cost") == "sqdist3u":
+            # one problem (configs[4]): the same seeded points on every rank; each
+            # rank builds the cost rows it owns on its GPU
+            g = torch.Generator(device="cpu")
+            g.manual_seed(1234)
+            x = torch.rand(cfg["B"], cfg["n"], 3, generator=g)
+            y = torch.rand(cfg["B"], cfg["m"], 3, generator=g)
+            lo, hi = shard_range(cfg["n"], rank, world) if self.rowshard else (0, cfg["n"])
+            C_gpu = torch.cdist(x[:, lo:hi].to(dev), y.to(dev)).square().contiguous()
+            inputs = {"C": C_gpu.cpu()}
+            del C_gpu
+        else:
+            inputs = make_inputs(cfg, seed=1234 if batch_split else 1234 + rank)
+        if cfg["kind"] == "bidir":
+            S_host = inputs["S"].pin_memory()
+            G_host = inputs["G"].pin_memory()
+            self.S_dev, self.G_dev = S_host.to(dev), G_host.to(dev)
+
+            def step(S, G):
+                s = S.detach().requires_grad_(True)
+                out = dot.bidirectional_softmax(s, tau=cfg["tau"])
+                out.backward(G)
+                return out
+
+            self.host_in = (S_host, G_host)
+            self.step_on = lambda bufs: step(*bufs).sum()
+            self.step_dev = lambda: step(self.S_dev, self.G_dev)
+            self.h2d = S_host.numel() * S_host.element_size() + G_host.numel() * 4
+            self.elems_local = None
+            return
         C_host = inputs["C"].pin_memory()
-        C_dev = C_host.to(dev)
-        a = inputs.get("a")
-        b = inputs.get("b")
+        self.C_dev = C_host.to(dev)
+        a, b = inputs.get("a"), inputs.get("b")
         a_dev = None if a is None else a.to(dev)
         b_dev = None if b is None else b.to(dev)
         fwd_only = cfg["kind"] == "sinkhorn_fwd"
+        rowshard = self.rowshard
 
         def step(C):
             if rowshard:
-                from dot_b200.distributed import sinkhorn_rowshard
-
                 res = sinkhorn_rowshard(C, cfg["reg"], cfg["iters"], n_total=cfg["n"])
                 return res["cost"].sum()
+            if batch_split:
+                Cg = C.detach().requires_grad_(True)
+                res = sinkhorn_batchshard(Cg, reg=cfg["reg"], n_iters=cfg["iters"], a=a_dev, b=b_dev, tol=0,
+                                          device=dev)
+                loss = res["cost"].sum()
+                loss.backward()
+                return loss
             Cg = C if fwd_only else C.detach().requires_grad_(True)
             res = dot.sinkhorn(Cg, reg=cfg["reg"], n_iters=cfg["iters"], a=a_dev, b=b_dev, tol=0)
             loss = res.cost.sum()
@@ -296,48 +333,74 @@ def run_ours(args, cfg: dict) -> None:
                 loss.backward()
             return loss
 
-        host_in = (C_host,)
+        self.host_in = (C_host,)
+        self.step_on = lambda bufs: step(*bufs)
+        self.step_dev = lambda: step(self.C_dev)
+        self.h2d = C_host.numel() * 4
+        self.elems_local = self.C_dev.numel()
+        if batch_split:
+            lo, hi = shard_range(cfg["B"], rank, world)
+            self.elems_local = (hi - lo) * cfg["n"] * cfg["m"]
 
-        def step_on(bufs):
-            return step(*bufs)
 
-        step_dev = lambda: step(C_dev)  # noqa: E731
-        h2d = C_host.numel() * 4
+def _barrier(world):
+    import torch.distributed as dist
 
-    clocks = ClockSampler(local_rank).start()
-    for _ in range(args.warmup):
-        step_dev()
+    if world > 1:
+        dist.barrier()
+
+
+def _max_over_ranks(ms: float, world: int, dev) -> float:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_device(step, steps: int, warmup: int, world: int, dev, profile: bool, clocks=None):
+    """W untimed steps, then K steps between a barrier + synchronize on both
+    sides, timed with CUDA events on the launching stream; returns (max-over-
+    ranks ms for the K steps, per-class launch counts / kernel ms)."""
+    import torch
+
+    from dot_b200 import _lib
+
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
-
-    # ---- timed region (device-resident inputs) ----
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
+    _barrier(world)
     torch.cuda.synchronize()
-    _lib.prof_begin(time_events=True)
-    clocks.mark_begin()
+    _lib.prof_begin(time_events=profile)
+    if clocks is not None:
+        clocks.mark_begin()
     ev0.record(stream)
-    for _ in range(args.steps):
-        step_dev()
+    for _ in range(steps):
+        step()
     ev1.record(stream)
     torch.cuda.synchronize()
-    clocks.mark_end()
-    clocks.stop()
+    if clocks is not None:
+        clocks.mark_end()
     prof = _lib.prof_end()
-    barrier()
-    ms = ev0.elapsed_time(ev1)
-    t_local = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
-    ms_max = float(t_local.item())
+    _barrier(world)
+    return _max_over_ranks(ev0.elapsed_time(ev1), world, dev), prof
 
-    # ---- timed region (end to end from pinned host memory) ----
-    # Every step's inputs are copied host -> device inside the timed region and
-    # its loss is read back to the host; the copy of step k+1's inputs runs on a
-    # second stream into a second set of device buffers while step k computes
-    # (double buffering, as an input pipeline would).
+
+def time_e2e(wl: Workload, steps: int, world: int, dev) -> float:
+    """End to end from pinned host memory: every step's inputs are copied host
+    -> device inside the timed region and its loss is read back to the host;
+    the copy of step k+1's inputs runs on a second stream into a second set of
+    device buffers while step k computes (double buffering, as an input
+    pipeline would)."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
     copy_stream = torch.cuda.Stream(dev)
-    dbufs = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host_in) for _ in range(2)]
+    dbufs = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in wl.host_in) for _ in range(2)]
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
 
@@ -345,50 +408,148 @@ def run_ours(args, cfg: dict) -> None:
         j = k % 2
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(free[j])   # step k-2 is done with these buffers
-            for d, h in zip(dbufs[j], host_in):
+            for d, h in zip(dbufs[j], wl.host_in):
                 d.copy_(h, non_blocking=True)
             ready[j].record(copy_stream)
 
-    def run_e2e(nsteps):
+    def run(nsteps):
         upload(0)
         for k in range(nsteps):
             if k + 1 < nsteps:
                 upload(k + 1)
             stream.wait_event(ready[k % 2])
-            loss = step_on(dbufs[k % 2])
+            loss = wl.step_on(dbufs[k % 2])
             free[k % 2].record(stream)
             loss.item()  # device -> host read of the step's result
 
     for j in range(2):
         free[j].record(stream)
-    run_e2e(1)   # untimed: first use of the e2e path's allocations
-    barrier()
+    run(1)   # untimed: first use of the e2e path's allocations
+    _barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    run_e2e(args.steps)
+    run(steps)
     e1.record(stream)
     torch.cuda.synchronize()
-    barrier()
-    t_e2e = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    _barrier(world)
+    return _max_over_ranks(e0.elapsed_time(e1), world, dev)
+
+
+def measure_config(name: str, steps: int, warmup: int, rank: int, world: int, dev, cpu_seconds: float,
+                   with_cpu: bool) -> dict:
+    """One secondary configuration at N=1: device-resident timing, the
+    dominant kernel's roofline and the CPU baseline."""
+    cfg = dict(CONFIGS[name])
+    cfg["name"] = name
+    wl = Workload(cfg, rank, world, dev)
+    ms, prof = time_device(wl.step_dev, steps, warmup, world, dev, profile=True)
+    units = units_per_step(cfg)
+    value = units * world * steps / (ms / 1e3)
+    out = {"workload": cfg["desc"], "metric": metric_of(cfg), "unit": unit_of(cfg), "ms_per_step": ms / steps,
+           "value": value, "value_per_gpu": value / world, "steps": steps, "warmup": warmup,
+           "roofline": roofline(cfg, prof, measured_peaks(), steps, elems_local=wl.elems_local),
+           "kernels": {k: v for k, v in prof.items() if v["launches"]}}
+    if with_cpu:
+        out["cpu_baseline"] = cpu_baseline(cfg, sample_seconds=cpu_seconds)
+    del wl
+    import torch
+
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_rowshard_cfg5(iters: int, rank: int, world: int, dev) -> dict:
+    """configs[4] (32768 x 32768, reg 0.01) forward at ``iters`` iterations:
+    at N=1 the single-GPU forward, at N>1 rows sharded over the ranks with the
+    library's per-iteration all-gather.  A separate profiled step gives the
+    per-iteration split between the sweep kernel and the exchange."""
+    import torch
+
+    cfg = dict(CONFIGS["cfg5"])
+    cfg["name"] = "cfg5"
+    cfg["iters"] = iters
+    wl = Workload(cfg, rank, world, dev)
+    steps = 3
+    ms, _ = time_device(wl.step_dev, steps, 3, world, dev, profile=False)
+    _, prof = time_device(wl.step_dev, 1, 0, world, dev, profile=True)
+    units = cfg["B"] * cfg["n"] * cfg["m"] * iters
+    peaks = measured_peaks()
+    fw, ex = prof["sk_fwd_iter"], prof["sk_exchange"]
+    sweep_bytes = 4 * wl.elems_local * iters
+    out = {"n_gpus": world, "n_iters": iters, "ms_per_step": ms / steps, "ms_per_iter": ms / steps / iters,
+           "value": units * steps / (ms / 1e3), "unit": "cost-elem-iters/s", "scaling": "strong",
+           "rows_per_gpu": wl.elems_local // cfg["m"],
+           "profiled_step": {"sweep_ms_per_iter": fw["ms"] / iters, "exchange_ms_per_iter": ex["ms"] / iters,
+                             "note": "one step with events around every launch (breaks the launch overlap "
+                                     "of the unprofiled steps)"},
+           "roofline": {"bound": "hbm", "kernel_class": "sk_fwd_iter",
+                        "achieved": sweep_bytes / (fw["ms"] / 1e3) / 1e9 if fw["ms"] > 0 else None,
+                        "peak": peaks["hbm_gbs"], "unit": "GB/s", "peak_source": peaks["source"]}}
+    r = out["roofline"]
+    r["frac"] = r["achieved"] / r["peak"] if r["achieved"] else None
+    del wl
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_batchshard_cfg4(rank: int, world: int, dev) -> dict:
+    """configs[3] (B=4096, 128x128, 100 iterations, fwd+bwd) with the batch
+    split over the ranks by ``sinkhorn_batchshard`` (strong scaling; the
+    per-step cost gather is the only collective)."""
+    import torch
+
+    cfg = dict(CONFIGS["cfg4"])
+    cfg["name"] = "cfg4"
+    wl = Workload(cfg, rank, world, dev, batch_split=True)
+    steps = 5
+    ms, _ = time_device(wl.step_dev, steps, 3, world, dev, profile=False)
+    units = units_per_step(cfg)
+    del wl
+    torch.cuda.empty_cache()
+    return {"n_gpus": world, "ms_per_step": ms / steps, "value": units * steps / (ms / 1e3),
+            "unit": "cost-elem-iters/s", "scaling": "strong", "problems_per_gpu": -(-cfg["B"] // world)}
+
+
+SECONDARY = ("cfg1", "cfg3", "cfg3bf16", "cfg4", "cfg5")
+
+
+def run_ours(args, cfg: dict) -> None:
+    import torch
+    import torch.distributed as dist
+
+    rank, local_rank, world = env_rank()
     if world > 1:
-        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
-    ms_e2e = float(t_e2e.item())
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    wl = Workload(cfg, rank, world, dev)
+    rowshard = wl.rowshard
+
+    clocks = ClockSampler(local_rank).start()
+    ms_max, prof = time_device(wl.step_dev, args.steps, args.warmup, world, dev, profile=True, clocks=clocks)
+    clocks.stop()
+    ms_e2e = time_e2e(wl, args.steps, world, dev)
 
     units = units_per_step(cfg)
     jobs = 1 if rowshard else world   # row sharding splits one problem; otherwise each rank runs its own batch
     value = units * jobs * args.steps / (ms_max / 1e3)
     e2e_value = units * jobs * args.steps / (ms_e2e / 1e3)
     launches = sum(v["launches"] for v in prof.values())
+    elems_local = wl.elems_local
+    del wl
+    torch.cuda.empty_cache()
 
+    line = None
     if rank == 0:
         peaks = measured_peaks()
-        roof = roofline(cfg, prof, peaks, args.steps,
-                        elems_local=(C_dev.numel() if cfg["kind"] != "bidir" else None))
         line = {
-            "metric": METRIC if cfg["kind"] != "bidir" else "bidirectional softmax fwd+bwd elements/s",
+            "metric": metric_of(cfg),
             "value": value,
-            "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
+            "unit": unit_of(cfg),
+            "value_per_gpu": value / world,
+            "value_is": "whole-job total over n_gpus (value_per_gpu = value / n_gpus)",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
@@ -398,31 +559,48 @@ def run_ours(args, cfg: dict) -> None:
             "vs_baseline": None,
             "dtype": "f32" if cfg.get("dtype", "f32") == "f32" else "bf16-in/f32",
             "data": "synthetic (seeded; shapes and distributions of the BASELINE config)",
-            "config": {"workload": cfg["desc"], **{k: cfg[k] for k in ("B", "n", "m") if k in cfg},
-                       **({"reg": cfg["reg"], "n_iters": cfg["iters"], "backward_iters": cfg["iters"],
-                           "tol": 0} if cfg["kind"] != "bidir" else {"tau": cfg["tau"]}),
-                       "per_rank_batch": cfg["B"],
-                       "l2": "inputs larger than L2 (126 MB)" if units_per_step(cfg) // max(cfg.get("iters", 1), 1) * 4
-                       > 126e6 else "small working set: L2-resident by design (on-chip solver)",
-                       "parallelism": (f"rows sharded x{world}, NCCL all-gather of column (max, sum) pairs "
-                                       "per iteration" if rowshard else
-                                       f"batch-independent x{world} (no collective)")},
-            "e2e": {"value": e2e_value, "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
-                    "ms_per_step": ms_e2e / args.steps,
+            "config": config_dict(cfg, world),
+            "e2e": {"value": e2e_value, "unit": unit_of(cfg),
+                    "h2d_bytes_per_step": h2d_bytes(cfg, elems_local),
+                    "d2h_bytes_per_step": 4, "ms_per_step": ms_e2e / args.steps,
                     "pipeline": "each step's inputs copied from pinned host memory inside the timed region, "
                                 "step k+1's on a second stream while step k computes; loss read back every step"},
             "gpu_launches": int(launches),
-            "roofline": roof,
+            "roofline": roofline(cfg, prof, peaks, args.steps, elems_local=elems_local),
             "kernels": {k: v for k, v in prof.items() if v["launches"]},
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, sample_seconds=args.cpu_seconds)
+    if world == 1 and not args.no_configs and cfg["name"] == "cfg2":
+        confs = {}
+        for name in SECONDARY:
+            confs[name] = measure_config(name, 3, 3, rank, world, dev, args.cpu_seconds / 2,
+                                         with_cpu=not args.no_cpu_baseline)
+        if line is not None:
+            line["configs"] = confs
+    if not args.no_scaling and cfg["name"] != "cfg5":
+        rs = measure_rowshard_cfg5(100, rank, world, dev)
+        bsd = measure_batchshard_cfg4(rank, world, dev)
+        if line is not None:
+            line["rowshard_cfg5"] = rs
+            line["batchshard_cfg4"] = bsd
+    if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
+        from dot_b200.distributed import release_communicators
+
         dist.barrier()
+        release_communicators()
         dist.destroy_process_group()
+
+
+def h2d_bytes(cfg: dict, elems_local) -> int:
+    """Bytes copied host -> device per end-to-end step."""
+    if cfg["kind"] == "bidir":
+        per = 4 if cfg.get("dtype", "f32") == "f32" else 2
+        return cfg["B"] * cfg["n"] * cfg["m"] * (per + 4)
+    return 4 * int(elems_local)
 
 
 def roofline(cfg: dict, prof: dict, peaks: dict, steps: int, elems_local: int | None = None) -> dict:
@@ -560,28 +738,79 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def sample_problems(cfg: dict, threads: int, seconds: float) -> int:
     """Problems per CPU sample: about `seconds` of CPU work, at least one per thread."""
-    per_problem = {"cfg1": 0.011, "cfg2": 1.7, "cfg3": 0.12, "cfg3bf16": 0.12, "cfg4": 0.046, "cfg5": 1e9}
+    per_problem = {"cfg1": 0.011, "cfg2": 1.7, "cfg3": 0.12, "cfg3bf16": 0.12, "cfg4": 0.046}
     est = per_problem.get(cfg.get("name", ""), 1.0)
     p = max(threads, int(seconds / est))
     p = (p // threads) * threads if p >= threads else threads
     return max(1, min(p, cfg["B"]))
 
 
+def cpu_cfg5_extrapolated(cfg: dict, kind: str, cols: int = 2048) -> tuple[float, str]:
+    """configs[4] on the host: the reference's CPU forward op (single-threaded
+    by construction) on all rows and a slice of ``cols`` columns, run for 0, 1
+    and 2 iterations; the per-iteration time and the fixed part (scaling and
+    plan) are scaled by m / cols and extrapolated to the configuration's
+    iteration count.  Returns (units/s, description)."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    n, m, T = cfg["n"], cfg["m"], cfg["iters"]
+    g = torch.Generator().manual_seed(99)
+    x = torch.rand(1, n, 3, generator=g)
+    y = torch.rand(1, cols, 3, generator=g)
+    log_alpha = np.ascontiguousarray(-torch.cdist(x, y).square().float().numpy())
+    t = []
+    for it in (0, 1, 2):
+        t0 = time.perf_counter()
+        O.sinkhorn_forward(log_alpha, cfg["reg"], it, kind=kind)
+        t.append(time.perf_counter() - t0)
+    per_iter = max((t[2] - t[0]) / 2, 1e-9)
+    full = (m / cols) * (t[0] + T * per_iter)
+    desc = (f"extrapolated: the reference CPU forward op on all {n} rows x {cols} of {m} columns, timed at 0/1/2 "
+            f"iterations ({t[0]:.2f}/{t[1]:.2f}/{t[2]:.2f} s), per-iteration time x {T} plus the fixed part, "
+            f"scaled by {m // cols}: {full / 3600:.2f} h per step on 1 core")
+    return n * m * T / full, desc
+
+
 def cpu_baseline(cfg: dict, sample_seconds: float = 15.0) -> dict:
-    if cfg["kind"] == "sinkhorn_fwd":
-        return {"value": None, "unit": "cost-elem-iters/s", "cores": 1, "kind": "reference",
-                "sample": "not run: one iteration of the 32768^2 problem takes minutes on one core"}
+    """The reference's CPU implementation timed on this host: all host threads
+    (one problem per thread at a time) and one thread (the op as-is)."""
     kind = cpu_kind()
+    ckind = "reference" if kind == "reference" else "port"
+    unit = unit_of(cfg)
+    if cfg["kind"] == "sinkhorn_fwd":
+        v, desc = cpu_cfg5_extrapolated(cfg, kind)
+        return {"value": v, "value_1thread": v, "unit": unit, "cores": 1, "kind": ckind, "cpu_model": cpu_model(),
+                "sample": desc + " (one problem: the single-threaded op cannot use more cores)"}
     threads = cpu_threads()
     problems = sample_problems(cfg, threads, sample_seconds)
-    v, dt, units = cpu_sample(cfg, problems, threads, kind)
-    return {"value": v, "unit": "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s",
-            "cores": threads, "kind": "reference" if kind == "reference" else "port",
-            "sample": f"{problems} of {cfg['B']} problems of the workload, full size and iterations, "
-                      f"{threads} threads (one problem per thread at a time), {dt:.1f} s wall; the reference's "
-                      "CPU fwd op, then its backward op (which re-runs the forward)"}
+    v, dt, _ = cpu_sample(cfg, problems, threads, kind)
+    p1 = sample_problems(cfg, 1, sample_seconds / 4)
+    v1, dt1, _ = cpu_sample(cfg, p1, 1, kind)
+    what = ("the reference's CPU fwd op, then its backward op (which re-runs the forward)"
+            if cfg["kind"] == "sinkhorn" else "the reference's CPU forward op, then its backward op")
+    return {"value": v, "value_1thread": v1, "unit": unit, "cores": threads, "kind": ckind,
+            "cpu_model": cpu_model(),
+            "sample": f"{problems} of {cfg['B']} problems of the workload, full size and iterations, {threads} threads "
+                      f"(one problem per thread at a time), {dt:.1f} s wall; 1 thread: {p1} problem(s), "
+                      f"{dt1:.1f} s; {what}"}
 
 
 def run_reference(args, cfg: dict) -> None:
@@ -590,30 +819,40 @@ def run_reference(args, cfg: dict) -> None:
         return
     kind = cpu_kind()
     threads = cpu_threads()
-    if cfg["kind"] == "sinkhorn_fwd":
-        print(json.dumps({"impl": "reference", "unavailable": "cfg5 on the host CPU takes ~16 h per step"}))
-        return
-    problems = sample_problems(cfg, threads, args.cpu_seconds)
-    for _ in range(args.warmup):
-        cpu_sample(cfg, threads, threads, kind)
+    unit = unit_of(cfg)
     vals, secs = [], []
-    for _ in range(args.steps):
-        v, dt, _ = cpu_sample(cfg, problems, threads, kind)
-        vals.append(v)
-        secs.append(dt)
+    if cfg["kind"] == "sinkhorn_fwd":
+        for _ in range(args.warmup):
+            cpu_cfg5_extrapolated(cfg, kind, cols=256)
+        for _ in range(args.steps):
+            v, desc = cpu_cfg5_extrapolated(cfg, kind)
+            vals.append(v)
+            secs.append(cfg["B"] * cfg["n"] * cfg["m"] * cfg["iters"] / v)
+        cores = 1
+        sample = desc
+    else:
+        problems = sample_problems(cfg, threads, args.cpu_seconds)
+        for _ in range(args.warmup):
+            cpu_sample(cfg, threads, threads, kind)
+        for _ in range(args.steps):
+            v, dt, _ = cpu_sample(cfg, problems, threads, kind)
+            vals.append(v)
+            secs.append(dt * cfg["B"] / problems)
+        cores = threads
+        sample = (f"{problems} of {cfg['B']} problems per step at full size and iterations, {threads} host threads, "
+                  f"reference CPU kernels ({'oracle/_ref, compiled from the reference sources' if kind == 'reference' else 'oracle restatement'}); "
+                  "ms_per_step scaled to the whole batch")
     value = statistics.median(vals)
-    unit = "cost-elem-iters/s" if cfg["kind"] != "bidir" else "elements/s"
-    sample = (f"{problems} of {cfg['B']} problems per step at full size and iterations, {threads} host threads, "
-              f"reference CPU kernels ({'oracle/_ref, compiled from the reference sources' if kind == 'reference' else 'oracle restatement'})")
     line = {
         "impl": "reference",
-        "metric": METRIC if cfg["kind"] != "bidir" else "bidirectional softmax fwd+bwd elements/s",
-        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * statistics.median(secs), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; shapes of the BASELINE config)",
-        "config": {"workload": cfg["desc"], "B": cfg["B"], "n": cfg["n"], "m": cfg["m"]},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": threads,
-                         "kind": "reference" if kind == "reference" else "port", "sample": sample},
+        "metric": metric_of(cfg), "value": value, "unit": unit, "value_per_gpu": value / world, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(secs),
+        "higher_is_better": True, "scaling": "strong" if cfg["kind"] == "sinkhorn_fwd" and world > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; shapes and distributions of the BASELINE config)",
+        "config": config_dict(cfg, world),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores,
+                         "kind": "reference" if kind == "reference" else "port", "cpu_model": cpu_model(),
+                         "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -628,6 +867,9 @@ def main() -> None:
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work per baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other BASELINE configs (N=1 default run)")
+    ap.add_argument("--no-scaling", action="store_true",
+                    help="skip the row-sharded configs[4] and batch-sharded configs[3] measurements")
     ap.add_argument("--iters", type=int, default=None, help="override the config's iteration count (profiling)")
     ap.add_argument("--rows", type=int, default=None, help="override the config's row count n (profiling)")
     args = ap.parse_args()

@@ -17,7 +17,8 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libdot_b200.so")
 ABI_VERSION = 1
 
 DOT_F32, DOT_BF16, DOT_F16 = 0, 1, 2
-KCLASSES = ("sk_fwd_iter", "sk_fwd_epi", "sk_bwd_iter", "sk_bwd_epi", "sk_resident", "bs_fwd", "bs_bwd")
+KCLASSES = ("sk_fwd_iter", "sk_fwd_epi", "sk_bwd_iter", "sk_bwd_epi", "sk_resident", "bs_fwd", "bs_bwd",
+            "sk_exchange")
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -36,23 +37,23 @@ _SIGS = {
     "dot_sinkhorn_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "dot_sinkhorn_bwd": (_i, [_vp, _f, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i, _vp, _vp, _vp, _sz,
                               _vp]),
-    "dot_sinkhorn_rows": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _i64, _f, _vp, _vp, _vp]),
-    "dot_sinkhorn_col_partials_workspace_bytes": (_sz, [_i64, _i64, _i64]),
-    "dot_sinkhorn_col_partials": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _f, _vp, _vp, _vp, _sz, _vp]),
     "dot_sinkhorn_fwd_hist": (_i, [_vp, _f, _vp, _vp, _i64, _i64, _i64, _f, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp,
                                    _vp, _vp, _sz, _vp]),
     "dot_sinkhorn_bwd_unrolled_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "dot_sinkhorn_bwd_unrolled": (_i, [_vp, _f, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i, _vp, _vp, _vp,
                                        _sz, _vp]),
     "dot_sinkhorn_rows_colpairs_workspace_bytes": (_sz, [_i64, _i64, _i64]),
-    "dot_sinkhorn_rows_colpairs": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _i64, _f, _vp, _vp, _vp, _vp, _sz, _vp]),
-    "dot_sinkhorn_col_pairs_workspace_bytes": (_sz, [_i64, _i64, _i64]),
-    "dot_sinkhorn_col_pairs": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _f, _vp, _vp, _sz, _vp]),
+    "dot_sinkhorn_rows_colpairs": (_i, [_vp, _f, _vp, _i64, _i64, _i64, _i64, _f, _vp, _vp, _vp, _vp, _vp, _sz,
+                                        _vp]),
     "dot_sinkhorn_col_merge": (_i, [_vp, _i, _vp, _i64, _i64, _vp, _vp]),
-    "dot_sinkhorn_col_rescale": (_i, [_vp, _vp, _vp, _i64, _vp]),
-    "dot_sinkhorn_col_finish": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _vp]),
     "dot_sinkhorn_plan_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "dot_sinkhorn_plan": (_i, [_vp, _f, _vp, _vp, _i64, _i64, _i64, _f, _i, _vp, _vp, _vp, _sz, _vp]),
+    "dot_sinkhorn_fwd_rowshard_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
+    "dot_sinkhorn_fwd_rowshard": (_i, [_vp, _f, _vp, _vp, _i64, _i64, _i64, _i64, _f, _i, _vp, _vp, _vp, _vp, _vp,
+                                       _vp, _vp, _sz, _vp]),
+    "dot_nccl_unique_id": (_i, [_vp]),
+    "dot_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _i, _vp, _i]),
+    "dot_nccl_comm_destroy": (_i, [_vp]),
     "dot_bidir_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "dot_bidir_fwd": (_i, [_vp, _i, _vp, _i64, _i64, _i64, _f, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dot_bidir_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64]),

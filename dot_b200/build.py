@@ -1,9 +1,11 @@
 """Build the dot_b200 C-ABI library for sm_100a with nvcc (in-tree).
 
-``python dot_b200/build.py`` compiles every ``csrc/*.cu`` into
-``dot_b200/_lib/libdot_b200.so`` with
+``python dot_b200/build.py`` compiles every ``csrc/*.cu`` (in parallel, one
+object per source under ``dot_b200/_lib/obj``) and links them into
+``dot_b200/_lib/libdot_b200.so``, with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3``.  The CUDA runtime is
-linked statically so the library carries no dependency beyond the driver.
+linked statically so the library carries no dependency beyond the driver
+(NCCL, used only by the row-sharded solver, is loaded at run time).
 The build is skipped when the library is newer than every source.
 """
 
@@ -11,6 +13,7 @@ from __future__ import annotations
 
 import glob
 import os
+from concurrent.futures import ThreadPoolExecutor
 import shutil
 import subprocess
 import sys
@@ -45,11 +48,24 @@ def _stale() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
-    os.makedirs(LIB_DIR, exist_ok=True)
+    obj_dir = os.path.join(LIB_DIR, "obj")
+    os.makedirs(obj_dir, exist_ok=True)
+    flags = [ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+             "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
+    nvcc = _nvcc()
+
+    def compile_one(src: str) -> str:
+        obj = os.path.join(obj_dir, os.path.splitext(os.path.basename(src))[0] + ".o")
+        cmd = [nvcc] + flags + ["-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(compile_one, sources()))
     tmp = LIB + ".tmp"
-    cmd = [_nvcc(), ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", "-cudart", "static",
-           "-I" + os.path.join(ROOT, "include"), "-o", tmp] + sources()
+    cmd = [nvcc, ARCH, "-shared", "-cudart", "static", "-o", tmp] + objs + ["-ldl"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

@@ -292,42 +292,6 @@ int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P, const flo
     return sk_stream_bwd(a, workspace, st);
 }
 
-int dot_sinkhorn_rows(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n, int64_t m,
-                      int64_t n_total, float tau, const float* pot_v, float* pot_u, void* stream) {
-    clear_error();
-    int rc = check_dims(B, n, m);
-    if (rc) return rc;
-    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
-    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
-    if (n_total < n) return fail(DOT_ERR_INVALID, "n_total must be >= the shard's row count");
-    if (B == 0 || n == 0 || m == 0) return DOT_OK;
-    if (!X || !pot_v || !pot_u) return fail(DOT_ERR_INVALID, "null tensor pointer");
-    return sk_split_rows(X, score_sign * (1.0f / tau), log_a, -logf(float(n_total)), B, n, m, pot_v, pot_u,
-                         static_cast<cudaStream_t>(stream));
-}
-
-size_t dot_sinkhorn_col_partials_workspace_bytes(int64_t B, int64_t n, int64_t m) {
-    if (B <= 0 || n <= 0 || m <= 0) return 0;
-    return sk_split_colpart_ws(B, n, m);
-}
-
-int dot_sinkhorn_col_partials(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n, int64_t m,
-                              float tau, float* col_max, float* col_sum, void* workspace, size_t workspace_bytes,
-                              void* stream) {
-    clear_error();
-    int rc = check_dims(B, n, m);
-    if (rc) return rc;
-    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
-    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
-    if (B == 0 || n == 0 || m == 0) return DOT_OK;
-    if (!X || !pot_u || !col_max || !col_sum) return fail(DOT_ERR_INVALID, "null tensor pointer");
-    const size_t need = sk_split_colpart_ws(B, n, m);
-    if (workspace == nullptr || workspace_bytes < need)
-        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
-    return sk_split_colpart(X, score_sign * (1.0f / tau), pot_u, B, n, m, col_max, col_sum, workspace,
-                            static_cast<cudaStream_t>(stream));
-}
-
 size_t dot_sinkhorn_rows_colpairs_workspace_bytes(int64_t B, int64_t n, int64_t m) {
     if (B <= 0 || n <= 0 || m <= 0) return 0;
     const size_t a = sk_split_colpairs_ws(B, n, m);
@@ -337,7 +301,7 @@ size_t dot_sinkhorn_rows_colpairs_workspace_bytes(int64_t B, int64_t n, int64_t 
 
 int dot_sinkhorn_rows_colpairs(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n, int64_t m,
                                int64_t n_total, float tau, const float* pot_v, float* pot_u, float* pairs,
-                               void* workspace, size_t workspace_bytes, void* stream) {
+                               int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
     clear_error();
     int rc = check_dims(B, n, m);
     if (rc) return rc;
@@ -345,7 +309,7 @@ int dot_sinkhorn_rows_colpairs(const float* X, float score_sign, const float* lo
     if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
     if (n_total < n) return fail(DOT_ERR_INVALID, "n_total must be >= the shard's row count");
     if (B == 0 || n == 0 || m == 0) return DOT_OK;
-    if (!X || !pot_v || !pot_u || !pairs) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    if (!X || !pot_v || !pot_u || !pairs || !status) return fail(DOT_ERR_INVALID, "null tensor pointer");
     if ((reinterpret_cast<uintptr_t>(pairs) & 7u) != 0) return fail(DOT_ERR_INVALID, "pairs must be 8-byte aligned");
     const size_t need = dot_sinkhorn_rows_colpairs_workspace_bytes(B, n, m);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))
@@ -355,32 +319,10 @@ int dot_sinkhorn_rows_colpairs(const float* X, float score_sign, const float* lo
     const float la_def = -logf(float(n_total));
     if (sk_wide_supported(B, n, m, X))
         return sk_wide_rows_pairs(X, kinv, log_a, la_def, B, n, m, pot_v, pot_u, reinterpret_cast<float2*>(pairs),
-                                  workspace, st);
+                                  status, workspace, st);
     rc = sk_split_rows(X, kinv, log_a, la_def, B, n, m, pot_v, pot_u, st);
     if (rc != DOT_OK) return rc;
     return sk_split_colpairs(X, kinv, pot_u, B, n, m, reinterpret_cast<float2*>(pairs), workspace, st);
-}
-
-size_t dot_sinkhorn_col_pairs_workspace_bytes(int64_t B, int64_t n, int64_t m) {
-    if (B <= 0 || n <= 0 || m <= 0) return 0;
-    return sk_split_colpairs_ws(B, n, m);
-}
-
-int dot_sinkhorn_col_pairs(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n, int64_t m,
-                           float tau, float* pairs, void* workspace, size_t workspace_bytes, void* stream) {
-    clear_error();
-    int rc = check_dims(B, n, m);
-    if (rc) return rc;
-    if (!(tau > 0.0f) || bad_float(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
-    if (score_sign != 1.0f && score_sign != -1.0f) return fail(DOT_ERR_INVALID, "score_sign must be +1 or -1");
-    if (B == 0 || n == 0 || m == 0) return DOT_OK;
-    if (!X || !pot_u || !pairs) return fail(DOT_ERR_INVALID, "null tensor pointer");
-    if ((reinterpret_cast<uintptr_t>(pairs) & 7u) != 0) return fail(DOT_ERR_INVALID, "pairs must be 8-byte aligned");
-    const size_t need = sk_split_colpairs_ws(B, n, m);
-    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
-        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
-    return sk_split_colpairs(X, score_sign * (1.0f / tau), pot_u, B, n, m, reinterpret_cast<float2*>(pairs), workspace,
-                             static_cast<cudaStream_t>(stream));
 }
 
 int dot_sinkhorn_col_merge(const float* pairs, int parts, const float* log_b, int64_t B, int64_t m, float* pot_v,
@@ -393,25 +335,6 @@ int dot_sinkhorn_col_merge(const float* pairs, int parts, const float* log_b, in
     if ((reinterpret_cast<uintptr_t>(pairs) & 7u) != 0) return fail(DOT_ERR_INVALID, "pairs must be 8-byte aligned");
     return sk_split_pair_merge(reinterpret_cast<const float2*>(pairs), parts, log_b, -logf(float(m)), B, m, pot_v,
                                static_cast<cudaStream_t>(stream));
-}
-
-int dot_sinkhorn_col_rescale(const float* col_max, float* col_sum, const float* global_max, int64_t count,
-                             void* stream) {
-    clear_error();
-    if (count < 0) return fail(DOT_ERR_INVALID, "negative count");
-    if (count == 0) return DOT_OK;
-    if (!col_max || !col_sum || !global_max) return fail(DOT_ERR_INVALID, "null tensor pointer");
-    return sk_split_rescale(col_max, col_sum, global_max, count, static_cast<cudaStream_t>(stream));
-}
-
-int dot_sinkhorn_col_finish(const float* global_max, const float* global_sum, const float* log_b, int64_t B,
-                            int64_t m, float* pot_v, void* stream) {
-    clear_error();
-    if (B < 0 || m < 0) return fail(DOT_ERR_INVALID, "negative dimension");
-    if (B == 0 || m == 0) return DOT_OK;
-    if (!global_max || !global_sum || !pot_v) return fail(DOT_ERR_INVALID, "null tensor pointer");
-    return sk_split_finish(global_max, global_sum, log_b, -logf(float(m)), B * m, pot_v,
-                           static_cast<cudaStream_t>(stream));
 }
 
 size_t dot_sinkhorn_plan_workspace_bytes(int64_t B, int64_t n, int64_t m) {

@@ -19,7 +19,9 @@ void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on the current device.  The host-side
 // name of the array is only a stand-in; the address is looked up once per
-// device, with that device current, and cached.
+// device, with that device current, and cached for the life of the process
+// (a primary context destroyed by cudaDeviceReset leaves the entry stale; the
+// header tells callers not to use this entry point after one).
 int scratch_on_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -82,9 +82,10 @@ bool sk_wide_supported(int64_t B, int64_t n, int64_t m, const void* X);
 size_t sk_wide_ws(int64_t B, int64_t n, int64_t m);
 int sk_wide_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 // Row shard: u for the shard's rows from the given v, and the shard's column
-// (max, sum) pairs [B, m] over those rows with the new u, in one pass.
+// (max, sum) pairs [B, m] over those rows with the new u, in one pass.  A
+// bounded wait that expires ORs kErrBarrierTimeout (0x100) into *err.
 int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
-                       const float* v2, float* u2, float2* pairs, void* ws, cudaStream_t st);
+                       const float* v2, float* u2, float2* pairs, int32_t* err, void* ws, cudaStream_t st);
 
 // Unrolled backward through a recorded forward (sinkhorn_unrolled.cu):
 // a.bwd_iters = the number of recorded iterations to differentiate through.
@@ -94,17 +95,11 @@ int sk_unrolled_bwd(const SkBwdArgs& a, const float* u_hist, const float* v_hist
 // Split half-steps for row-sharded problems (sinkhorn_stream.cu).
 int sk_split_rows(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
                   const float* v2, float* u2, cudaStream_t st);
-size_t sk_split_colpart_ws(int64_t B, int64_t n, int64_t m);
-int sk_split_colpart(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m,
-                     float* col_max, float* col_sum, void* ws, cudaStream_t st);
 size_t sk_split_colpairs_ws(int64_t B, int64_t n, int64_t m);
 int sk_split_colpairs(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m, float2* pairs,
                       void* ws, cudaStream_t st);
 int sk_split_pair_merge(const float2* pairs, int parts, const float* lb, float lb_def, int64_t B, int64_t m,
                         float* v2, cudaStream_t st);
-int sk_split_rescale(const float* col_max, float* col_sum, const float* gmax, int64_t count, cudaStream_t st);
-int sk_split_finish(const float* gmax, const float* gsum, const float* lb, float lb_def, int64_t count, float* v2,
-                    cudaStream_t st);
 size_t sk_split_plan_ws(int64_t B, int64_t n);
 int sk_split_plan(const float* X, float kinv, const float* u2, const float* v2, int64_t B, int64_t n, int64_t m,
                   int out_mode, float* out, float* cost, void* ws, cudaStream_t st);

@@ -235,33 +235,6 @@ __global__ void sk_shard_merge_kernel(const float2* __restrict__ pairs, int part
     v2[i] = (lb ? lb[i] : lb_def) - lse_finish(mm, ss);
 }
 
-// (max, sum) pairs -> two arrays (the form the shard all-reduces take).
-__global__ void sk_pair_unpack_kernel(const float2* __restrict__ pair, float* __restrict__ max_out,
-                                      float* __restrict__ sum_out, int64_t count) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= count) return;
-    const float2 p = pair[i];
-    max_out[i] = p.x;
-    sum_out[i] = p.y;
-}
-
-// Shard combine, step 1 (array form): sum_j *= exp(max_local_j - max_global_j).
-__global__ void sk_pair_rescale_kernel(const float* __restrict__ lmax, float* __restrict__ lsum,
-                                       const float* __restrict__ gmax, int64_t count) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= count) return;
-    lsum[i] = lsum[i] * exp_shift(lmax[i] - gmax[i]);
-}
-
-// Shard combine, step 2: v_j = lb_j - (max_j + log(max(sum_j, 1e-12))).
-__global__ void sk_col_finish_kernel(const float* __restrict__ gmax, const float* __restrict__ gsum,
-                                     const float* __restrict__ lb, float lb_def, float* __restrict__ v2,
-                                     int64_t count) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= count) return;
-    v2[i] = (lb ? lb[i] : lb_def) - lse_finish(gmax[i], gsum[i]);
-}
-
 // ---------------------------------------------------------------------------
 // forward epilogue: plan (or log-plan) + per-row cost, warp per row
 // ---------------------------------------------------------------------------
@@ -801,37 +774,6 @@ int sk_split_rows(const float* X, float kinv, const float* la, float la_def, int
     return check_launch("sinkhorn row half-step");
 }
 
-size_t sk_split_colpart_ws(int64_t B, int64_t n, int64_t m) {
-    Carve c(nullptr);
-    const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
-    c.take<float2>(size_t(B * m));
-    if (chunks > 1) c.take<float2>(size_t(B * chunks * m));
-    return c.size();
-}
-
-int sk_split_colpart(const float* X, float kinv, const float* u2, int64_t B, int64_t n, int64_t m,
-                     float* col_max, float* col_sum, void* ws, cudaStream_t st) {
-    Carve c(ws);
-    float2* pair = c.take<float2>(size_t(B * m));
-    const int64_t rpc = col_rows_per_chunk(n);
-    const int chunks = int(ceil_div(n, rpc));
-    float2* part = chunks > 1 ? c.take<float2>(size_t(B * chunks * m)) : nullptr;
-    SkCtl ctl{nullptr, nullptr, 0.0f, 0};
-    const dim3 col_grid(unsigned(ceil_div(m, kColTile)), unsigned(chunks), unsigned(B));
-    {
-        ProfScope ps(DOT_K_SK_FWD_ITER, st);
-        sk_col_kernel<<<col_grid, kColWarps * 32, 0, st>>>(X, kinv, u2, nullptr, 0.0f, nullptr, part, n, m, rpc,
-                                                           chunks, ctl, pair);
-    }
-    if (chunks > 1) {
-        ProfScope ps(DOT_K_SK_FWD_ITER, st);
-        sk_col_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(part, nullptr, 0.0f, nullptr, B, m,
-                                                                            chunks, ctl, pair);
-    }
-    sk_pair_unpack_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pair, col_max, col_sum, B * m);
-    return check_launch("sinkhorn column partials");
-}
-
 size_t sk_split_colpairs_ws(int64_t B, int64_t n, int64_t m) {
     Carve c(nullptr);
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
@@ -864,20 +806,9 @@ int sk_split_pair_merge(const float2* pairs, int parts, const float* lb, float l
                         float* v2, cudaStream_t st) {
     // the shards' pairs laid out [parts][B*m] are the chunk partials of one
     // problem: merge them in shard order exactly as the chunk merge does
-    ProfScope ps(DOT_K_SK_FWD_ITER, st);
+    ProfScope ps(DOT_K_SK_EXCHANGE, st);
     sk_shard_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pairs, parts, lb, lb_def, v2, B * m);
     return check_launch("sinkhorn shard merge");
-}
-
-int sk_split_rescale(const float* col_max, float* col_sum, const float* gmax, int64_t count, cudaStream_t st) {
-    sk_pair_rescale_kernel<<<unsigned(ceil_div(count, 256)), 256, 0, st>>>(col_max, col_sum, gmax, count);
-    return check_launch("sinkhorn column rescale");
-}
-
-int sk_split_finish(const float* gmax, const float* gsum, const float* lb, float lb_def, int64_t count, float* v2,
-                    cudaStream_t st) {
-    sk_col_finish_kernel<<<unsigned(ceil_div(count, 256)), 256, 0, st>>>(gmax, gsum, lb, lb_def, v2, count);
-    return check_launch("sinkhorn column finish");
 }
 
 size_t sk_split_plan_ws(int64_t B, int64_t n) {

@@ -109,7 +109,6 @@ struct WideArgs {
     int32_t* cnt;       // [B][kWC] arrival counters, zero between launches
     float2* pairs;      // row-shard mode: merged column pairs [B][m]; nullptr: write v
     int32_t* err;       // bounded-wait expiry word
-    int wmode;          // barrier wait form (mbar_wait_mode)
 };
 
 __host__ __device__ __forceinline__ int w_q(const WideArgs& a, int k) { return int(int64_t(k) * a.TB / a.G); }
@@ -117,10 +116,11 @@ __host__ __device__ __forceinline__ int w_owner(const WideArgs& a, int x) {
     return int((int64_t(x + 1) * a.G + a.TB - 1) / a.TB) - 1;
 }
 
-// Exact column LSE over all n rows of problem b (max pass, then sum pass);
-// one warp, strided reads; only for columns flagged by the merge.
-__device__ float w_exact_column(const float* X, const float* u2, float kinv, int64_t b, int64_t n, int64_t m,
-                                int64_t col) {
+// Exact column (max, sum) pair over all n rows of problem b (max pass, then
+// the sum of exp(t - max) -- at least 1); one warp, strided reads; only for
+// columns whose shared-reference sum is too small to trust.
+__device__ float2 w_exact_pair(const float* X, const float* u2, float kinv, int64_t b, int64_t n, int64_t m,
+                               int64_t col) {
     const int lane = threadIdx.x & 31;
     const float* xb = X + b * n * m + col;
     const float* ub = u2 + b * n;
@@ -129,8 +129,13 @@ __device__ float w_exact_column(const float* X, const float* u2, float kinv, int
     mx = warp_max<32>(mx);
     float sm = 0.0f;
     for (int64_t i = lane; i < n; i += 32) sm += exp_shift(kplus(__ldcg(xb + i * m), kinv, __ldcg(ub + i)) - mx);
-    sm = warp_sum<32>(sm);
-    return lse_finish(mx, sm);
+    return make_float2(mx, warp_sum<32>(sm));
+}
+
+__device__ float w_exact_column(const float* X, const float* u2, float kinv, int64_t b, int64_t n, int64_t m,
+                                int64_t col) {
+    const float2 p = w_exact_pair(X, u2, kinv, b, n, m, col);
+    return lse_finish(p.x, p.y);
 }
 
 template <class CFG, int NQ, bool FULL>
@@ -179,13 +184,13 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
     };
     auto wait_full = [&](int g) -> bool {
         if (s_abort) return false;
-        const bool r = mbar_wait_mode(&full[sidx(g)], sphase(g), a.wmode, false, a.err);
+        const bool r = mbar_wait_sleep(&full[sidx(g)], sphase(g), a.err);
         if (!r) s_abort = 1;
         return r;
     };
     auto wait_pairs = [&](int g) -> bool {
         if (s_abort) return false;
-        const bool r = mbar_wait_mode(&xbar[xidx(g)], xphase(g), a.wmode, true, a.err);
+        const bool r = mbar_wait_cluster(&xbar[xidx(g)], xphase(g), a.err);
         if (!r) s_abort = 1;
         return r;
     };
@@ -276,7 +281,7 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
             __syncwarp();
             if (lane == 0) mbar_arrive(&ubar[slot]);
         }
-        if (!s_abort && !mbar_wait_mode(&ubar[slot], xphase(gp), a.wmode, false, a.err)) s_abort = 1;
+        if (!s_abort && !mbar_wait_sleep(&ubar[slot], xphase(gp), a.err)) s_abort = 1;
 #pragma unroll
         for (int ir = 0; ir < RM; ++ir) uw[ir] = s_uv[slot][ir];
     };
@@ -508,38 +513,55 @@ __global__ void __launch_bounds__(CFG::T, CFG::MINB) skw_iter_kernel(WideArgs a)
 // the clusters that touched it, in cluster order (max pass, then the
 // rescaled sums -- the arithmetic of the in-kernel slice merge), into the
 // (max, sum) pairs [B][m].  One thread per column; segment loads are issued
-// eight at a time so a thread waits on L2 about nseg/4 times in all.
+// eight at a time so a thread waits on L2 about nseg/4 times in all.  A
+// column whose merged sum is too small to trust (kTinyW, as in the in-kernel
+// merge) gets its pair recomputed exactly over the shard's rows by one warp
+// of the CTA, so the cross-shard merge never starts from an underflowed sum.
 constexpr int kMT = 128;   // threads per merge CTA
 constexpr int kMU = 8;     // segment loads in flight per thread
 __global__ void __launch_bounds__(kMT) skw_pairs_merge_kernel(WideArgs a, int64_t B) {
+    __shared__ int s_fix[kMT];
+    __shared__ int s_nfix;
     pdl_launch_dependents();
+    if (threadIdx.x == 0) s_nfix = 0;
     pdl_wait();   // the iteration kernel's partials are complete and visible
+    __syncthreads();
     const int64_t idx = int64_t(blockIdx.x) * kMT + threadIdx.x;
-    if (idx >= B * a.m) return;
-    const int b = int(idx / a.m);
-    const int64_t col = idx - int64_t(b) * a.m;
-    const int kfirst = w_owner(a, b * a.nbat);
-    const int nseg = w_owner(a, (b + 1) * a.nbat - 1) - kfirst + 1;
-    const float2* pc = a.part + int64_t(b) * a.maxseg * a.m + col;
-    float mm = kNegBig;
-    for (int s0 = 0; s0 < nseg; s0 += kMU) {
-        float x[kMU];
+    if (idx < B * a.m) {
+        const int b = int(idx / a.m);
+        const int64_t col = idx - int64_t(b) * a.m;
+        const int kfirst = w_owner(a, b * a.nbat);
+        const int nseg = w_owner(a, (b + 1) * a.nbat - 1) - kfirst + 1;
+        const float2* pc = a.part + int64_t(b) * a.maxseg * a.m + col;
+        float mm = kNegBig;
+        for (int s0 = 0; s0 < nseg; s0 += kMU) {
+            float x[kMU];
 #pragma unroll
-        for (int k = 0; k < kMU; ++k) x[k] = s0 + k < nseg ? __ldcg(&pc[int64_t(s0 + k) * a.m].x) : kNegBig;
+            for (int k = 0; k < kMU; ++k) x[k] = s0 + k < nseg ? __ldcg(&pc[int64_t(s0 + k) * a.m].x) : kNegBig;
 #pragma unroll
-        for (int k = 0; k < kMU; ++k) mm = fmaxf(mm, x[k]);
+            for (int k = 0; k < kMU; ++k) mm = fmaxf(mm, x[k]);
+        }
+        float ss = 0.0f;
+        for (int s0 = 0; s0 < nseg; s0 += kMU) {
+            float2 pp[kMU];
+#pragma unroll
+            for (int k = 0; k < kMU; ++k)
+                pp[k] = s0 + k < nseg ? __ldcg(pc + int64_t(s0 + k) * a.m) : make_float2(kNegBig, 0.0f);
+#pragma unroll
+            for (int k = 0; k < kMU; ++k)
+                if (s0 + k < nseg) ss = fmaf(pp[k].y, exp_shift(pp[k].x - mm), ss);
+        }
+        if (ss < kTinyW) s_fix[atomicAdd(&s_nfix, 1)] = int(threadIdx.x);
+        else a.pairs[idx] = make_float2(mm, ss);
     }
-    float ss = 0.0f;
-    for (int s0 = 0; s0 < nseg; s0 += kMU) {
-        float2 pp[kMU];
-#pragma unroll
-        for (int k = 0; k < kMU; ++k)
-            pp[k] = s0 + k < nseg ? __ldcg(pc + int64_t(s0 + k) * a.m) : make_float2(kNegBig, 0.0f);
-#pragma unroll
-        for (int k = 0; k < kMU; ++k)
-            if (s0 + k < nseg) ss = fmaf(pp[k].y, exp_shift(pp[k].x - mm), ss);
+    __syncthreads();
+    const int nfix = s_nfix;
+    for (int k = int(threadIdx.x >> 5); k < nfix; k += kMT / 32) {
+        const int64_t j = int64_t(blockIdx.x) * kMT + s_fix[k];
+        const int b = int(j / a.m);
+        const float2 p = w_exact_pair(a.X, a.u2, a.kinv, b, a.n, a.m, j - int64_t(b) * a.m);
+        if ((threadIdx.x & 31) == 0) a.pairs[j] = p;
     }
-    a.pairs[int64_t(b) * a.m + col] = make_float2(mm, ss);
 }
 
 // Stages plus the pair-exchange slots for batches of R rows.
@@ -579,16 +601,6 @@ int wide_shape(int64_t mc) {
     if (pref == kShapeA) return pref;
     if (pref == kShapeB && mc <= 4096) return pref;
     return mc <= 4096 ? kShapeB : kShapeA;
-}
-
-// DOT_B200_WIDE_WAIT = 0 | 1 | 2 selects the barrier wait form (tuning runs).
-int wide_wait_mode() {
-    static int v = [] {
-        const char* e = std::getenv("DOT_B200_WIDE_WAIT");
-        const int x = e ? std::atoi(e) : 0;
-        return (x >= 0 && x <= 2) ? x : 0;
-    }();
-    return v;
 }
 
 template <class CFG>
@@ -744,7 +756,6 @@ int sk_wide_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     w.maxseg = int(wide_seg_bound(a.B, a.n, a.m));
     w.pairs = nullptr;
     w.err = a.status + 3;
-    w.wmode = wide_wait_mode();
     const int64_t rows = a.B * a.n;
     const bool hist = a.u_hist != nullptr && a.v_hist != nullptr;
     ProfScope ps(DOT_K_SK_FWD_ITER, st, a.n_iters);
@@ -762,7 +773,7 @@ int sk_wide_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
 
 // One row half-step and the shard's column pairs for a row shard.
 int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
-                       const float* v2, float* u2, float2* pairs, void* ws, cudaStream_t st) {
+                       const float* v2, float* u2, float2* pairs, int32_t* err, void* ws, cudaStream_t st) {
     const WidePlan p = wide_plan(B, n, m);
     if (p.maxseg > wide_seg_bound(B, n, m))
         return fail(DOT_ERR_WORKSPACE, "wide Sinkhorn: more row segments than the workspace holds");
@@ -787,11 +798,13 @@ int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def
     w.G = p.G;
     w.maxseg = int(wide_seg_bound(B, n, m));
     w.pairs = pairs;
-    w.err = nullptr;
-    w.wmode = wide_wait_mode();
-    ProfScope ps(DOT_K_SK_FWD_ITER, st);
-    launch_any(w, st);
+    w.err = err;
+    {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st);
+        launch_any(w, st);
+    }
     // the pair merge starts (PDL) while the iteration kernel drains
+    ProfScope ps(DOT_K_SK_EXCHANGE, st);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -141,61 +141,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     return false;
 }
 
-// Bounded wait in one of three forms (wide-row kernel tuning): 0 suspending
-// try_wait with the kSuspendNs hint, 1 try_wait with the system's default
-// time limit, 2 test_wait polling.  `cluster` selects cluster-scope acquire.
-__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, int mode, bool cluster) {
-    uint32_t ok;
-    if (mode == 0) return cluster ? mbar_try_cluster(bar, parity) : mbar_try(bar, parity);
-    if (mode == 1) {
-        if (cluster)
-            asm volatile(
-                "{\n\t.reg .pred p;\n\t"
-                "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-                "selp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(ok)
-                : "r"(smem_u32(bar)), "r"(parity)
-                : "memory");
-        else
-            asm volatile(
-                "{\n\t.reg .pred p;\n\t"
-                "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                "selp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(ok)
-                : "r"(smem_u32(bar)), "r"(parity)
-                : "memory");
-        return ok != 0;
-    }
-    if (cluster)
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-    else
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-    return ok != 0;
-}
-// Gives up after 2^19 (modes 0, 1) or 2^24 (mode 2) polls, records
-// kErrBarrierTimeout in *err and returns false.
-__device__ __forceinline__ bool mbar_wait_mode(uint64_t* bar, uint32_t parity, int mode, bool cluster,
-                                               int32_t* err) {
-    const uint32_t lim = mode == 2 ? (1u << 24) : (1u << 19);
-    for (uint32_t i = 0; i < lim; ++i) {
-        if (mbar_poll(bar, parity, mode, cluster)) return true;
-    }
-    if (err != nullptr) atomicOr(err, kErrBarrierTimeout);
-    return false;
-}
-
 // Address of the same shared-memory object in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank) {
     uint32_t a;

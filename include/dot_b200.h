@@ -104,7 +104,10 @@ DOT_API int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_
  *    (e.g. B=256 x 512 x 512 and B=4096 x 128 x 128 fit).
  *  * The first call on a device looks up the array's device address with that
  *    device current and caches it; make that first call before any stream
- *    capture begins.
+ *    capture begins.  The cache is never invalidated: after cudaDeviceReset,
+ *    or anything else that destroys and re-creates the device's primary
+ *    context, the cached address is stale -- do not call this entry point
+ *    again in that process.
  *  * All calls share the one array per device, and it keeps the last call's
  *    contents (the call clears what must start at zero itself).  Calls that
  *    overlap on the GPU -- on different streams, or from several host threads
@@ -180,58 +183,71 @@ DOT_API int dot_sinkhorn_bwd_unrolled(const float* X, float score_sign, const fl
  * One forward iteration of dot_sinkhorn_fwd split at its only exchange point,
  * for a shard holding rows [r0, r0 + n) of each problem's n_total x m matrix.
  * Per iteration every shard runs
- *     dot_sinkhorn_rows          u_i = log_a_i - LSE_j(K_ij + v_j)      (local rows)
- *     dot_sinkhorn_col_partials  (max_j, sum_j) of LSE_i(K_ij + u_i)     (local rows)
- *     all-reduce MAX of max_j -> gmax_j   (caller, e.g. NCCL)
- *     dot_sinkhorn_col_rescale   sum_j *= exp(max_j - gmax_j)
- *     all-reduce SUM of sum_j -> gsum_j   (caller)
- *     dot_sinkhorn_col_finish    v_j = log_b_j - (gmax_j + log(max(gsum_j, 1e-12)))
- * and finally dot_sinkhorn_plan for its rows (plus an all-reduce SUM of the
- * per-shard costs).  Same arithmetic as the reference's row/column update
- * kernels (src/sinkhorn/kernels.cu:503-545, 629-753 -- its split-column
- * phase1/phase2 merge is the same max-then-rescaled-sum combine) and
- * materialisation (kernels.cu:755-775); the reference itself has no
- * multi-GPU path.
- */
-DOT_API int dot_sinkhorn_rows(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n,
-                              int64_t m, int64_t n_total, float tau, const float* pot_v, float* pot_u,
-                              void* stream);
-DOT_API size_t dot_sinkhorn_col_partials_workspace_bytes(int64_t B, int64_t n, int64_t m);
-DOT_API int dot_sinkhorn_col_partials(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n,
-                                      int64_t m, float tau, float* col_max, float* col_sum, void* workspace,
-                                      size_t workspace_bytes, void* stream);
-DOT_API int dot_sinkhorn_col_rescale(const float* col_max, float* col_sum, const float* global_max,
-                                     int64_t count, void* stream);
-DOT_API int dot_sinkhorn_col_finish(const float* global_max, const float* global_sum, const float* log_b,
-                                    int64_t B, int64_t m, float* pot_v, void* stream);
-/*
- * One-collective form of the same exchange: each shard writes its column
- * (max, sum) pairs with dot_sinkhorn_col_pairs (pairs [B,m,2]), the caller
- * gathers every shard's pairs in shard order into [parts,B,m,2] (e.g. an NCCL
- * all-gather), and dot_sinkhorn_col_merge merges them in that order and
- * writes v_j = log_b_j - LSE (log_b NULL: -log(m)).  Every shard computes the
- * same v bit for bit.  Same combine as above; no counterpart in the reference.
- */
-/*
- * dot_sinkhorn_rows followed by dot_sinkhorn_col_pairs in one call; for wide
- * rows (8192 <= m <= 65536, m % 32 == 0) a single pass over the shard on
- * thread-block clusters (the matrix is read once per iteration instead of
- * twice).  No counterpart in the reference (it has no multi-GPU path).
+ *     dot_sinkhorn_rows_colpairs   u_i = log_a_i - LSE_j(K_ij + v_j) for its rows, then
+ *                                  its column pairs (max_j, sum_j) of LSE_i(K_ij + u_i)
+ *     gather of every shard's pairs in shard order (caller, e.g. NCCL all-gather)
+ *     dot_sinkhorn_col_merge       v_j = log_b_j - LSE over the gathered pairs
+ * and finally dot_sinkhorn_plan for its rows (plus a sum of the per-shard
+ * costs).  Same arithmetic as the reference's row/column update kernels
+ * (src/sinkhorn/kernels.cu:503-545, 629-753 -- its split-column phase1/phase2
+ * merge is the same max-then-rescaled-sum combine) and materialisation
+ * (kernels.cu:755-775); the reference itself has no multi-GPU path.
+ *
+ * dot_sinkhorn_rows_colpairs: pairs [B,m,2]; for wide rows (8192 <= m <=
+ * 65536, m % 32 == 0) a single pass over the shard on thread-block clusters
+ * (the matrix is read once per iteration instead of twice).  status is a
+ * device int32 error word: a bounded wait inside the kernels that expires
+ * ORs 0x100 into it (zero it before the first iteration, read it after the
+ * last).  dot_sinkhorn_col_merge merges [parts,B,m,2] in part order and
+ * writes v (log_b NULL: -log(m)); every shard computes the same v bit for bit.
  */
 DOT_API size_t dot_sinkhorn_rows_colpairs_workspace_bytes(int64_t B, int64_t n, int64_t m);
 DOT_API int dot_sinkhorn_rows_colpairs(const float* X, float score_sign, const float* log_a, int64_t B, int64_t n,
                                        int64_t m, int64_t n_total, float tau, const float* pot_v, float* pot_u,
-                                       float* pairs, void* workspace, size_t workspace_bytes, void* stream);
-DOT_API size_t dot_sinkhorn_col_pairs_workspace_bytes(int64_t B, int64_t n, int64_t m);
-DOT_API int dot_sinkhorn_col_pairs(const float* X, float score_sign, const float* pot_u, int64_t B, int64_t n,
-                                   int64_t m, float tau, float* pairs, void* workspace, size_t workspace_bytes,
-                                   void* stream);
+                                       float* pairs, int32_t* status, void* workspace, size_t workspace_bytes,
+                                       void* stream);
 DOT_API int dot_sinkhorn_col_merge(const float* pairs, int parts, const float* log_b, int64_t B, int64_t m,
                                    float* pot_v, void* stream);
 DOT_API size_t dot_sinkhorn_plan_workspace_bytes(int64_t B, int64_t n, int64_t m);
 DOT_API int dot_sinkhorn_plan(const float* X, float score_sign, const float* pot_u, const float* pot_v, int64_t B,
                               int64_t n, int64_t m, float tau, int out_mode, float* out, float* cost,
                               void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The whole row-sharded forward in one call, with the exchange done by the
+ * library: n_iters iterations of dot_sinkhorn_rows_colpairs on this rank's
+ * rows, an NCCL all-gather of every rank's column pairs (in place, rank
+ * order) and dot_sinkhorn_col_merge; then, if out != NULL, the plan rows
+ * (dot_sinkhorn_plan) and, if cost != NULL, the global cost sum_ij P_ij X_ij
+ * (an NCCL all-reduce of the per-rank sums).  nccl_comm is an ncclComm_t
+ * whose rank order is the row order of the shards (NULL: a single shard, no
+ * collective).  X [B,n,m] holds this rank's rows of each [B,n_total,m]
+ * problem (n may be 0); log_a [B,n] this rank's rows of the row marginals and
+ * log_b [B,m] the column marginals (NULL: uniform over n_total / m).  pot_u
+ * [B,n], pot_v [B,m] receive the potentials (pot_v identical on every rank);
+ * status is one device int32 word: 0, or 0x100 if a bounded wait expired.
+ * Every rank of the communicator must make the same call (same B, m, n_total,
+ * tau, n_iters, and out/cost both given or both NULL).  No counterpart in the
+ * reference (it has no multi-GPU path); the per-rank arithmetic is that of the
+ * reference's row/column updates and materialisation (kernels.cu:503-775).
+ */
+DOT_API size_t dot_sinkhorn_fwd_rowshard_workspace_bytes(int64_t B, int64_t n, int64_t m, int nranks);
+DOT_API int dot_sinkhorn_fwd_rowshard(const float* X, float score_sign, const float* log_a, const float* log_b,
+                                      int64_t B, int64_t n, int64_t m, int64_t n_total, float tau, int n_iters,
+                                      void* nccl_comm, float* out, float* cost, float* pot_u, float* pot_v,
+                                      int32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * NCCL communicator for dot_sinkhorn_fwd_rowshard, for callers that have
+ * none: rank 0 creates a 128-byte id, the caller hands it to every rank (any
+ * channel), and each rank calls dot_nccl_comm_init with its CUDA device
+ * current (collective: it returns once all nranks have joined).  NCCL is
+ * loaded at run time (the process's copy of libnccl.so.2 if one is loaded);
+ * without it these return DOT_ERR_UNSUPPORTED.
+ */
+DOT_API int dot_nccl_unique_id(void* id_out);
+DOT_API int dot_nccl_comm_init(void** comm_out, int nranks, const void* id, int rank);
+DOT_API int dot_nccl_comm_destroy(void* comm);
 
 /* ------------------------------------------------------------------------ */
 /* Bidirectional softmax                                                     */
@@ -287,7 +303,9 @@ enum dot_kclass {
     DOT_K_SK_RESIDENT = 4,   /* on-chip resident solver kernels              */
     DOT_K_BS_FWD = 5,        /* bidirectional softmax forward                */
     DOT_K_BS_BWD = 6,        /* bidirectional softmax backward               */
-    DOT_K_NCLASS = 7
+    DOT_K_SK_EXCHANGE = 7,   /* row-shard column exchange: pair merges and   */
+                             /* the all-gather between the shards            */
+    DOT_K_NCLASS = 8
 };
 
 /* Start counting launches per class; with time_events != 0 also bracket each

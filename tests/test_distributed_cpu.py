@@ -1,17 +1,18 @@
 """Host-side logic of the multi-GPU drivers, run as world_size-2 gloo ranks on
-CPU: shard ranges, and the exactness of the two-all-reduce combine of
-per-rank column (max, sum) partials (the rescale step is stood in for by a
-torch expression here; on the GPU it is dot_sinkhorn_col_rescale)."""
+CPU: shard ranges, the hand-over of the NCCL id that the row-sharded solver's
+communicator is built from, and the batch-sharded solver's split and gathers
+(with the CPU oracle standing in for the GPU solve)."""
 
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from dot_b200.distributed import combine_column_partials, gather_column_pairs, shard_range
+from dot_b200.distributed import broadcast_unique_id, nccl_communicator, shard_range
 
 
 def test_shard_range_partitions_exactly():
@@ -27,85 +28,94 @@ def test_shard_range_partitions_exactly():
         shard_range(10, 2, 2)
 
 
+def test_single_rank_needs_no_communicator():
+    assert nccl_communicator() is None
+    assert broadcast_unique_id(lambda: b"x" * 128) == b"x" * 128
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _rescale_cpu(col_max, col_sum, gmax):
-    col_sum.mul_(torch.exp(col_max - gmax))
-
-
-def _worker(rank, world, port, out):
+def _init(rank, world, port):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=__import__("datetime").timedelta(seconds=60))
+
+
+def _worker_id(rank, world, port, out):
+    _init(rank, world, port)
     try:
-        g = torch.Generator().manual_seed(0)
-        n, m = 37, 11
-        t = torch.randn(n, m, generator=g, dtype=torch.float64) * 30.0   # wide range: partial maxima differ
-        lo, hi = shard_range(n, rank, world)
-        local = t[lo:hi]
-        cmax = local.max(0).values.float()
-        csum = torch.exp(local - local.max(0).values).sum(0).float()
-        gmax, gsum = combine_column_partials(cmax, csum, _rescale_cpu)
-        lse = (gmax.double() + torch.log(gsum.double()))
-        ref = torch.logsumexp(t, dim=0)
-        out[rank] = float((lse - ref).abs().max())
+        calls = []
+
+        def make():
+            calls.append(rank)
+            return bytes(np.random.default_rng(1234 + rank).integers(0, 256, 128, dtype=np.uint8))
+
+        out[rank] = (broadcast_unique_id(make), list(calls))
     finally:
         dist.destroy_process_group()
 
 
-def _merge_cpu(gathered):
-    """Rank-order merge of gathered (max, sum) pairs [world, m, 2] (the
-    arithmetic of dot_sinkhorn_col_merge, in float64 here)."""
-    mm = torch.full(gathered.shape[1:-1], -3.4e38, dtype=torch.float64)
-    ss = torch.zeros_like(mm)
-    for p in gathered.double():
-        mn = torch.maximum(mm, p[..., 0])
-        ss = ss * torch.exp(mm - mn) + p[..., 1] * torch.exp(p[..., 0] - mn)
-        mm = mn
-    return mm + torch.log(ss)
+def test_unique_id_reaches_every_rank_gloo():
+    """Only rank 0 makes the id; every rank receives the same 128 bytes."""
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker_id, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    assert len(out) == world
+    assert out[0][0] == out[1][0] and len(out[0][0]) == 128
+    assert out[0][1] == [0] and out[1][1] == []
 
 
-def _worker_pairs(rank, world, port, out):
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=__import__("datetime").timedelta(seconds=60))
+class _Result:
+    def __init__(self, P, cost):
+        self.transport_plan = P
+        self.cost = cost
+
+
+def _oracle_solve(C, reg, n_iters, a=None, b=None, **kw):
+    from oracle import oracle as O
+
+    B = C.shape[0]
+    a2 = None if a is None else (a if a.dim() == 2 else a.expand(B, -1)).numpy()
+    b2 = None if b is None else (b if b.dim() == 2 else b.expand(B, -1)).numpy()
+    r = O.sinkhorn_api(C.numpy(), reg, n_iters, a2, b2, with_grad=False)
+    return _Result(torch.from_numpy(r["P"]), torch.from_numpy(np.asarray(r["cost"], np.float32)))
+
+
+def _worker_batch(rank, world, port, out):
+    from dot_b200.distributed import sinkhorn_batchshard
+
+    _init(rank, world, port)
     try:
-        g = torch.Generator().manual_seed(1)
-        n, m = 41, 13
-        t = torch.randn(n, m, generator=g, dtype=torch.float64) * 30.0
-        lo, hi = shard_range(n, rank, world)
-        local = t[lo:hi]
-        pairs = torch.stack([local.max(0).values, torch.exp(local - local.max(0).values).sum(0)], -1).float()
-        gathered, parts = gather_column_pairs(pairs)
-        assert parts == world and tuple(gathered.shape) == (world, m, 2)
-        lse = _merge_cpu(gathered)
-        out[rank] = (float((lse - torch.logsumexp(t, dim=0)).abs().max()), lse.numpy().tobytes())
+        g = torch.Generator().manual_seed(3)
+        B, n, m = 5, 9, 7           # 5 problems over 2 ranks: 3 + 2
+        C = torch.rand(B, n, m, generator=g)
+        b = torch.full((m,), 1.0 / m)
+        r = sinkhorn_batchshard(C, reg=0.3, n_iters=15, b=b, gather_plans=True, device="cpu", solve=_oracle_solve)
+        out[rank] = (r["lo"], r["hi"], r["costs"].numpy(), r["plans"].numpy(), r["cost"].numpy())
     finally:
         dist.destroy_process_group()
 
 
-def test_gather_column_pairs_two_ranks_gloo():
-    """One all-gather of (max, sum) pairs, merged in rank order, gives the
-    exact column LSE and the same bits on every rank."""
+def test_batchshard_splits_and_gathers_gloo():
+    """Each rank solves its shard_range slice; the gathered costs and plans
+    equal one solve of the whole batch, on every rank, uneven split included."""
     world = 2
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_worker_pairs, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_worker_batch, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
     assert len(out) == world
-    assert max(v[0] for v in out.values()) < 1e-5
-    assert out[0][1] == out[1][1]
-
-
-def test_combine_column_partials_two_ranks_gloo():
-    world = 2
-    mgr = mp.get_context("spawn").Manager()
-    out = mgr.dict()
-    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
-    assert len(out) == world
-    assert max(out.values()) < 1e-5
+    g = torch.Generator().manual_seed(3)
+    C = torch.rand(5, 9, 7, generator=g)
+    ref = _oracle_solve(C, 0.3, 15)
+    assert (out[0][0], out[0][1], out[1][0], out[1][1]) == (0, 3, 3, 5)
+    for rank in range(world):
+        lo, hi, costs, plans, local = out[rank]
+        np.testing.assert_array_equal(costs, ref.cost.numpy())
+        np.testing.assert_array_equal(plans, ref.transport_plan.numpy())
+        np.testing.assert_array_equal(local, ref.cost.numpy()[lo:hi])

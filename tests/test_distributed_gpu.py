@@ -1,6 +1,7 @@
-"""Row-sharded Sinkhorn over NCCL (2 ranks, one GPU each) against the
-single-GPU forward on the same problem (skipped with fewer than 2 GPUs), and
-the same loop on one GPU without a process group."""
+"""Row-sharded Sinkhorn (dot_sinkhorn_fwd_rowshard: the library's own NCCL
+all-gather per iteration) on 2 ranks, one GPU each, against the single-GPU
+forward on the same problem (skipped with fewer than 2 GPUs), and the same
+solver on one GPU without a process group (one shard, no collective)."""
 
 import os
 import socket
@@ -18,13 +19,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out, shape=(2, 1030, 2000)):
+def _worker(rank, world, port, out, shape=(2, 1030, 2000), reg=0.05, T=30, cube=False):
     import datetime
 
     import torch.distributed as dist
 
     from dot_b200 import ops
-    from dot_b200.distributed import shard_range, sinkhorn_rowshard
+    from dot_b200.distributed import release_communicators, shard_range, sinkhorn_rowshard
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -33,10 +34,8 @@ def _worker(rank, world, port, out, shape=(2, 1030, 2000)):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
-        g = torch.Generator().manual_seed(0)
         B, n, m = shape
-        reg, T = 0.05, 30
-        C = torch.rand(B, n, m, generator=g)
+        C = _cost(B, n, m, cube)
         lo, hi = shard_range(n, rank, world)
         res = sinkhorn_rowshard(C[:, lo:hi].cuda(), reg, T, n_total=n)
         torch.cuda.synchronize()
@@ -48,7 +47,17 @@ def _worker(rank, world, port, out, shape=(2, 1030, 2000)):
         out[rank] = (dP, dv, dc)
         dist.barrier()
     finally:
+        release_communicators()
         dist.destroy_process_group()
+
+
+def _cost(B, n, m, cube):
+    g = torch.Generator().manual_seed(0)
+    if not cube:
+        return torch.rand(B, n, m, generator=g)
+    x = torch.rand(B, n, 3, generator=g)
+    y = torch.rand(B, m, 3, generator=g)
+    return torch.cdist(x, y).square().float()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -79,19 +88,36 @@ def test_rowshard_wide_rows_two_gpus_matches_single_gpu():
         assert dc < 1e-5, (rank, dc)
 
 
-@pytest.mark.parametrize("shape", [(3, 700, 8192), (1, 514, 16384)])
-def test_rowshard_wide_rows_one_rank_matches_forward(shape):
-    """Without a process group the row-shard loop runs on one GPU with a
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_rowshard_cfg5_regime_two_gpus_matches_single_gpu():
+    """configs[4]'s regime (U[0,1)^3 squared distances, reg 0.01, 32768
+    columns) split over two GPUs."""
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), out, (1, 1200, 32768), 0.01, 20, True), nprocs=world,
+                       join=True, start_method="spawn")
+    assert len(out) == world
+    for rank, (dP, dv, dc) in out.items():
+        assert dP < 1e-5, (rank, dP)
+        assert dv < 1e-4, (rank, dv)
+        assert dc < 1e-5, (rank, dc)
+
+
+@pytest.mark.parametrize("shape,reg,cube", [((3, 700, 8192), 0.05, False), ((1, 514, 16384), 0.05, False),
+                                            ((1, 300, 32768), 0.01, True)], ids=["8192x3", "16384", "32768-cube"])
+def test_rowshard_wide_rows_one_rank_matches_forward(shape, reg, cube):
+    """Without a process group the row-shard solver runs on one GPU with a
     single part: the cluster kernel publishes its segment partials, the pair
     merge kernel combines them and the column merge writes v.  Several
-    problems per cluster range (B=3) cover partials flushed mid-range."""
+    problems per cluster range (B=3) cover partials flushed mid-range; the
+    32768-column case is configs[4]'s kernel instantiation and regime."""
     from dot_b200 import ops
     from dot_b200.distributed import sinkhorn_rowshard
 
-    g = torch.Generator().manual_seed(1)
     B, n, m = shape
-    reg, T = 0.05, 20
-    C = torch.rand(B, n, m, generator=g).cuda()
+    T = 20
+    C = _cost(B, n, m, cube).cuda()
     res = sinkhorn_rowshard(C, reg, T, n_total=n)
     P_ref, cost_ref, _, v_ref, _ = ops.sinkhorn_forward_raw(C, -1.0, reg, T, want_cost=True)
     torch.cuda.synchronize()
