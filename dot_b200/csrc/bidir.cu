@@ -96,11 +96,11 @@ template <typename T>
 __global__ void __launch_bounds__(kColWarps * 32)
 bs_col_stats_kernel(const T* __restrict__ sim, const int32_t* __restrict__ lengths, int64_t L1,
                     int64_t L2, float invT, int64_t rows_per_chunk, int chunks,
-                    float2* __restrict__ cstat, float2* __restrict__ part) {
+                    float2* __restrict__ cstat, float2* __restrict__ part, int64_t b0) {
     __shared__ float sm_M[kColWarps][kColTile];
     __shared__ float sm_S[kColWarps][kColTile];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t b = blockIdx.z, chunk = blockIdx.y;
+    const int64_t b = b0 + blockIdx.z, chunk = blockIdx.y;
     const int64_t cbase = int64_t(blockIdx.x) * kColTile;
     int64_t l1, l2;
     window(lengths, b, L1, L2, l1, l2);
@@ -227,10 +227,10 @@ bs_bwd_coldot_kernel(const T* __restrict__ sim, const float* __restrict__ gout,
                      const int32_t* __restrict__ lengths, int64_t L1, int64_t L2, float invT,
                      const float2* __restrict__ rstat, const float2* __restrict__ cstat,
                      int64_t rows_per_chunk, int chunks, float* __restrict__ cdot,
-                     float* __restrict__ part) {
+                     float* __restrict__ part, int64_t b0) {
     __shared__ float sm[kColWarps][kColTile];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t b = blockIdx.z, chunk = blockIdx.y;
+    const int64_t b = b0 + blockIdx.z, chunk = blockIdx.y;
     const int64_t cbase = int64_t(blockIdx.x) * kColTile;
     int64_t l1, l2;
     window(lengths, b, L1, L2, l1, l2);
@@ -379,9 +379,11 @@ int bs_fwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int
     }
     {
         ProfScope ps(DOT_K_BS_FWD, st);
-        dim3 g(unsigned(ceil_div(L2, kColTile)), unsigned(chunks), unsigned(B));
-        bs_col_stats_kernel<T><<<g, kColWarps * 32, 0, st>>>(sim, lengths, L1, L2, invT, rpc, chunks, cstat,
-                                                             w.part);
+        for (int64_t b0 = 0; b0 < B; b0 += kMaxGridZ) {
+            const dim3 g(unsigned(ceil_div(L2, kColTile)), unsigned(chunks), unsigned(std::min<int64_t>(kMaxGridZ, B - b0)));
+            bs_col_stats_kernel<T><<<g, kColWarps * 32, 0, st>>>(sim, lengths, L1, L2, invT, rpc, chunks, cstat,
+                                                                 w.part, b0);
+        }
     }
     if (chunks > 1) {
         ProfScope ps(DOT_K_BS_FWD, st);
@@ -411,9 +413,11 @@ int bs_bwd_impl(const T* sim, const int32_t* lengths, int64_t B, int64_t L1, int
     }
     {
         ProfScope ps(DOT_K_BS_BWD, st);
-        dim3 g(unsigned(ceil_div(L2, kColTile)), unsigned(chunks), unsigned(B));
-        bs_bwd_coldot_kernel<T><<<g, kColWarps * 32, 0, st>>>(sim, gout, lengths, L1, L2, invT, rstat, cstat,
-                                                              rpc, chunks, w.cdot, w.part);
+        for (int64_t b0 = 0; b0 < B; b0 += kMaxGridZ) {
+            const dim3 g(unsigned(ceil_div(L2, kColTile)), unsigned(chunks), unsigned(std::min<int64_t>(kMaxGridZ, B - b0)));
+            bs_bwd_coldot_kernel<T><<<g, kColWarps * 32, 0, st>>>(sim, gout, lengths, L1, L2, invT, rstat, cstat,
+                                                                  rpc, chunks, w.cdot, w.part, b0);
+        }
     }
     if (chunks > 1) {
         ProfScope ps(DOT_K_BS_BWD, st);

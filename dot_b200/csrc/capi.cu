@@ -103,8 +103,6 @@ bool bad_float(float x) { return !std::isfinite(x); }
 
 int check_dims(int64_t B, int64_t n, int64_t m) {
     if (B < 0 || n < 0 || m < 0) return fail(DOT_ERR_INVALID, "negative dimension");
-    // int32 grid limits of the column kernels: B <= 65535 and n*m per problem.
-    if (B > 65535) return fail(DOT_ERR_UNSUPPORTED, "batch larger than 65535 is not supported");
     return DOT_OK;
 }
 
@@ -166,6 +164,11 @@ int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_a, const
     a.la = log_a;
     a.lb = log_b;
     if (tol == 0.0f && sk_resident_supported(n, m)) return sk_resident_fwd(a, workspace, st);
+    if (tol == 0.0f && sk_cluster_supported(B, n, m, X)) {
+        rc = sk_cluster_fwd(a, st);
+        if (rc != DOT_ERR_UNSUPPORTED) return rc;
+        clear_error();
+    }
     return sk_stream_fwd(a, workspace, st);
 }
 
@@ -289,6 +292,11 @@ int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P, const flo
     a.gX = grad_X;
     a.gtau = grad_tau;
     if (sk_resident_supported(n, m)) return sk_resident_bwd(a, workspace, st);
+    if (sk_cluster_supported(B, n, m, P) && workspace != nullptr) {
+        rc = sk_cluster_bwd(a, static_cast<int32_t*>(workspace), st);
+        if (rc != DOT_ERR_UNSUPPORTED) return rc;
+        clear_error();
+    }
     return sk_stream_bwd(a, workspace, st);
 }
 

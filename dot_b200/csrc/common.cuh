@@ -148,6 +148,11 @@ __device__ __forceinline__ float kplus(float x, float kinv, float w) {
     return __fadd_rn(__fmul_rn(x, kinv), w);
 }
 
+// Column kernels put the batch index in gridDim.z, at most kMaxGridZ per
+// launch; larger batches are launched in slices, each kernel adding the
+// slice's first batch index b0 to blockIdx.z.
+constexpr int64_t kMaxGridZ = 65535;
+
 __device__ __forceinline__ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

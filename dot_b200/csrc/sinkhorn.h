@@ -113,4 +113,14 @@ int sk_resident_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 size_t sk_resident_bwd_ws(int64_t B, int64_t n, int64_t m);
 int sk_resident_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
 
+// Cluster-resident solvers (sinkhorn_cluster.cu): one thread-block cluster per
+// problem, the problem's rows spread over the cluster's shared memory, all
+// iterations on chip; m % 4 == 0, m <= 1024, tol == 0.  The entry points
+// return DOT_ERR_UNSUPPORTED (having launched nothing) when the device cannot
+// hold a cluster of the configuration; the caller then streams.  No workspace
+// beyond the backward's error word.
+bool sk_cluster_supported(int64_t B, int64_t n, int64_t m, const void* data);
+int sk_cluster_fwd(const SkFwdArgs& a, cudaStream_t st);
+int sk_cluster_bwd(const SkBwdArgs& a, int32_t* err, cudaStream_t st);
+
 }  // namespace dotb

@@ -139,12 +139,12 @@ __global__ void __launch_bounds__(kColWarps * 32)
 sk_col_kernel(const float* __restrict__ X, float kinv, const float* __restrict__ u2,
               const float* __restrict__ lb, float lb_def, float* __restrict__ v2,
               float2* __restrict__ part, int64_t n, int64_t m, int64_t rows_per_chunk,
-              int chunks, SkCtl ctl, float2* __restrict__ pair_out) {
+              int chunks, SkCtl ctl, float2* __restrict__ pair_out, int64_t b0) {
     __shared__ float sm_M[kColWarps][kColTile];
     __shared__ float sm_S[kColWarps][kColTile];
     if (ctl_done(ctl)) return;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t b = blockIdx.z, chunk = blockIdx.y;
+    const int64_t b = b0 + blockIdx.z, chunk = blockIdx.y;
     const int64_t cbase = int64_t(blockIdx.x) * kColTile;
     const int64_t r0 = chunk * rows_per_chunk;
     const int64_t r1 = min(n, r0 + rows_per_chunk);
@@ -353,10 +353,10 @@ __global__ void __launch_bounds__(kColWarps * 32)
 skb_col_prep_kernel(const float* __restrict__ X, const float* __restrict__ P,
                     const float* __restrict__ gP, const float* __restrict__ gcost,
                     float2* __restrict__ cinv, float2* __restrict__ part, int64_t n, int64_t m,
-                    int64_t rows_per_chunk, int chunks) {
+                    int64_t rows_per_chunk, int chunks, int64_t b0) {
     __shared__ float2 sm[kColWarps][kColTile];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t b = blockIdx.z, chunk = blockIdx.y;
+    const int64_t b = b0 + blockIdx.z, chunk = blockIdx.y;
     const int64_t cbase = int64_t(blockIdx.x) * kColTile;
     const int64_t r0 = chunk * rows_per_chunk, r1 = min(n, r0 + rows_per_chunk);
     const float gc = gcost ? gcost[b] : 0.0f;
@@ -439,10 +439,10 @@ __global__ void __launch_bounds__(kColWarps * 32)
 skb_col_iter_kernel(const float* __restrict__ P, const float* __restrict__ lam,
                     const float2* __restrict__ cinv, float* __restrict__ mu,
                     float* __restrict__ part, int64_t n, int64_t m, int64_t rows_per_chunk,
-                    int chunks) {
+                    int chunks, int64_t b0) {
     __shared__ float sm[kColWarps][kColTile];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t b = blockIdx.z, chunk = blockIdx.y;
+    const int64_t b = b0 + blockIdx.z, chunk = blockIdx.y;
     const int64_t cbase = int64_t(blockIdx.x) * kColTile;
     const int64_t r0 = chunk * rows_per_chunk, r1 = min(n, r0 + rows_per_chunk);
     const float* Pb = P + b * n * m;
@@ -633,8 +633,11 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
         }
         {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
-            sk_col_kernel<<<col_grid, kColWarps * 32, 0, st>>>(a.X, a.kinv, a.u2, a.lb, a.lb_def, a.v2,
-                                                               w.part, a.n, a.m, rpc, chunks, ctl, nullptr);
+            for (int64_t b0 = 0; b0 < a.B; b0 += kMaxGridZ) {
+                const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, a.B - b0)));
+                sk_col_kernel<<<gz, kColWarps * 32, 0, st>>>(a.X, a.kinv, a.u2, a.lb, a.lb_def, a.v2,
+                                                                   w.part, a.n, a.m, rpc, chunks, ctl, nullptr, b0);
+            }
         }
         if (chunks > 1) {
             ProfScope ps(DOT_K_SK_FWD_ITER, st);
@@ -710,8 +713,11 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
     }
     {
         ProfScope ps(DOT_K_SK_BWD_EPI, st);
-        skb_col_prep_kernel<<<col_grid, kColWarps * 32, 0, st>>>(a.X, a.P, a.gP, a.gcost, w.cinv, w.part2,
-                                                                 a.n, a.m, rpc, chunks);
+        for (int64_t b0 = 0; b0 < a.B; b0 += kMaxGridZ) {
+            const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, a.B - b0)));
+            skb_col_prep_kernel<<<gz, kColWarps * 32, 0, st>>>(a.X, a.P, a.gP, a.gcost, w.cinv, w.part2,
+                                                                     a.n, a.m, rpc, chunks, b0);
+        }
     }
     if (chunks > 1) {
         ProfScope ps(DOT_K_SK_BWD_EPI, st);
@@ -736,8 +742,11 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
         }
         {
             ProfScope ps(DOT_K_SK_BWD_ITER, st);
-            skb_col_iter_kernel<<<col_grid, kColWarps * 32, 0, st>>>(a.P, w.lam, w.cinv, w.mu, w.part1,
-                                                                     a.n, a.m, rpc, chunks);
+            for (int64_t b0 = 0; b0 < a.B; b0 += kMaxGridZ) {
+                const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, a.B - b0)));
+                skb_col_iter_kernel<<<gz, kColWarps * 32, 0, st>>>(a.P, w.lam, w.cinv, w.mu, w.part1,
+                                                                         a.n, a.m, rpc, chunks, b0);
+            }
         }
         if (chunks > 1) {
             ProfScope ps(DOT_K_SK_BWD_ITER, st);
@@ -791,8 +800,11 @@ int sk_split_colpairs(const float* X, float kinv, const float* u2, int64_t B, in
     const dim3 col_grid(unsigned(ceil_div(m, kColTile)), unsigned(chunks), unsigned(B));
     {
         ProfScope ps(DOT_K_SK_FWD_ITER, st);
-        sk_col_kernel<<<col_grid, kColWarps * 32, 0, st>>>(X, kinv, u2, nullptr, 0.0f, nullptr, part, n, m, rpc,
-                                                           chunks, ctl, pairs);
+        for (int64_t b0 = 0; b0 < B; b0 += kMaxGridZ) {
+            const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, B - b0)));
+            sk_col_kernel<<<gz, kColWarps * 32, 0, st>>>(X, kinv, u2, nullptr, 0.0f, nullptr, part, n, m, rpc,
+                                                               chunks, ctl, pairs, b0);
+        }
     }
     if (chunks > 1) {
         ProfScope ps(DOT_K_SK_FWD_ITER, st);

@@ -47,10 +47,10 @@ __global__ void sku_init_kernel(const float* __restrict__ X, const float* __rest
 // Column sums of Gamma over a row chunk: grid (ceil(m/128), chunks, B).
 __global__ void __launch_bounds__(kUT)
 sku_colsum_kernel(const float* __restrict__ Gm, int64_t n, int64_t m, int64_t rows_per_chunk, int chunks,
-                  float* __restrict__ part, float* __restrict__ s_out) {
+                  float* __restrict__ part, float* __restrict__ s_out, int64_t b0) {
     __shared__ float sm[kUW][kUColTile];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t b = blockIdx.z, chunk = blockIdx.y;
+    const int64_t b = b0 + blockIdx.z, chunk = blockIdx.y;
     const int64_t cbase = int64_t(blockIdx.x) * kUColTile;
     const int64_t r0 = chunk * rows_per_chunk, r1 = min(n, r0 + rows_per_chunk);
     const float* gb = Gm + b * n * m;
@@ -196,7 +196,10 @@ int sk_unrolled_bwd(const SkBwdArgs& a, const float* u_hist, const float* v_hist
     if (a.bwd_iters > 0) {
         ProfScope ps(DOT_K_SK_BWD_ITER, st, a.bwd_iters * (chunks > 1 ? 3 : 2));
         for (int t = a.bwd_iters - 1; t >= 0; --t) {
-            sku_colsum_kernel<<<col_grid, kUT, 0, st>>>(w.gamma, a.n, a.m, rpc, chunks, w.part, w.colsum);
+            for (int64_t b0 = 0; b0 < a.B; b0 += kMaxGridZ) {
+                const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, a.B - b0)));
+                sku_colsum_kernel<<<gz, kUT, 0, st>>>(w.gamma, a.n, a.m, rpc, chunks, w.part, w.colsum, b0);
+            }
             if (chunks > 1)
                 sku_colsum_merge_kernel<<<unsigned(ceil_div(a.B * a.m, 256)), 256, 0, st>>>(w.part, chunks, a.B,
                                                                                           a.m, w.colsum);

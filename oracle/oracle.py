@@ -185,6 +185,30 @@ def sinkhorn_dual(log_alpha, tau: float, n_iters: int, log_a=None, log_b=None, t
     return u, v, int(used), bool(conv.value)
 
 
+def sinkhorn_dual_fp64(log_alpha, tau: float, n_iters: int, log_a=None, log_b=None) -> np.ndarray:
+    """The dual-potential iteration of :func:`sinkhorn_dual` (the reference's
+    CUDA path, ``src/sinkhorn/torch_cuda.cpp:147-264``, row then column update
+    from ``u = v = 0``, default marginals ``-log n`` / ``-log m``) evaluated in
+    float64 from the fp32 input, as a rounding-free yardstick for problems
+    whose fp32 sums are long (m in the tens of thousands), where the
+    reference's own two fp32 formulations already differ at the 1e-5 level.
+    Returns the plan [B,n,m] (float64)."""
+    K = _f32(log_alpha).astype(np.float64) / float(tau)
+    B, n, m = K.shape
+    la = np.full((B, n), -math.log(n)) if log_a is None else np.asarray(log_a, np.float64)
+    lb = np.full((B, m), -math.log(m)) if log_b is None else np.asarray(log_b, np.float64)
+    u = np.zeros((B, n))
+    v = np.zeros((B, m))
+    for _ in range(int(n_iters)):
+        t = K + v[:, None, :]
+        mx = t.max(axis=2, keepdims=True)
+        u = la - (mx[..., 0] + np.log(np.exp(t - mx).sum(axis=2)))
+        t = K + u[:, :, None]
+        mx = t.max(axis=1, keepdims=True)
+        v = lb - (mx[:, 0] + np.log(np.exp(t - mx).sum(axis=1)))
+    return np.exp(K + u[:, :, None] + v[:, None, :])
+
+
 def bidir_forward(sim, tau: float, lengths, kind: str = "restated"):
     """Returns ``(out, row_softmax, col_softmax)``, all [B,L1,L2] fp32.
 
