@@ -164,7 +164,7 @@ int dot_sinkhorn_fwd(const float* X, float score_sign, const float* log_a, const
     a.la = log_a;
     a.lb = log_b;
     if (tol == 0.0f && sk_resident_supported(n, m)) return sk_resident_fwd(a, workspace, st);
-    if (tol == 0.0f && sk_cluster_supported(B, n, m, X)) {
+    if (tol == 0.0f && sk_cluster_preferred(B, n, m, X)) {
         rc = sk_cluster_fwd(a, st);
         if (rc != DOT_ERR_UNSUPPORTED) return rc;
         clear_error();
@@ -292,7 +292,7 @@ int dot_sinkhorn_bwd(const float* X, float score_sign, const float* P, const flo
     a.gX = grad_X;
     a.gtau = grad_tau;
     if (sk_resident_supported(n, m)) return sk_resident_bwd(a, workspace, st);
-    if (sk_cluster_supported(B, n, m, P) && workspace != nullptr) {
+    if (sk_cluster_preferred(B, n, m, P) && workspace != nullptr) {
         rc = sk_cluster_bwd(a, static_cast<int32_t*>(workspace), st);
         if (rc != DOT_ERR_UNSUPPORTED) return rc;
         clear_error();

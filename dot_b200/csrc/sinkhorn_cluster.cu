@@ -56,6 +56,7 @@ struct CCfg {
     static constexpr int NP = NC / 2;         // float2 pairs per lane
     static constexpr int CW = 128 * VPL;      // columns covered (>= m)
     static constexpr int T = 32 * W;
+    static constexpr int MINB = T <= 256 ? 2 : 1;   // CTAs per SM the launch bounds target
 };
 
 __device__ __forceinline__ uint32_t cl_rank() {
@@ -170,7 +171,7 @@ __device__ __forceinline__ void store_part(const CSmem<C>& S, int wid, int lane,
 // forward
 // ---------------------------------------------------------------------------
 template <class C>
-__global__ void __launch_bounds__(C::T, 1) skc_fwd_kernel(SkFwdArgs a, ClusterGeom geo) {
+__global__ void __launch_bounds__(C::T, C::MINB) skc_fwd_kernel(SkFwdArgs a, ClusterGeom geo) {
     constexpr int W = C::W, VPL = C::VPL, NP = C::NP, CL = C::CL, T = C::T;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bar_tile, bar_in, bar_v;
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(C::T, 1) skc_fwd_kernel(SkFwdArgs a, ClusterGe
 // backward (implicit adjoint on the resident plan tile)
 // ---------------------------------------------------------------------------
 template <class C>
-__global__ void __launch_bounds__(C::T, 1) skc_bwd_kernel(SkBwdArgs a, ClusterGeom geo, int32_t* err) {
+__global__ void __launch_bounds__(C::T, C::MINB) skc_bwd_kernel(SkBwdArgs a, ClusterGeom geo, int32_t* err) {
     constexpr int W = C::W, VPL = C::VPL, NP = C::NP, CL = C::CL, T = C::T;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bar_tile, bar_in, bar_v;
@@ -658,26 +659,34 @@ cudaLaunchConfig_t cluster_config(int64_t B, size_t sm, cudaStream_t st, cudaLau
     return cfg;
 }
 
-// Whether the device can hold one cluster of this kernel with `sm` bytes of
-// dynamic shared memory (cached per device, kernel and size).
+// Clusters of this kernel with `sm` bytes of dynamic shared memory the
+// device holds at once (0: none fits), cached per device, kernel and size;
+// sets the kernel's shared-memory attribute as a side effect.
 template <class C, int WHICH, typename K>
-bool can_launch(K kernel, size_t sm) {
+int resident_clusters(K kernel, size_t sm) {
     constexpr int kMaxDev = 64;
-    static size_t ok_sm[kMaxDev] = {};   // one cache per configuration and direction
+    static size_t c_sm[kMaxDev] = {};   // one cache per configuration and direction
+    static int c_ncl[kMaxDev] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDev && ok_sm[dev] == sm) return true;
+    if (dev >= 0 && dev < kMaxDev && c_sm[dev] == sm) return c_ncl[dev];
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    if (C::CL > 8) cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cluster_config<C>(1, sm, nullptr, attr);
     int ncl = 0;
     if (cudaOccupancyMaxActiveClusters(&ncl, kernel, &cfg) != cudaSuccess) {
         cudaGetLastError();
-        return false;
+        ncl = 0;
     }
-    if (ncl >= 1 && dev >= 0 && dev < kMaxDev) ok_sm[dev] = sm;
-    return ncl >= 1;
+    if (dev >= 0 && dev < kMaxDev) {
+        c_sm[dev] = sm;
+        c_ncl[dev] = ncl;
+    }
+    return ncl;
 }
+template <class C, int WHICH, typename K>
+bool can_launch(K kernel, size_t sm) { return resident_clusters<C, WHICH>(kernel, sm) >= 1; }
 
 template <int VPL>
 int fwd_v(const SkFwdArgs& a, const ClusterGeom& g, cudaStream_t st) {
@@ -712,6 +721,15 @@ __global__ void skc_status_kernel(int32_t* status, int n_iters) {
 
 }  // namespace
 
+int sk_cluster_capacity(int64_t n, int64_t m) {
+    const ClusterGeom g = geom_of(n, m);
+    switch (vpl_of(m)) {
+        case 2: return resident_clusters<CfgV<2>, 0>(skc_fwd_kernel<CfgV<2>>, smem_bytes<2>(g, m));
+        case 4: return resident_clusters<CfgV<4>, 0>(skc_fwd_kernel<CfgV<4>>, smem_bytes<4>(g, m));
+        default: return resident_clusters<CfgV<8>, 0>(skc_fwd_kernel<CfgV<8>>, smem_bytes<8>(g, m));
+    }
+}
+
 bool sk_cluster_supported(int64_t B, int64_t n, int64_t m, const void* data) {
     if (B < 1 || n < 1 || m < 4 || m > 1024 || (m % 4) != 0) return false;
     if ((reinterpret_cast<uintptr_t>(data) & 15u) != 0) return false;
@@ -719,6 +737,10 @@ bool sk_cluster_supported(int64_t B, int64_t n, int64_t m, const void* data) {
     const ClusterGeom g = geom_of(n, m);
     if (size_t(g.rpc) * size_t(m) * 4 > kTileBudget) return false;
     return smem_of(g, m) <= 227 * 1024 - 64;
+}
+
+bool sk_cluster_preferred(int64_t B, int64_t n, int64_t m, const void* data) {
+    return sk_cluster_supported(B, n, m, data) && B <= int64_t(sk_cluster_capacity(n, m));
 }
 
 int sk_cluster_fwd(const SkFwdArgs& a, cudaStream_t st) {

@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "pack.cuh"
 #include "sinkhorn.h"
 #include "tma.cuh"
 
@@ -256,7 +257,8 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
     if (tid == 0) s_nfix = 0;
 
     auto live = [&](int p) -> bool { return FULL || (4 * lane + 128 * p) < m; };
-    float vr[NC], cS[NC];
+    // packed two-lane arithmetic (pack.cuh) on element pairs (2k, 2k+1)
+    float2 vr[NC / 2], cS[NC / 2];
     float A = kNegBig;   // warp-wide column reference (uniform across the warp)
     float dmax = 0.0f;
     int cur = -1;
@@ -270,13 +272,11 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
                 const int64_t col = 4 * lane + 128 * p;
                 const float4 v4 = live(p) ? __ldcg(reinterpret_cast<const float4*>(a.v2 + b * m + col))
                                           : make_float4(0, 0, 0, 0);
-                vr[4 * p + 0] = v4.x;
-                vr[4 * p + 1] = v4.y;
-                vr[4 * p + 2] = v4.z;
-                vr[4 * p + 3] = v4.w;
+                vr[2 * p] = make_float2(v4.x, v4.y);
+                vr[2 * p + 1] = make_float2(v4.z, v4.w);
             }
 #pragma unroll
-            for (int e = 0; e < NC; ++e) cS[e] = 0.0f;
+            for (int k = 0; k < NC / 2; ++k) cS[k] = make_float2(0.0f, 0.0f);
             A = kNegBig;
         }
         const int rj = int(min(int64_t(R), n - int64_t(jb) * R));
@@ -295,24 +295,21 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
         const float* xs = rg.buf(g);
         auto do_row = [&](int q) {
             const int i = wid + kFW * q;
-            float t[NC];
-            float mx = kNegBig;
+            float2 t[NC / 2];
+            const float2 k2 = splat2(a.kinv);
 #pragma unroll
             for (int p = 0; p < VPL; ++p) {
                 if (live(p)) {
                     const float4 x = *reinterpret_cast<const float4*>(xs + i * int(m) + 4 * lane + 128 * p);
-                    t[4 * p + 0] = kplus(x.x, a.kinv, vr[4 * p + 0]);
-                    t[4 * p + 1] = kplus(x.y, a.kinv, vr[4 * p + 1]);
-                    t[4 * p + 2] = kplus(x.z, a.kinv, vr[4 * p + 2]);
-                    t[4 * p + 3] = kplus(x.w, a.kinv, vr[4 * p + 3]);
+                    // K + v with K = X * kinv rounded first (the reference's log_K)
+                    t[2 * p] = add2(mul2(make_float2(x.x, x.y), k2), vr[2 * p]);
+                    t[2 * p + 1] = add2(mul2(make_float2(x.z, x.w), k2), vr[2 * p + 1]);
                 } else {
-                    t[4 * p + 0] = t[4 * p + 1] = t[4 * p + 2] = t[4 * p + 3] = -INFINITY;
+                    t[2 * p] = t[2 * p + 1] = make_float2(-INFINITY, -INFINITY);
                 }
             }
-#pragma unroll
-            for (int e = 0; e < NC; ++e) mx = fmaxf(mx, t[e]);
             // row LSE, max pass then sum pass (the reference's two-pass order)
-            mx = warp_max<32>(mx);
+            const float mx = warp_max<32>(max_of(t));
             // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e
             // rounded; cr = mx*log2e - mL exactly (FMA remainder), so every
             // term carries the common factor 2^cr, taken out of the row LSE
@@ -320,9 +317,14 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             const float mxc = fmaxf(mx, -1.0e37f);   // a row of -inf terms keeps mL finite
             const float mL = mxc * kLog2e;
             const float cr = fmaf(mxc, kLog2e, -mL);
+            const float2 l2 = splat2(kLog2e), nm = splat2(-mL);
 #pragma unroll
-            for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));   // t now holds E_ij * 2^cr
-            const float s = warp_sum<32>(tree_sum(t));
+            for (int k = 0; k < NC / 2; ++k) {   // t now holds E_ij * 2^cr
+                const float2 e = fma2(t[k], l2, nm);
+                t[k] = make_float2(ex2(e.x), ex2(e.y));
+            }
+            const float2 s2 = tree_sum2(t);
+            const float s = warp_sum<32>(s2.x + s2.y);
             const int64_t grow = grow0 + i;
             const float unew = lar[q] - (mx + (fast_log(fmaxf(s, kSumFloor)) - cr * kLn2));
             if (lane == 0) {
@@ -331,14 +333,14 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             }
             const float ai = mx + unew;
             if (ai > A + kRaise) {            // warp-uniform
-                const float sc = exp_shift(A - ai);
+                const float2 sc = splat2(exp_shift(A - ai));
 #pragma unroll
-                for (int e = 0; e < NC; ++e) cS[e] *= sc;
+                for (int k = 0; k < NC / 2; ++k) cS[k] = mul2(cS[k], sc);
                 A = ai;
             }
-            const float w = ex2(fmaf(ai - A, kLog2e, -cr));   // exp(ai - A) / 2^cr
+            const float2 w = splat2(ex2(fmaf(ai - A, kLog2e, -cr)));   // exp(ai - A) / 2^cr
 #pragma unroll
-            for (int e = 0; e < NC; ++e) cS[e] = fmaf(t[e], w, cS[e]);
+            for (int k = 0; k < NC / 2; ++k) cS[k] = fma2(t[k], w, cS[k]);
         };
         if (rj == R) {
 #pragma unroll
@@ -365,10 +367,11 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
 #pragma unroll
                 for (int p = 4 * ch; p < VPL && p < 4 * ch + 4; ++p) {
                     if (live(p)) {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            mb[wid * kMergeCols + 4 * lane + 128 * (p - 4 * ch) + e] =
-                                make_float2(A - vr[4 * p + e], cS[4 * p + e]);
+                        float2* dst = mb + wid * kMergeCols + 4 * lane + 128 * (p - 4 * ch);
+                        dst[0] = make_float2(A - vr[2 * p].x, cS[2 * p].x);
+                        dst[1] = make_float2(A - vr[2 * p].y, cS[2 * p].y);
+                        dst[2] = make_float2(A - vr[2 * p + 1].x, cS[2 * p + 1].x);
+                        dst[3] = make_float2(A - vr[2 * p + 1].y, cS[2 * p + 1].y);
                     }
                 }
                 __syncthreads();

@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "pack.cuh"
 #include "sinkhorn.h"
 #include "tma.cuh"
 
@@ -151,12 +152,9 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
     // the tile holds K = X * kinv from here on (rounded once, as the reference
     // materialises log_K); the cost epilogue re-reads X
     for (int64_t q = tid; q < (n * m) >> 2; q += C::T) {
-        float4 x = reinterpret_cast<float4*>(S.tile)[q];
-        x.x = __fmul_rn(x.x, a.kinv);
-        x.y = __fmul_rn(x.y, a.kinv);
-        x.z = __fmul_rn(x.z, a.kinv);
-        x.w = __fmul_rn(x.w, a.kinv);
-        reinterpret_cast<float4*>(S.tile)[q] = x;
+        const float4 x = reinterpret_cast<float4*>(S.tile)[q];
+        const float2 lo = mul2(make_float2(x.x, x.y), splat2(a.kinv)), hi = mul2(make_float2(x.z, x.w), splat2(a.kinv));
+        reinterpret_cast<float4*>(S.tile)[q] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
     __syncthreads();
 
@@ -166,47 +164,48 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
     const float* lb = a.lb ? a.lb + b * m : nullptr;
 
     for (int it = 0; it < a.n_iters; ++it) {
-        float vr[NC];
+        // packed two-lane arithmetic (pack.cuh): element pairs (2k, 2k+1)
+        float2 vr[NC / 2];
 #pragma unroll
         for (int p = 0; p < VPL; ++p) {
             const float4 v4 = *reinterpret_cast<const float4*>(S.v + colof(p));
-            vr[4 * p + 0] = v4.x;
-            vr[4 * p + 1] = v4.y;
-            vr[4 * p + 2] = v4.z;
-            vr[4 * p + 3] = v4.w;
+            vr[2 * p] = make_float2(v4.x, v4.y);
+            vr[2 * p + 1] = make_float2(v4.z, v4.w);
         }
-        float cs[NC];
+        float2 cs[NC / 2];
 #pragma unroll
-        for (int e = 0; e < NC; ++e) cs[e] = 0.0f;
+        for (int k = 0; k < NC / 2; ++k) cs[k] = make_float2(0.0f, 0.0f);
         float A = kNegBig;
         for (int sl = 0; sl < nslots; ++sl) {
             const int64_t i = int64_t(sl) * C::ROWS_PER_SLOT + wid * G + grp;
             const bool rok = i < n;
-            float t[NC];
-            float mx = kNegBig;
+            float2 t[NC / 2];
 #pragma unroll
             for (int p = 0; p < VPL; ++p) {
                 const int col = colof(p);
                 if (rok && col < m) {
                     const float4 k4 = *reinterpret_cast<const float4*>(S.tile + i * m + col);
-                    t[4 * p + 0] = __fadd_rn(k4.x, vr[4 * p + 0]);
-                    t[4 * p + 1] = __fadd_rn(k4.y, vr[4 * p + 1]);
-                    t[4 * p + 2] = __fadd_rn(k4.z, vr[4 * p + 2]);
-                    t[4 * p + 3] = __fadd_rn(k4.w, vr[4 * p + 3]);
+                    t[2 * p] = add2(make_float2(k4.x, k4.y), vr[2 * p]);
+                    t[2 * p + 1] = add2(make_float2(k4.z, k4.w), vr[2 * p + 1]);
                 } else {
-                    t[4 * p + 0] = t[4 * p + 1] = t[4 * p + 2] = t[4 * p + 3] = -INFINITY;
+                    t[2 * p] = t[2 * p + 1] = make_float2(-INFINITY, -INFINITY);
                 }
             }
-            mx = group_max<LPR>(fmaxf(mx, tree_max(t)));
+            const float mx = group_max<LPR>(max_of(t));
             // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e rounded;
             // every term carries 2^cr, cr = mx*log2e - mL exactly (FMA
             // remainder), taken out of the row LSE and the column weight
             const float mxc = fmaxf(mx, -1.0e37f);   // a row of -inf terms keeps mL finite
             const float mL = mxc * kLog2e;
             const float cr = fmaf(mxc, kLog2e, -mL);
+            const float2 l2 = splat2(kLog2e), nm = splat2(-mL);
 #pragma unroll
-            for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));
-            const float s = group_sum<LPR>(tree_sum(t));
+            for (int k = 0; k < NC / 2; ++k) {
+                const float2 e = fma2(t[k], l2, nm);
+                t[k] = make_float2(ex2(e.x), ex2(e.y));
+            }
+            const float2 s2 = tree_sum2(t);
+            const float s = group_sum<LPR>(s2.x + s2.y);
             float ai = -INFINITY;
             if (rok) {
                 const float unew = (la ? la[i] : a.la_def) - (mx + (fast_log(fmaxf(s, kSumFloor)) - cr * kLn2));
@@ -215,22 +214,25 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
             }
             const float amax = across_groups_max<LPR>(ai);
             if (amax > A + kRaiseR) {          // warp-uniform
-                const float sc = exp_shift(A - amax);
+                const float2 sc = splat2(exp_shift(A - amax));
 #pragma unroll
-                for (int e = 0; e < NC; ++e) cs[e] *= sc;
+                for (int k = 0; k < NC / 2; ++k) cs[k] = mul2(cs[k], sc);
                 A = amax;
             }
-            const float w = ex2(fmaf(ai - A, kLog2e, -cr));   // exp(ai - A) / 2^cr
+            const float2 w = splat2(ex2(fmaf(ai - A, kLog2e, -cr)));   // exp(ai - A) / 2^cr
 #pragma unroll
-            for (int e = 0; e < NC; ++e) cs[e] = fmaf(t[e], w, cs[e]);
+            for (int k = 0; k < NC / 2; ++k) cs[k] = fma2(t[k], w, cs[k]);
         }
 #pragma unroll
-        for (int e = 0; e < NC; ++e) cs[e] = across_groups_sum<LPR>(cs[e]);
+        for (int k = 0; k < NC / 2; ++k) {
+            cs[k].x = across_groups_sum<LPR>(cs[k].x);
+            cs[k].y = across_groups_sum<LPR>(cs[k].y);
+        }
         if (grp == 0) {
 #pragma unroll
             for (int p = 0; p < VPL; ++p)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) S.part[wid * C::CW + colof(p) + e] = cs[4 * p + e];
+                *reinterpret_cast<float4*>(S.part + wid * C::CW + colof(p)) =
+                    make_float4(cs[2 * p].x, cs[2 * p].y, cs[2 * p + 1].x, cs[2 * p + 1].y);
         }
         if (lane == 0) S.aw[wid] = A;
         __syncthreads();
@@ -417,54 +419,55 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_bwd_kernel(SkBwdArgs a, int
     }
     __syncthreads();
 
-    // ---- Gauss-Seidel sweeps
+    // ---- Gauss-Seidel sweeps (packed two-lane arithmetic, pairs of columns)
     for (int it = 0; it < a.bwd_iters; ++it) {
-        float mr[NC], acc[NC];
+        float2 mr[NC / 2], acc[NC / 2];
 #pragma unroll
         for (int p = 0; p < VPL; ++p) {
             const float4 u4 = *reinterpret_cast<const float4*>(mu + colof(p));
-            mr[4 * p + 0] = u4.x;
-            mr[4 * p + 1] = u4.y;
-            mr[4 * p + 2] = u4.z;
-            mr[4 * p + 3] = u4.w;
+            mr[2 * p] = make_float2(u4.x, u4.y);
+            mr[2 * p + 1] = make_float2(u4.z, u4.w);
         }
 #pragma unroll
-        for (int e = 0; e < NC; ++e) acc[e] = 0.0f;
+        for (int k = 0; k < NC / 2; ++k) acc[k] = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int sl = 0; sl < MAXSLOTS; ++sl) {
             if (sl >= nslots) break;
             const int64_t i = int64_t(sl) * C::ROWS_PER_SLOT + wid * G + grp;
             const bool rok = i < n;
-            float pv[NC];
+            float2 pv[NC / 2];
 #pragma unroll
             for (int p = 0; p < VPL; ++p) {
                 const int col = colof(p);
                 if (rok && col < m) {
                     const float4 x = *reinterpret_cast<const float4*>(S.tile + i * m + col);
-                    pv[4 * p + 0] = x.x;
-                    pv[4 * p + 1] = x.y;
-                    pv[4 * p + 2] = x.z;
-                    pv[4 * p + 3] = x.w;
+                    pv[2 * p] = make_float2(x.x, x.y);
+                    pv[2 * p + 1] = make_float2(x.z, x.w);
                 } else {
-                    pv[4 * p + 0] = pv[4 * p + 1] = pv[4 * p + 2] = pv[4 * p + 3] = 0.0f;
+                    pv[2 * p] = pv[2 * p + 1] = make_float2(0.0f, 0.0f);
                 }
             }
-            float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four independent chains
+            float2 sq[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};   // four independent chains
 #pragma unroll
-            for (int e = 0; e < NC; ++e) sq[e & 3] = fmaf(pv[e], mr[e], sq[e & 3]);
-            const float s = group_sum<LPR>((sq[0] + sq[1]) + (sq[2] + sq[3]));
+            for (int k = 0; k < NC / 2; ++k) sq[k & 1] = fma2(pv[k], mr[k], sq[k & 1]);
+            const float2 sq2 = add2(sq[0], sq[1]);
+            const float s = group_sum<LPR>(sq2.x + sq2.y);
             const float l = rok ? (rPG[sl] - s) * rP[sl] : 0.0f;
             if (rok && gl == 0) lam[i] = l;
+            const float2 l2 = splat2(l);
 #pragma unroll
-            for (int e = 0; e < NC; ++e) acc[e] += pv[e] * l;
+            for (int k = 0; k < NC / 2; ++k) acc[k] = fma2(pv[k], l2, acc[k]);
         }
 #pragma unroll
-        for (int e = 0; e < NC; ++e) acc[e] = across_groups_sum<LPR>(acc[e]);
+        for (int k = 0; k < NC / 2; ++k) {
+            acc[k].x = across_groups_sum<LPR>(acc[k].x);
+            acc[k].y = across_groups_sum<LPR>(acc[k].y);
+        }
         if (grp == 0) {
 #pragma unroll
             for (int p = 0; p < VPL; ++p)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) S.part[wid * C::CW + colof(p) + e] = acc[4 * p + e];
+                *reinterpret_cast<float4*>(S.part + wid * C::CW + colof(p)) =
+                    make_float4(acc[2 * p].x, acc[2 * p].y, acc[2 * p + 1].x, acc[2 * p + 1].y);
         }
         __syncthreads();
         for (int64_t j = tid; j < m; j += C::T) {

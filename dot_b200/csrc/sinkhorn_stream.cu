@@ -224,7 +224,6 @@ __global__ void sk_col_merge_kernel(const float2* __restrict__ part, const float
 // (max, sum) over its rows, gathered from every rank) merged in shard order.
 __global__ void sk_shard_merge_kernel(const float2* __restrict__ pairs, int parts, const float* __restrict__ lb,
                                       float lb_def, float* __restrict__ v2, int64_t count) {
-    pdl_launch_dependents();   // the next row half-step may set up and start its copies
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= count) return;
     float mm = kNegBig, ss = 0.0f;

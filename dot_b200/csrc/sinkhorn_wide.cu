@@ -609,10 +609,14 @@ int nq_of(int64_t mc) {
     return mc <= per ? 1 : mc <= 2 * per ? 2 : 4;
 }
 
+// Consecutive forward iterations overlap through programmatic dependent
+// launch.  A row shard's iteration follows the column merge instead, and
+// there the programmatic launch measured twice the iteration time on one GPU
+// (2307 vs 1254 us per 32768^2 iteration), so row shards launch plainly.
 template <class CFG, int NQ>
 void launch_nq(const WideArgs& a, cudaStream_t st) {
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = wide_config<CFG>(a.G * kWC, a.R, st, attr, true);
+    cudaLaunchConfig_t cfg = wide_config<CFG>(a.G * kWC, a.R, st, attr, a.pairs == nullptr);
     if (a.mc == 4 * CFG::T * NQ) cudaLaunchKernelEx(&cfg, skw_iter_kernel<CFG, NQ, true>, a);
     else cudaLaunchKernelEx(&cfg, skw_iter_kernel<CFG, NQ, false>, a);
 }
