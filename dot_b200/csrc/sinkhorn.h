@@ -56,7 +56,6 @@ struct FusedPlan {
     int64_t nblk = 1;          // row blocks per problem
     int64_t total_blocks = 1;  // B * nblk
     int maxseg = 1;            // most CTAs whose ranges touch one problem
-    int keep = 0;              // leading blocks per CTA range copied with L2 evict_last
     int stages = 2;            // bulk-copy pipeline depth
 };
 bool sk_fused_shape_ok(int64_t B, int64_t n, int64_t m);
@@ -64,9 +63,13 @@ bool sk_fused_supported(int64_t B, int64_t n, int64_t m, const void* data);
 FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m);
 // first: launched without programmatic dependency (the previous stream work
 // writes what the kernel reads before its dependency wait); last: plain
-// copies, which leave the L2 keep set at normal priority.
+// copies (earlier iterations copy with L2 evict_first).
 int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta,
                       int iter, bool first, bool last, cudaStream_t st);
+// Invariants of the adjoint system (row and column sums of P G and P) in one
+// sweep over P and X; part [B, p.maxseg, m] float2, cnt [B] zero.
+int sk_fused_bwd_prep(const SkBwdArgs& a, const FusedPlan& p, float2* rinv, float2* cinv, float2* part,
+                      int32_t* cnt, cudaStream_t st);
 int sk_fused_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv, const float2* cinv,
                       float* lam, float* mu, float* part, int32_t* cnt, int32_t* err, bool first, bool last,
                       cudaStream_t st);
@@ -122,10 +125,12 @@ int sk_resident_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st);
 bool sk_cluster_supported(int64_t B, int64_t n, int64_t m, const void* data);
 // Problems of this shape the device solves at once on clusters (0: none fits).
 int sk_cluster_capacity(int64_t n, int64_t m);
-// The cluster path is taken when the whole batch fits one wave of clusters:
-// beyond that the streaming kernels, whose per-iteration cost is amortised
-// over the batch, are faster (B = 256 of 512 x 512: 21.6 vs 20.3 ms per
-// fwd+bwd step); below it the streaming kernels leave most of the GPU idle.
+// The cluster path is taken for batches of at most kClusterWaves waves of
+// clusters.  Measured on 512 x 512, 200 fwd + 200 adjoint iterations: one
+// wave (B <= 8) 1.23 ms per fwd+bwd step against 3.9-4.7 ms streaming (the
+// streaming kernels leave most of the GPU idle); B = 256 (19 waves) 21.6 ms
+// against 20.3 ms streaming, whose per-iteration cost is amortised over the
+// batch; the per-problem costs cross near B = 200.
 bool sk_cluster_preferred(int64_t B, int64_t n, int64_t m, const void* data);
 int sk_cluster_fwd(const SkFwdArgs& a, cudaStream_t st);
 int sk_cluster_bwd(const SkBwdArgs& a, int32_t* err, cudaStream_t st);

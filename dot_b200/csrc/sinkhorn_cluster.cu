@@ -739,8 +739,10 @@ bool sk_cluster_supported(int64_t B, int64_t n, int64_t m, const void* data) {
     return smem_of(g, m) <= 227 * 1024 - 64;
 }
 
+constexpr int64_t kClusterWaves = 8;
+
 bool sk_cluster_preferred(int64_t B, int64_t n, int64_t m, const void* data) {
-    return sk_cluster_supported(B, n, m, data) && B <= int64_t(sk_cluster_capacity(n, m));
+    return sk_cluster_supported(B, n, m, data) && B <= kClusterWaves * int64_t(sk_cluster_capacity(n, m));
 }
 
 int sk_cluster_fwd(const SkFwdArgs& a, cudaStream_t st) {

@@ -29,13 +29,12 @@
 // Launches of consecutive iterations overlap through programmatic dependent
 // launch: a CTA initialises its barriers and starts its first bulk copies of
 // the (read-only) matrix, then waits for the previous iteration's grid before
-// reading the potentials.  When the matrix is larger than L2, a fixed leading
-// part of every CTA's range can be copied with an L2 evict_last policy and
-// the rest with evict_first, so that the kept part is served from L2 on the next
-// iteration (opt-in, DOT_B200_L2_KEEP_MB).  The last iteration uses no hint,
-// which leaves the kept lines at normal priority.
+// reading the potentials.  Every iteration but the last copies with an L2
+// evict_first policy (the matrix streams through L2; keeping a fixed part of
+// it resident across iterations with evict_last measured no gain at 48, 64 or
+// 96 MiB); the last uses plain copies, which leave the lines at normal
+// priority.
 #include <cmath>
-#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -65,8 +64,7 @@ struct Sched {
     int nblk;        // blocks per problem
     int G;           // CTAs
     int maxseg;      // max segments (CTAs) touching one problem
-    int keep;        // leading blocks of each range copied with evict_last
-    int hint;        // 0: plain copies; 1: evict_last / evict_first split
+    int hint;        // 0: plain copies; 1: evict_first copies
 };
 
 __host__ __device__ __forceinline__ int sched_q(const Sched& s, int k) { return int(int64_t(k) * s.T / s.G); }
@@ -134,8 +132,7 @@ struct Ring {
         uint64_t* bb = barrier(g);
         mbar_arrive_expect_tx(bb, bytes);
         if (c->s.hint) {
-            const uint64_t pol = (g - g0) < c->s.keep ? l2_policy_evict_last() : l2_policy_evict_first();
-            bulk_g2s_hint(buf(g), src, bytes, bb, pol);
+            bulk_g2s_hint(buf(g), src, bytes, bb, l2_policy_evict_first());
         } else {
             bulk_g2s(buf(g), src, bytes, bb);
         }
@@ -565,6 +562,152 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_bw
 }
 
 // ---------------------------------------------------------------------------
+// backward set-up: the invariants of the adjoint system in one sweep
+// ---------------------------------------------------------------------------
+// rinv_i = (sum_k P_ik G_ik, sum_k P_ik) and cinv_k = (sum_i P_ik G_ik,
+// sum_i P_ik) with G = grad_cost_b * X + grad_P (autograd's rounding), read
+// from one pass over P and X on the adjoint iterations' persistent schedule:
+// warp per row (row sums by warp reduction), each lane's columns accumulated
+// over the CTA's rows, merged per CTA through shared memory and across CTAs
+// by the one that arrives last for the problem (segment order).  The
+// reference computes the same sums inside its adjoint kernels
+// (src/sinkhorn/kernels.cu:965-1047).
+struct BwdPrep {
+    const float* P;
+    const float* X;
+    const float* gP;       // may be nullptr
+    const float* gcost;    // may be nullptr
+    int64_t n, m;
+    int R;
+    Sched s;
+    float2* rinv;          // [B, n]
+    float2* cinv;          // [B, m]
+    float2* part;          // [B, maxseg, m]
+    int32_t* cnt;          // [B] arrival counters, zero between launches
+};
+
+template <int VPL, bool FULL>
+__global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : 3)) skf_bwd_prep_kernel(BwdPrep a) {
+    constexpr int NC = 4 * VPL, RPW = FCfg<VPL>::RPW;
+    extern __shared__ __align__(128) unsigned char smem[];   // [kFW][kMergeCols] float2
+    __shared__ int s_flag;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int64_t m = a.m, n = a.n;
+    const int g0 = sched_q(a.s, blockIdx.x), g1 = sched_q(a.s, int(blockIdx.x) + 1);
+    auto live = [&](int p) -> bool { return FULL || (4 * lane + 128 * p) < m; };
+    float cpg[NC], cp[NC];
+    float gc = 0.0f;
+    int cur = -1;
+    int b = g0 / a.s.nblk, jb = g0 - b * a.s.nblk;
+    for (int g = g0; g < g1; ++g) {
+        if (b != cur) {
+            cur = b;
+            gc = a.gcost ? __ldg(a.gcost + b) : 0.0f;
+#pragma unroll
+            for (int e = 0; e < NC; ++e) cpg[e] = cp[e] = 0.0f;
+        }
+        const int rj = int(min(int64_t(a.R), n - int64_t(jb) * a.R));
+        const int64_t grow0 = int64_t(b) * n + int64_t(jb) * a.R;
+#pragma unroll 1
+        for (int q = 0; q < RPW; ++q) {   // one row in flight per warp: the accumulators fill the registers
+            const int i = wid + kFW * q;
+            if (i >= rj) break;   // warp-uniform
+            const int64_t rbase = (grow0 + i) * m;
+            float spg = 0.0f, sp = 0.0f;
+#pragma unroll
+            for (int c0 = 0; c0 < VPL; c0 += 4) {   // at most four float4 of each input live at a time
+                constexpr int CH = VPL < 4 ? VPL : 4;
+                float4 p4[CH], x4[CH];
+#pragma unroll
+                for (int k = 0; k < CH; ++k) {   // the chunk's loads first: bytes in flight
+                    const int p = c0 + k;
+                    const int64_t col = 4 * lane + 128 * p;
+                    p4[k] = live(p) ? __ldg(reinterpret_cast<const float4*>(a.P + rbase + col)) : make_float4(0, 0, 0, 0);
+                    x4[k] = live(p) ? __ldg(reinterpret_cast<const float4*>(a.X + rbase + col)) : make_float4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int k = 0; k < CH; ++k) {
+                    const int p = c0 + k;
+                    const float pv[4] = {p4[k].x, p4[k].y, p4[k].z, p4[k].w};
+                    const float xv[4] = {x4[k].x, x4[k].y, x4[k].z, x4[k].w};
+                    float gpv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (a.gP != nullptr && live(p)) {
+                        const float4 g4 = __ldg(reinterpret_cast<const float4*>(a.gP + rbase + 4 * lane + 128 * p));
+                        gpv[0] = g4.x;
+                        gpv[1] = g4.y;
+                        gpv[2] = g4.z;
+                        gpv[3] = g4.w;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float gv = __fmul_rn(gc, xv[e]);
+                        if (a.gP != nullptr) gv = __fadd_rn(gv, gpv[e]);
+                        const float pg = pv[e] * gv;
+                        spg += pg;
+                        sp += pv[e];
+                        cpg[4 * p + e] += pg;
+                        cp[4 * p + e] += pv[e];
+                    }
+                }
+            }
+            spg = warp_sum<32>(spg);
+            sp = warp_sum<32>(sp);
+            if (lane == 0) a.rinv[grow0 + i] = make_float2(spg, sp);
+        }
+        if (g + 1 == g1 || jb + 1 == a.s.nblk) {
+            // ---- end of this CTA's part of problem b: merge the warps, publish ----
+            const int kfirst = sched_owner(a.s, b * a.s.nblk);
+            const int nseg = sched_owner(a.s, (b + 1) * a.s.nblk - 1) - kfirst + 1;
+            const int seg = int(blockIdx.x) - kfirst;
+            float2* mb = reinterpret_cast<float2*>(smem);
+            float2* dst = nseg == 1 ? a.cinv + int64_t(b) * m : a.part + (int64_t(b) * a.s.maxseg + seg) * m;
+#pragma unroll
+            for (int ch = 0; ch < (VPL + 3) / 4; ++ch) {
+                __syncthreads();   // the merge buffer is free
+#pragma unroll
+                for (int p = 4 * ch; p < VPL && p < 4 * ch + 4; ++p) {
+                    if (live(p)) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            mb[wid * kMergeCols + 4 * lane + 128 * (p - 4 * ch) + e] =
+                                make_float2(cpg[4 * p + e], cp[4 * p + e]);
+                    }
+                }
+                __syncthreads();
+                const int ncols = int(min(int64_t(kMergeCols), m - int64_t(kMergeCols) * ch));
+                for (int cl = tid; cl < ncols; cl += kFT) {
+                    float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int w = 0; w < kFW; ++w) {
+                        const float2 v = mb[w * kMergeCols + cl];
+                        acc.x += v.x;
+                        acc.y += v.y;
+                    }
+                    dst[int64_t(kMergeCols) * ch + cl] = acc;
+                }
+            }
+            if (nseg > 1 && arrive_last(a.cnt, b, nseg, &s_flag)) {
+                const float2* pb = a.part + int64_t(b) * a.s.maxseg * m;
+                for (int64_t col = tid; col < m; col += kFT) {
+                    float2 acc = make_float2(0.0f, 0.0f);
+                    for (int sg = 0; sg < nseg; ++sg) {
+                        const float2 v = __ldcg(pb + int64_t(sg) * m + col);
+                        acc.x += v.x;
+                        acc.y += v.y;
+                    }
+                    a.cinv[int64_t(b) * m + col] = acc;
+                }
+                if (tid == 0) a.cnt[b] = 0;
+            }
+        }
+        if (++jb == a.s.nblk) {
+            jb = 0;
+            ++b;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 int vpl_for(int64_t m) { return m <= 128 ? 1 : m <= 256 ? 2 : m <= 512 ? 4 : 8; }
@@ -577,28 +720,9 @@ int sm_count() {
     return n > 0 ? n : 148;
 }
 
-// Pipeline depth: 2 stages (3 CTAs per SM) or 3 stages (2 CTAs per SM).
-// DOT_B200_FUSED_STAGES overrides the default for tuning runs.
-int stages() {
-    static int s = [] {
-        const char* e = std::getenv("DOT_B200_FUSED_STAGES");
-        const int v = e ? std::atoi(e) : 0;
-        return (v == 2 || v == 3) ? v : 2;
-    }();
-    return s;
-}
-
-// Bytes of every iteration's matrix stream copied with L2 evict_last
-// (DOT_B200_L2_KEEP_MB, 0 = off).  Off by default: at B=256, 512x512 a keep
-// set of 48, 64 or 96 MiB measured the same launch time as none.
-int64_t l2_keep_bytes() {
-    static int64_t k = [] {
-        const char* e = std::getenv("DOT_B200_L2_KEEP_MB");
-        const long v = e ? std::atol(e) : 0;
-        return int64_t(v < 0 ? 0 : v) << 20;
-    }();
-    return k;
-}
+// Pipeline depth: 2 stages (3 CTAs per SM); 3 stages (2 CTAs per SM)
+// measured 64 vs 60 us per cfg2 forward iteration.
+constexpr int kStages = 2;
 
 template <int VPL, bool FULL, int S>
 void set_attr_one() {
@@ -694,7 +818,6 @@ Sched sched_of(const FusedPlan& p) {
     s.nblk = int(p.nblk);
     s.G = p.G;
     s.maxseg = p.maxseg;
-    s.keep = p.keep;
     s.hint = 1;
     return s;
 }
@@ -715,7 +838,7 @@ FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m) {
     FusedPlan p;
     ensure_attrs();
     const int R = rows_per_block(m);
-    p.stages = stages();
+    p.stages = kStages;
     const int per_sm = p.stages == 3 ? per_sm_for<3>(vpl_for(m)) : per_sm_for<2>(vpl_for(m));
     p.nblk = (n + R - 1) / R;
     p.total_blocks = B * p.nblk;
@@ -729,11 +852,6 @@ FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m) {
     }
     p.maxseg = maxseg;
     p.nseg = maxseg;
-    // L2 keep set: only when the matrix does not fit L2 by itself
-    const int64_t bytes = B * n * m * 4;
-    const int64_t blk_bytes = int64_t(R) * m * 4;
-    const int64_t keep_total = l2_keep_bytes();
-    p.keep = (bytes > keep_total && keep_total > 0) ? int(keep_total / (blk_bytes * p.G)) : 0;
     return p;
 }
 
@@ -762,6 +880,32 @@ int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int3
     f.iter = iter;
     if (p.stages == 3) launch_fwd_s<3>(f, p.G, !first, st);
     else launch_fwd_s<2>(f, p.G, !first, st);
+    return DOT_OK;
+}
+
+int sk_fused_bwd_prep(const SkBwdArgs& a, const FusedPlan& p, float2* rinv, float2* cinv, float2* part,
+                      int32_t* cnt, cudaStream_t st) {
+    BwdPrep f{};
+    f.P = a.P;
+    f.X = a.X;
+    f.gP = a.gP;
+    f.gcost = a.gcost;
+    f.n = a.n;
+    f.m = a.m;
+    f.R = rows_per_block(a.m);
+    f.s = sched_of(p);
+    f.rinv = rinv;
+    f.cinv = cinv;
+    f.part = part;
+    f.cnt = cnt;
+    const size_t sm = size_t(kFW) * kMergeCols * sizeof(float2);
+    const bool full = a.m == 128 * vpl_for(a.m);
+    switch (vpl_for(a.m)) {
+        case 1: full ? skf_bwd_prep_kernel<1, true><<<p.G, kFT, sm, st>>>(f) : skf_bwd_prep_kernel<1, false><<<p.G, kFT, sm, st>>>(f); break;
+        case 2: full ? skf_bwd_prep_kernel<2, true><<<p.G, kFT, sm, st>>>(f) : skf_bwd_prep_kernel<2, false><<<p.G, kFT, sm, st>>>(f); break;
+        case 4: full ? skf_bwd_prep_kernel<4, true><<<p.G, kFT, sm, st>>>(f) : skf_bwd_prep_kernel<4, false><<<p.G, kFT, sm, st>>>(f); break;
+        default: full ? skf_bwd_prep_kernel<8, true><<<p.G, kFT, sm, st>>>(f) : skf_bwd_prep_kernel<8, false><<<p.G, kFT, sm, st>>>(f); break;
+    }
     return DOT_OK;
 }
 

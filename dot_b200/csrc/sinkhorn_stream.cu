@@ -521,7 +521,31 @@ skb_final_kernel(const float* __restrict__ X, float sign, const float* __restric
     const float l = lam[row];
     const float* mb = mu + b * m;
     float acc = 0.0f;
-    for (int64_t j = lane; j < m; j += 32) {
+    const bool vec = (m & 3) == 0 && aligned16(X) && aligned16(P) && aligned16(gX) && aligned16(mu) &&
+                     (gP == nullptr || aligned16(gP));
+    if (vec) {   // four columns per lane per step, 16-byte accesses
+        for (int64_t j = 4 * lane; j < m; j += 128) {
+            const int64_t idx = row * m + j;
+            const float4 x4 = __ldg(reinterpret_cast<const float4*>(X + idx));
+            const float4 p4 = __ldg(reinterpret_cast<const float4*>(P + idx));
+            const float4 m4 = __ldg(reinterpret_cast<const float4*>(mb + j));
+            float4 g4 = make_float4(0, 0, 0, 0);
+            if (gP != nullptr) g4 = __ldg(reinterpret_cast<const float4*>(gP + idx));
+            const float xs[4] = {x4.x, x4.y, x4.z, x4.w}, ps[4] = {p4.x, p4.y, p4.z, p4.w};
+            const float ms[4] = {m4.x, m4.y, m4.z, m4.w}, gs[4] = {g4.x, g4.y, g4.z, g4.w};
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float gt = __fmul_rn(gc, xs[e]);
+                if (gP != nullptr) gt = __fadd_rn(gt, gs[e]);
+                const float g = ps[e] * (gt - l - ms[e]) / tau;
+                o[e] = __fadd_rn(sign * g, __fmul_rn(gc, ps[e]));
+                acc += g * (sign * xs[e]);
+            }
+            *reinterpret_cast<float4*>(gX + idx) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+    }
+    for (int64_t j = vec ? m : lane; j < m; j += 32) {
         const int64_t idx = row * m + j;
         const float x = __ldg(X + idx);
         const float p = __ldg(P + idx);
@@ -680,13 +704,16 @@ static SkBwdWs carve_bwd(Carve& c, int64_t B, int64_t n, int64_t m) {
     w.cinv = c.take<float2>(size_t(B * m));
     w.lam = c.take<float>(size_t(B * n));
     w.mu = c.take<float>(size_t(B * m));
-    w.part2 = chunks > 1 ? c.take<float2>(size_t(B * chunks * m)) : nullptr;
+    const int64_t p2 = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
+    w.part2 = p2 > 0 ? c.take<float2>(size_t(B * p2 * m)) : nullptr;
     const int64_t p1 = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
     w.part1 = p1 > 0 ? c.take<float>(size_t(B * p1 * m)) : nullptr;
     w.tau_row = c.take<float>(size_t(B * n));
     w.cnt = c.take<int32_t>(size_t(B + 1));
     return w;
 }
+
+static bool aligned16_host(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 size_t sk_stream_bwd_ws(int64_t B, int64_t n, int64_t m) {
     Carve c(nullptr);
@@ -706,27 +733,32 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
 
     cudaMemsetAsync(w.mu, 0, sizeof(float) * size_t(a.B * a.m), st);
     cudaMemsetAsync(w.lam, 0, sizeof(float) * size_t(rows), st);
-    {
-        ProfScope ps(DOT_K_SK_BWD_EPI, st);
-        skb_row_prep_kernel<<<row_grid, kRowThreads, 0, st>>>(a.X, a.P, a.gP, a.gcost, w.rinv, rows, a.n, a.m);
-    }
-    {
-        ProfScope ps(DOT_K_SK_BWD_EPI, st);
-        for (int64_t b0 = 0; b0 < a.B; b0 += kMaxGridZ) {
-            const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, a.B - b0)));
-            skb_col_prep_kernel<<<gz, kColWarps * 32, 0, st>>>(a.X, a.P, a.gP, a.gcost, w.cinv, w.part2,
-                                                                     a.n, a.m, rpc, chunks, b0);
-        }
-    }
-    if (chunks > 1) {
-        ProfScope ps(DOT_K_SK_BWD_EPI, st);
-        skb_col_prep_merge_kernel<<<merge_grid, 256, 0, st>>>(w.part2, w.cinv, a.B, a.m, chunks);
-    }
-    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.P);
+    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.P) && aligned16_host(a.X) &&
+                       (a.gP == nullptr || aligned16_host(a.gP));
     FusedPlan plan;
     if (fused) {
         plan = sk_fused_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B + 1), st);
+        // invariants in one sweep over P and X on the iterations' schedule
+        ProfScope ps(DOT_K_SK_BWD_EPI, st);
+        sk_fused_bwd_prep(a, plan, w.rinv, w.cinv, w.part2, w.cnt, st);
+    } else {
+        {
+            ProfScope ps(DOT_K_SK_BWD_EPI, st);
+            skb_row_prep_kernel<<<row_grid, kRowThreads, 0, st>>>(a.X, a.P, a.gP, a.gcost, w.rinv, rows, a.n, a.m);
+        }
+        {
+            ProfScope ps(DOT_K_SK_BWD_EPI, st);
+            for (int64_t b0 = 0; b0 < a.B; b0 += kMaxGridZ) {
+                const dim3 gz(col_grid.x, col_grid.y, unsigned(std::min<int64_t>(kMaxGridZ, a.B - b0)));
+                skb_col_prep_kernel<<<gz, kColWarps * 32, 0, st>>>(a.X, a.P, a.gP, a.gcost, w.cinv, w.part2,
+                                                                         a.n, a.m, rpc, chunks, b0);
+            }
+        }
+        if (chunks > 1) {
+            ProfScope ps(DOT_K_SK_BWD_EPI, st);
+            skb_col_prep_merge_kernel<<<merge_grid, 256, 0, st>>>(w.part2, w.cinv, a.B, a.m, chunks);
+        }
     }
     if (fused && a.bwd_iters > 0) {
         ProfScope ps(DOT_K_SK_BWD_ITER, st, a.bwd_iters);

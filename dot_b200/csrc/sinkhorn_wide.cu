@@ -589,19 +589,9 @@ cudaLaunchConfig_t wide_config(int grid, int R, cudaStream_t st, cudaLaunchAttri
     return cfg;
 }
 
-// DOT_B200_WIDE_SHAPE = a | b selects the CTA shape (tuning runs; b only
-// where the slice fits it, mc <= 4096).  Default: b for mc <= 4096, else a.
-int wide_shape(int64_t mc) {
-    static int pref = [] {
-        const char* e = std::getenv("DOT_B200_WIDE_SHAPE");
-        if (e == nullptr) return -1;
-        const std::string v(e);
-        return v == "a" ? int(kShapeA) : v == "b" ? int(kShapeB) : -1;
-    }();
-    if (pref == kShapeA) return pref;
-    if (pref == kShapeB && mc <= 4096) return pref;
-    return mc <= 4096 ? kShapeB : kShapeA;
-}
+// CTA shape: b (two 256-thread CTAs per SM) where the slice fits it,
+// mc <= 4096 columns, else a (one 512-thread CTA per SM).
+int wide_shape(int64_t mc) { return mc <= 4096 ? kShapeB : kShapeA; }
 
 template <class CFG>
 int nq_of(int64_t mc) {

@@ -209,6 +209,28 @@ def sinkhorn_dual_fp64(log_alpha, tau: float, n_iters: int, log_a=None, log_b=No
     return np.exp(K + u[:, :, None] + v[:, None, :])
 
 
+def sinkhorn_implicit_fp64(log_alpha, P, G, tau: float, n_iters: int):
+    """The reference's implicit backward (Gauss-Seidel adjoint of
+    ``src/sinkhorn/kernels_cpu.cpp:247-327`` run for ``n_iters`` sweeps, no
+    early stop, then grad = P (G - lambda - mu) / tau and grad_tau =
+    -sum(grad * log_alpha) / tau) evaluated in float64, as a rounding-free
+    yardstick for quantities whose fp32 sums cancel (the temperature gradient
+    of a batch).  Returns (grad [B,n,m], grad_tau [B]) in float64."""
+    la = np.asarray(log_alpha, np.float64)
+    P = np.asarray(P, np.float64)
+    G = np.asarray(G, np.float64)
+    B, n, m = P.shape
+    rPG, rP = (P * G).sum(2), np.maximum(P.sum(2), 1e-12)
+    cPG, cP = (P * G).sum(1), np.maximum(P.sum(1), 1e-12)
+    lam = np.zeros((B, n))
+    mu = np.zeros((B, m))
+    for _ in range(int(n_iters)):
+        lam = (rPG - (P * mu[:, None, :]).sum(2)) / rP
+        mu = (cPG - (P * lam[:, :, None]).sum(1)) / cP
+    grad = P * (G - lam[:, :, None] - mu[:, None, :]) / float(tau)
+    return grad, -(grad * la).sum((1, 2)) / float(tau)
+
+
 def bidir_forward(sim, tau: float, lengths, kind: str = "restated"):
     """Returns ``(out, row_softmax, col_softmax)``, all [B,L1,L2] fp32.
 

@@ -715,3 +715,41 @@ def test_batch_beyond_one_grid_dimension():
         ref = O.sinkhorn_api(C[lo:hi].numpy(), 0.5, 6, g_cost=cw[lo:hi].numpy(), bwd_tol=0.0)
         U.assert_normwise(r["P"][lo:hi], ref["P"], U.PLAN_RTOL, f"plan[{lo}:{hi}]")
         U.assert_normwise(r["dC"][lo:hi], ref["dC"], U.GRAD_RTOL, f"dC[{lo}:{hi}]")
+
+
+# ---------------------------------------------------------------------------
+# streaming single-pass path (m <= 1024, problems too tall for a cluster):
+# one launch per forward iteration and per adjoint sweep, the adjoint's
+# invariants from one sweep over P and C
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("B,n,m,reg,T,with_plan_grad", [(3, 1200, 512, 0.05, 30, True), (2, 1500, 260, 0.1, 20, False),
+                                                         (1, 900, 1024, 0.2, 10, True)], ids=lambda v: str(v))
+def test_streaming_single_pass_path_matches_oracle(B, n, m, reg, T, with_plan_grad):
+    from dot_b200 import _lib
+
+    g = U.gen(13000 + n + m)
+    C = torch.rand(B, n, m, generator=g)
+    W = torch.randn(B, n, m, generator=g) if with_plan_grad else None
+    cw = torch.randn(B, generator=g)
+    ref = O.sinkhorn_api(C.numpy(), reg, T, g_cost=cw.numpy(), grad_P=None if W is None else W.numpy(), bwd_tol=0.0)
+    _lib.prof_begin(time_events=False)
+    r = run_api(C, reg, T, cost_weight=cw, plan_weight=W, reg_tensor=True)
+    torch.cuda.synchronize()
+    prof = _lib.prof_end()
+    assert prof["sk_fwd_iter"]["launches"] == T and prof["sk_bwd_iter"]["launches"] == T, prof
+    U.assert_normwise(r["P"], ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_rel(r["cost"], ref["cost"], U.COST_RTOL, "cost", atol=1e-9)
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
+    # d loss / d reg sums signed per-problem terms over ~10^6 elements each
+    # (here -1.0, +1.7, -0.46 for the 3 x 1200 x 512 case): the fp32 oracle
+    # lands 1.3e-3 from a float64 evaluation of the same backward, so the
+    # yardstick is the float64 restatement (on the float64 plan), and the
+    # oracle may be off by its own gap plus the tolerance
+    Cn = C.numpy()
+    G = cw.numpy()[:, None, None].astype(np.float64) * Cn + (0.0 if W is None else W.numpy())
+    _, gtau64 = O.sinkhorn_implicit_fp64(-Cn, O.sinkhorn_dual_fp64(-Cn, reg, T), G, reg, T)
+    dreg64 = float(gtau64.sum())
+    assert r["dreg"] == pytest.approx(dreg64, rel=U.GRAD_RTOL, abs=1e-6)
+    own = abs(float(ref["dreg"]) - dreg64)
+    assert abs(r["dreg"] - float(ref["dreg"])) <= own + U.GRAD_RTOL * abs(dreg64) + 1e-6
