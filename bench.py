@@ -872,6 +872,7 @@ def main() -> None:
                     help="skip the row-sharded configs[4] and batch-sharded configs[3] measurements")
     ap.add_argument("--iters", type=int, default=None, help="override the config's iteration count (profiling)")
     ap.add_argument("--rows", type=int, default=None, help="override the config's row count n (profiling)")
+    ap.add_argument("--batch", type=int, default=None, help="override the config's batch size B (profiling)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     cfg["name"] = args.config
@@ -881,6 +882,9 @@ def main() -> None:
     if args.rows is not None:
         cfg["n"] = args.rows
         cfg["desc"] += f" (run with {args.rows} rows)"
+    if args.batch is not None:
+        cfg["B"] = args.batch
+        cfg["desc"] += f" (run with batch {args.batch})"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

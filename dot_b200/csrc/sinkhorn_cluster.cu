@@ -34,6 +34,7 @@
 // at the next CTA barrier; every CTA arrives at the final cluster barrier.
 #include <cmath>
 
+#include "cluster.cuh"
 #include "common.cuh"
 #include "internal.h"
 #include "pack.cuh"
@@ -58,33 +59,6 @@ struct CCfg {
     static constexpr int T = 32 * W;
     static constexpr int MINB = T <= 256 ? 2 : 1;   // CTAs per SM the launch bounds target
 };
-
-__device__ __forceinline__ uint32_t cl_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cl_id() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cl_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, uint32_t remote_bar, float v) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote_addr),
-                 "f"(v), "r"(remote_bar)
-                 : "memory");
-}
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
 
 // Shared-memory carve (dynamic part): tile [rpc*m] | part [W*CW] | v [CW] |
 // u [rpc] | in [CL*cpo] float2 | cinv [cpo] float2 | rinv [rpc] float2 |
