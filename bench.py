@@ -511,6 +511,42 @@ def measure_batchshard_cfg4(rank: int, world: int, dev) -> dict:
             "unit": "cost-elem-iters/s", "scaling": "strong", "problems_per_gpu": -(-cfg["B"] // world)}
 
 
+def measure_points_cfg5(dev) -> dict:
+    """configs[4] (32768 x 32768 U[0,1)^3 clouds, reg 0.01, 500 iterations)
+    through ``dot_b200.sinkhorn_points``: the squared distances built inside
+    the sweeps from the two clouds (no 4 GiB cost matrix), with and without
+    writing the plan.  The iterations then read no matrix from HBM; their
+    bound is the exponential unit (one ex2 per element-iteration)."""
+    import torch
+
+    import dot_b200
+
+    cfg = CONFIGS["cfg5"]
+    g = torch.Generator(device="cpu")
+    g.manual_seed(1234)
+    x = torch.rand(cfg["n"], 3, generator=g).to(dev)
+    y = torch.rand(cfg["m"], 3, generator=g).to(dev)
+    units = cfg["n"] * cfg["m"] * cfg["iters"]
+    out = {"workload": cfg["desc"] + "; cost built in the sweeps from the two clouds",
+           "n_gpus": 1, "unit": "cost-elem-iters/s"}
+    for key, plan in (("with_plan", True), ("cost_only", False)):
+        def step(plan=plan):
+            return dot_b200.sinkhorn_points(x, y, cfg["reg"], cfg["iters"], return_plan=plan).cost
+        steps = 3
+        ms, prof = time_device(step, steps, 3, 1, dev, profile=True)
+        it = prof["sk_fwd_iter"]
+        out[key] = {"ms_per_step": ms / steps, "value": units * steps / (ms / 1e3),
+                    "iterations_ms": it["ms"] / steps, "launches_per_step": it["launches"] // steps}
+    it_s = out["cost_only"]["iterations_ms"] / 1e3
+    peak = 148 * 16 * 1965e6
+    out["roofline"] = {"bound": "sfu", "kernel_class": "sk_fwd_iter",
+                       "achieved": units / it_s / 1e12 if it_s > 0 else None, "unit": "Tex2/s",
+                       "peak": peak / 1e12, "peak_source": "nominal: 16 ex2 per SM per clock x 148 SMs x 1965 MHz",
+                       "frac": (units / it_s) / peak if it_s > 0 else None}
+    torch.cuda.empty_cache()
+    return out
+
+
 SECONDARY = ("cfg1", "cfg3", "cfg3bf16", "cfg4", "cfg5")
 
 
@@ -577,8 +613,10 @@ def run_ours(args, cfg: dict) -> None:
         for name in SECONDARY:
             confs[name] = measure_config(name, 3, 3, rank, world, dev, args.cpu_seconds / 2,
                                          with_cpu=not args.no_cpu_baseline)
+        pts = measure_points_cfg5(dev)
         if line is not None:
             line["configs"] = confs
+            line["points_cfg5"] = pts
     if not args.no_scaling and cfg["name"] != "cfg5":
         rs = measure_rowshard_cfg5(100, rank, world, dev)
         bsd = measure_batchshard_cfg4(rank, world, dev)

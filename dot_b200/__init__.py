@@ -8,8 +8,11 @@ Public API (same names and behaviour as the reference package ``dot``,
     P = bidirectional_softmax(sim_matrix, tau=1.0)
 
 plus the nn.Module wrappers ``Sinkhorn``, ``SinkhornFromScores`` and
-``BidirectionalSoftmax``.  Low-level operators mirroring the reference's
-``dot._ops`` live in :mod:`dot_b200.ops`; the C-ABI they call is
+``BidirectionalSoftmax``, and one extension with no counterpart in the
+reference: ``sinkhorn_points(x, y, reg, n_iters)``, Sinkhorn on two point
+clouds with the squared-distance cost built inside the solver.  Low-level
+operators mirroring the reference's ``dot._ops`` live in
+:mod:`dot_b200.ops`; the C-ABI they call is
 ``include/dot_b200.h``.  Importing the package loads the native library and
 fails if it is missing.
 """
@@ -24,6 +27,7 @@ from .bidirectional_softmax import (  # noqa: E402
     bidirectional_softmax,
     bidirectional_softmax_with_lengths,
 )
+from .points import sinkhorn_points  # noqa: E402
 from .sinkhorn import (  # noqa: E402
     Sinkhorn,
     SinkhornFromScores,
@@ -43,4 +47,5 @@ __all__ = [
     "bidirectional_softmax",
     "bidirectional_softmax_with_lengths",
     "BidirectionalSoftmax",
+    "sinkhorn_points",
 ]

@@ -148,6 +148,34 @@ __device__ __forceinline__ float kplus(float x, float kinv, float w) {
     return __fadd_rn(__fmul_rn(x, kinv), w);
 }
 
+// Scaled squared Euclidean distance of two points of dimension d:
+//   s = (x_0 - y_0)^2, then s = fma(x_k - y_k, x_k - y_k, s) for k = 1..d-1
+//   (every difference rounded to fp32), cost = s * scale rounded.
+// The point-cloud solvers build every cost entry with exactly these
+// operations (the packed f32x2 forms perform the same IEEE operations per
+// half), so a cost matrix materialised by dot_sq_dist equals, bit for bit,
+// the one the fused sweeps see.
+template <int PD>
+__device__ __forceinline__ float sq_dist(const float (&x)[PD], const float (&y)[PD], float scale) {
+    float d = __fsub_rn(x[0], y[0]);
+    float s = __fmul_rn(d, d);
+#pragma unroll
+    for (int k = 1; k < PD; ++k) {
+        d = __fsub_rn(x[k], y[k]);
+        s = __fmaf_rn(d, d, s);
+    }
+    return __fmul_rn(s, scale);
+}
+__device__ __forceinline__ float sq_dist_n(const float* x, const float* y, int dim, float scale) {
+    float d = __fsub_rn(x[0], y[0]);
+    float s = __fmul_rn(d, d);
+    for (int k = 1; k < dim; ++k) {
+        d = __fsub_rn(x[k], y[k]);
+        s = __fmaf_rn(d, d, s);
+    }
+    return __fmul_rn(s, scale);
+}
+
 // Column kernels put the batch index in gridDim.z, at most kMaxGridZ per
 // launch; larger batches are launched in slices, each kernel adding the
 // slice's first batch index b0 to blockIdx.z.

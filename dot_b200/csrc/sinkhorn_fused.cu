@@ -298,7 +298,10 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             for (int p = 0; p < VPL; ++p) {
                 if (live(p)) {
                     const float4 x = *reinterpret_cast<const float4*>(xs + i * int(m) + 4 * lane + 128 * p);
-                    // K + v with K = X * kinv rounded first (the reference's log_K)
+                    // K + v: ptxas contracts this packed multiply and add into
+                    // one fused multiply-add (measured), so t = fma(X, kinv, v)
+                    // rounds once where the reference rounds log_K = X * kinv
+                    // first; the two differ by at most one rounding of t
                     t[2 * p] = add2(mul2(make_float2(x.x, x.y), k2), vr[2 * p]);
                     t[2 * p + 1] = add2(mul2(make_float2(x.z, x.w), k2), vr[2 * p + 1]);
                 } else {

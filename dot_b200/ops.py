@@ -163,6 +163,62 @@ def sinkhorn_backward_raw(X: torch.Tensor, score_sign: float, P: torch.Tensor, u
     return gX, gtau
 
 
+def sq_dist(x: torch.Tensor, y: torch.Tensor, cost_scale: float = 1.0) -> torch.Tensor:
+    """``dot_sq_dist``: C [B,n,m] = cost_scale * |x_i - y_j|^2 from x [B,n,d],
+    y [B,m,d], with the entry arithmetic the point-cloud solver uses."""
+    _need_cuda(x, "x")
+    _need_cuda(y, "y")
+    if x.dim() != 3 or y.dim() != 3 or x.size(0) != y.size(0) or x.size(2) != y.size(2):
+        raise ValueError("x and y must be [B, n, d] and [B, m, d]")
+    x, y = _f32c(x), _f32c(y)
+    B, n, d = x.shape
+    m = y.size(1)
+    C = torch.empty((B, n, m), dtype=torch.float32, device=x.device)
+    rc = _lib.load().dot_sq_dist(_lib.ptr(x), _lib.ptr(y), B, n, m, d, float(cost_scale), _lib.ptr(C),
+                                 _lib.stream_of(x))
+    _lib.check(rc, "dot_sq_dist")
+    return C
+
+
+def sinkhorn_points_forward_raw(x: torch.Tensor, y: torch.Tensor, cost_scale: float, tau: float, n_iters: int,
+                                log_a: Optional[torch.Tensor] = None, log_b: Optional[torch.Tensor] = None,
+                                tol: float = 0.0, want_plan: bool = True, want_cost: bool = True):
+    """One call of ``dot_sinkhorn_points_fwd`` (cost = cost_scale * squared
+    distances of the clouds x [B,n,d], y [B,m,d], built inside the solver).
+
+    Returns ``(plan_or_None, cost_or_None, u, v, status)``.
+    """
+    _need_cuda(x, "x")
+    _need_cuda(y, "y")
+    if x.dim() != 3 or y.dim() != 3 or x.size(0) != y.size(0) or x.size(2) != y.size(2):
+        raise ValueError("x and y must be [B, n, d] and [B, m, d]")
+    if not tau > 0.0:
+        raise ValueError("tau must be > 0")
+    if n_iters < 0:
+        raise ValueError("n_iters must be >= 0")
+    x, y = _f32c(x), _f32c(y)
+    B, n, d = x.shape
+    m = y.size(1)
+    dev = x.device
+    la = _check_marg(log_a, B, n, "log_a", dev)
+    lb = _check_marg(log_b, B, m, "log_b", dev)
+    plan = torch.empty((B, n, m), dtype=torch.float32, device=dev) if want_plan else None
+    cost = torch.empty((B,), dtype=torch.float32, device=dev) if want_cost else None
+    u = torch.empty((B, n), dtype=torch.float32, device=dev)
+    v = torch.empty((B, m), dtype=torch.float32, device=dev)
+    status = torch.zeros((4,), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    nbytes = lib.dot_sinkhorn_points_fwd_workspace_bytes(B, n, m, d, int(n_iters), float(tol), 1 if want_plan else 0,
+                                                         1 if want_cost else 0)
+    ws = _lib.workspace(nbytes, dev)
+    rc = lib.dot_sinkhorn_points_fwd(_lib.ptr(x), _lib.ptr(y), B, n, m, d, float(cost_scale), _lib.ptr(la),
+                                     _lib.ptr(lb), float(tau), int(n_iters), float(tol), _lib.ptr(plan),
+                                     _lib.ptr(cost), _lib.ptr(u), _lib.ptr(v), _lib.ptr(status), _lib.ptr(ws),
+                                     nbytes, _lib.stream_of(x))
+    _lib.check(rc, "dot_sinkhorn_points_fwd")
+    return plan, cost, u, v, status
+
+
 # ---- reference-named ops ------------------------------------------------------
 
 def sinkhorn(log_alpha, tau: float, n_iters: int, log_a=None, log_b=None) -> torch.Tensor:

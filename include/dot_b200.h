@@ -237,6 +237,49 @@ DOT_API int dot_sinkhorn_fwd_rowshard(const float* X, float score_sign, const fl
                                       void* nccl_comm, float* out, float* cost, float* pot_u, float* pot_v,
                                       int32_t* status, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Sinkhorn on point clouds (squared-distance cost built in the sweeps)     */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * C [B,n,m] from two point clouds x [B,n,d] and y [B,m,d] (fp32, row-major):
+ *     s = (x_i0 - y_j0)^2, then s = fma(x_ik - y_jk, x_ik - y_jk, s) for
+ *     k = 1..d-1 (each difference rounded), C_ij = s * cost_scale rounded.
+ * These are exactly the entries dot_sinkhorn_points_fwd builds internally.
+ * Replaces the cost construction the reference leaves to its callers
+ * (torch.cdist(x, y) ** 2 before sinkhorn(); e.g. the squared-distance costs
+ * of its benchmarks); no op of the reference corresponds.
+ */
+DOT_API int dot_sq_dist(const float* x, const float* y, int64_t B, int64_t n, int64_t m, int d,
+                        float cost_scale, float* C, void* stream);
+
+/* Bytes of workspace dot_sinkhorn_points_fwd needs (want_plan / want_cost:
+ * whether plan / cost will be non-NULL). */
+DOT_API size_t dot_sinkhorn_points_fwd_workspace_bytes(int64_t B, int64_t n, int64_t m, int d,
+                                                       int n_iters, float tol, int want_plan,
+                                                       int want_cost);
+
+/*
+ * dot_sinkhorn_fwd with X = dot_sq_dist(x, y, cost_scale) and score_sign = -1
+ * (out_mode 0), without the matrix: for 1 <= d <= 4 and tol == 0 (any n, m)
+ * every half-step builds the cost entries it needs from the points, so no
+ * B x n x m array is read or written in the iterations; other requests
+ * (d > 4, tol > 0) materialise C in the workspace and run the matrix solvers.
+ * plan [B,n,m] may be NULL (potentials and cost only: the point kernels then
+ * write no B x n x m array at all); cost [B] may be NULL.  log_a, log_b,
+ * pot_u, pot_v and status as dot_sinkhorn_fwd.  Results agree with
+ * dot_sinkhorn_fwd on the materialised matrix within rounding (the point
+ * kernels form K + v with one rounding and merge the log-sum-exps in another
+ * order).
+ * Extension with no counterpart in the reference (its sinkhorn() takes a
+ * materialised cost, dot/sinkhorn.py:1284-1714).
+ */
+DOT_API int dot_sinkhorn_points_fwd(const float* x, const float* y, int64_t B, int64_t n, int64_t m,
+                                    int d, float cost_scale, const float* log_a, const float* log_b,
+                                    float tau, int n_iters, float tol, float* plan, float* cost,
+                                    float* pot_u, float* pot_v, int32_t* status, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /*
  * NCCL communicator for dot_sinkhorn_fwd_rowshard, for callers that have
  * none: rank 0 creates a 128-byte id, the caller hands it to every rank (any

@@ -428,3 +428,32 @@ void orc_bidir_backward(const float *sim, const float *out, const float *g,
     free(dr);
     free(dc);
 }
+
+/*
+ * Squared-distance cost of two point clouds, for the point-cloud solver
+ * (dot_sinkhorn_points_fwd), which has no counterpart in the reference: its
+ * callers build such costs with torch.cdist(x, y) ** 2 and pass the matrix to
+ * sinkhorn() (dot/sinkhorn.py:1284).  x [B,n,d], y [B,m,d], C [B,n,m]:
+ *     s = (x_0 - y_0)^2,  s = fmaf(x_k - y_k, x_k - y_k, s) for k >= 1,
+ *     C = s * scale,
+ * every operation rounded once to fp32 (C99 fmaf is the correctly rounded
+ * fused multiply-add), the operation sequence the GPU kernels perform.
+ */
+void orc_sq_dist(const float *x, const float *y, float *C, int64_t B, int64_t n,
+                 int64_t m, int d, float scale) {
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t i = 0; i < n; ++i) {
+            const float *xi = x + (b * n + i) * d;
+            float *ci = C + (b * n + i) * m;
+            for (int64_t j = 0; j < m; ++j) {
+                const float *yj = y + (b * m + j) * d;
+                float t = xi[0] - yj[0];
+                float s = t * t;
+                for (int k = 1; k < d; ++k) {
+                    t = xi[k] - yj[k];
+                    s = fmaf(t, t, s);
+                }
+                ci[j] = s * scale;
+            }
+        }
+}

@@ -80,6 +80,9 @@ def _lib(kind: str) -> ctypes.CDLL:
         f.argtypes = [_fp, _fp, _fp, _fp, _fp, _fp, _fp, i64, i64, i64, ctypes.c_float, ctypes.c_int]
         f.restype = None
         if kind == "restated":
+            f = lib.orc_sq_dist
+            f.argtypes = [_fp, _fp, _fp, i64, i64, i64, ctypes.c_int, ctypes.c_float]
+            f.restype = None
             f = lib.orc_sinkhorn_dual
             f.argtypes = [_fp, _fp, _fp, i64, i64, i64, ctypes.c_float, ctypes.c_int,
                           ctypes.c_float, _fp, _fp, ctypes.POINTER(ctypes.c_int)]
@@ -321,6 +324,36 @@ def sinkhorn_api(C, reg: float, n_iters: int, a=None, b=None, backward_iters: in
         gla, gtau = sinkhorn_backward_implicit(log_alpha, P, G, reg, bi, tol=bwd_tol, kind=kind)
     dC = (g[:, None, None] * P - gla).astype(np.float32)
     out.update(dC=dC, dreg=np.float32(gtau.sum(dtype=np.float64)), grad_log_alpha=gla, grad_tau=gtau)
+    return out
+
+
+def sq_dist(x, y, cost_scale: float = 1.0) -> np.ndarray:
+    """Squared-distance cost of point clouds x [B,n,d], y [B,m,d] with the
+    operation sequence of the GPU point-cloud solver (``orc_sq_dist``)."""
+    x, y = _f32(x), _f32(y)
+    B, n, d = x.shape
+    m = y.shape[1]
+    C = np.empty((B, n, m), np.float32)
+    _lib("restated").orc_sq_dist(_ptr(x), _ptr(y), _ptr(C), B, n, m, d, cost_scale)
+    return C
+
+
+def sinkhorn_points_api(x, y, reg: float, n_iters: int, a=None, b=None, cost_scale: float = 1.0,
+                        with_grad: bool = True, backward_iters: int | None = None) -> dict:
+    """``sinkhorn(sq_dist(x, y), reg, n_iters, a, b)`` on the reference's CPU
+    path (``sinkhorn_api``) plus the gradients of ``cost.sum()`` with respect
+    to the points, chained through ``dC`` in float64:
+    ``dx_i = 2 s sum_j dC_ij (x_i - y_j)``, ``dy_j = 2 s sum_i dC_ij (y_j - x_i)``."""
+    x, y = _f32(x), _f32(y)
+    C = sq_dist(x, y, cost_scale)
+    out = sinkhorn_api(C, reg, n_iters, a, b, backward_iters=backward_iters, with_grad=with_grad)
+    out["C"] = C
+    if with_grad:
+        dC = out["dC"].astype(np.float64)
+        xd, yd = x.astype(np.float64), y.astype(np.float64)
+        out["dx"] = (2.0 * cost_scale * (xd * dC.sum(axis=2)[..., None] - dC @ yd)).astype(np.float32)
+        out["dy"] = (2.0 * cost_scale * (yd * dC.sum(axis=1)[..., None] -
+                                         np.swapaxes(dC, 1, 2) @ xd)).astype(np.float32)
     return out
 
 
