@@ -511,38 +511,51 @@ def measure_batchshard_cfg4(rank: int, world: int, dev) -> dict:
             "unit": "cost-elem-iters/s", "scaling": "strong", "problems_per_gpu": -(-cfg["B"] // world)}
 
 
-def measure_points_cfg5(dev) -> dict:
+def measure_points_cfg5(dev, n=None, iters=None, steps: int = 3, warmup: int = 3) -> dict:
     """configs[4] (32768 x 32768 U[0,1)^3 clouds, reg 0.01, 500 iterations)
     through ``dot_b200.sinkhorn_points``: the squared distances built inside
-    the sweeps from the two clouds (no 4 GiB cost matrix), with and without
-    writing the plan.  The iterations then read no matrix from HBM; their
-    bound is the exponential unit (one ex2 per element-iteration)."""
+    the half-steps from the two clouds (no 4 GiB cost matrix), with and
+    without writing the plan.  The iterations read no matrix from HBM; per
+    element-iteration the two half-steps execute 2 ex2 and 2 x (2 d + 3) FP32
+    lane operations (d = 3: 18), so the roofline is the FP32 pipe (128 lane
+    operations per SM per clock) with the exponential unit (16 per SM per
+    clock) beside it."""
     import torch
 
     import dot_b200
 
     cfg = CONFIGS["cfg5"]
+    n = cfg["n"] if n is None else n
+    iters = cfg["iters"] if iters is None else iters
     g = torch.Generator(device="cpu")
     g.manual_seed(1234)
-    x = torch.rand(cfg["n"], 3, generator=g).to(dev)
+    x = torch.rand(n, 3, generator=g).to(dev)
     y = torch.rand(cfg["m"], 3, generator=g).to(dev)
-    units = cfg["n"] * cfg["m"] * cfg["iters"]
-    out = {"workload": cfg["desc"] + "; cost built in the sweeps from the two clouds",
-           "n_gpus": 1, "unit": "cost-elem-iters/s"}
+    units = n * cfg["m"] * iters
+    out = {"workload": cfg["desc"] + "; cost built in the half-steps from the two clouds"
+                       + (f" (run with {n} rows, {iters} iterations)" if (n, iters) != (cfg["n"], cfg["iters"]) else ""),
+           "metric": METRIC_FWD, "n_gpus": 1, "unit": "cost-elem-iters/s", "steps": steps, "warmup": warmup}
     for key, plan in (("with_plan", True), ("cost_only", False)):
         def step(plan=plan):
-            return dot_b200.sinkhorn_points(x, y, cfg["reg"], cfg["iters"], return_plan=plan).cost
-        steps = 3
-        ms, prof = time_device(step, steps, 3, 1, dev, profile=True)
+            return dot_b200.sinkhorn_points(x, y, cfg["reg"], iters, return_plan=plan).cost
+        ms, prof = time_device(step, steps, warmup, 1, dev, profile=True)
         it = prof["sk_fwd_iter"]
         out[key] = {"ms_per_step": ms / steps, "value": units * steps / (ms / 1e3),
                     "iterations_ms": it["ms"] / steps, "launches_per_step": it["launches"] // steps}
     it_s = out["cost_only"]["iterations_ms"] / 1e3
-    peak = 148 * 16 * 1965e6
-    out["roofline"] = {"bound": "sfu", "kernel_class": "sk_fwd_iter",
-                       "achieved": units / it_s / 1e12 if it_s > 0 else None, "unit": "Tex2/s",
-                       "peak": peak / 1e12, "peak_source": "nominal: 16 ex2 per SM per clock x 148 SMs x 1965 MHz",
-                       "frac": (units / it_s) / peak if it_s > 0 else None}
+    clock = 1965e6
+    fp32_peak, xu_peak = 148 * 128 * clock, 148 * 16 * clock
+    fp32 = 18 * units / it_s if it_s > 0 else None
+    xu = 2 * units / it_s if it_s > 0 else None
+    out["roofline"] = {"bound": "fp32", "kernel_class": "sk_fwd_iter",
+                       "achieved": fp32 / 1e12 if fp32 else None, "unit": "T FP32 lane-ops/s",
+                       "peak": fp32_peak / 1e12, "frac": fp32 / fp32_peak if fp32 else None,
+                       "peak_source": "nominal: 128 FP32 lanes per SM per clock x 148 SMs x 1965 MHz "
+                                      "(packed f32x2 measured at the same lane rate)",
+                       "sfu": {"achieved": xu / 1e12 if xu else None, "unit": "T ex2/s", "peak": xu_peak / 1e12,
+                               "frac": xu / xu_peak if xu else None}}
+    out["value"] = out["with_plan"]["value"]
+    out["ms_per_step"] = out["with_plan"]["ms_per_step"]
     torch.cuda.empty_cache()
     return out
 
@@ -911,6 +924,8 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=None, help="override the config's iteration count (profiling)")
     ap.add_argument("--rows", type=int, default=None, help="override the config's row count n (profiling)")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch size B (profiling)")
+    ap.add_argument("--points", action="store_true",
+                    help="configs[4] from its two point clouds through dot_b200.sinkhorn_points (1 GPU)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     cfg["name"] = args.config
@@ -925,6 +940,12 @@ def main() -> None:
         cfg["desc"] += f" (run with batch {args.batch})"
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif args.points:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps(measure_points_cfg5(torch.device("cuda", 0), n=args.rows, iters=args.iters,
+                                             steps=args.steps, warmup=args.warmup)), flush=True)
     else:
         run_ours(args, cfg)
 

@@ -61,7 +61,7 @@ skp_sqdist_kernel(const float* __restrict__ x, const float* __restrict__ y, int6
 // are exactly 0), so the sweep needs no bounds checks.
 constexpr int kHW = 4;              // warps per CTA
 constexpr int kHRows = 32 * kHW;    // side-a points per CTA (one per lane)
-constexpr int kHU = 8;              // side-b points per inner step
+constexpr int kHU = 16;             // side-b padding and chunk granularity (a multiple of every step)
 
 __host__ __device__ constexpr int rec_f4(int d) { return (2 * (d + 1) + 3) / 4; }   // float4 per record
 __host__ __device__ inline int64_t padded_points(int64_t nb) { return (nb + kHU - 1) / kHU * kHU; }
@@ -94,70 +94,114 @@ struct HalfArgs {
     float2* part;        // [B][nchunk][na] (max, sum) partials
 };
 
-// One chunk of one half-step: the lane's point i of side a against side-b
-// points [j0, j1): (max, sum) of t_j = K_ij + w_j, with
+// One chunk of one half-step: each lane's RL points i of side a against
+// side-b points [j0, j1): (max, sum) of t_j = K_ij + w_j, with
 //   s = sq_dist's sum of squares (packed, per column pair), t = fma(s, kfold, w)
 //   (one rounding; C * kinv with C = s * scale for scale 1 exactly),
 //   sum of exp(t - m) as 2^(t log2e - mL), mL = m log2e rounded and the
 //   remainder 2^-(m log2e - mL) taken out at the end (as the matrix kernels do).
-template <int PD>
+// The RL points of a lane share every record load and give the warp RL
+// independent dependency chains.  Measured on 32768 x 32768 3-D clouds (one
+// half-step, ms): 1 point per lane 0.59 (0.55 with the next step's records
+// loaded one step ahead), 2 points 0.39, 4 points 0.38 (10 elements per clock
+// per SM; steps of 2 or 8 pairs 0.40), 8 points 0.44 (spills) -- kRL = 4,
+// kNP = 4.
+template <int PD, int RL, int NP>
 __global__ void __launch_bounds__(kHW * 32) skp_half_kernel(HalfArgs h, int64_t b0) {
+    static_assert(kHU % (2 * NP) == 0, "a step must divide the chunk granularity");
     constexpr int R4 = rec_f4(PD);
     const int64_t b = b0 + blockIdx.z;
-    const int64_t i = int64_t(blockIdx.x) * kHRows + threadIdx.x;
+    const int64_t i0 = int64_t(blockIdx.x) * (kHRows * RL) + threadIdx.x;   // points i0 + r * kHRows
     const int chunk = int(blockIdx.y);
     const int64_t nbp = padded_points(h.nb);
     const int j0 = int(int64_t(chunk) * h.ch / 2);                     // pair indices
     const int j1 = int(min(nbp, int64_t(chunk) * h.ch + h.ch) / 2);
-    const bool own = i < h.na;
-    float2 xs[PD];
+    float2 xs[RL][PD];
 #pragma unroll
-    for (int k = 0; k < PD; ++k) xs[k] = splat2(own ? __ldg(h.pa + (b * h.na + i) * PD + k) : 0.0f);
+    for (int r = 0; r < RL; ++r) {
+        const int64_t i = i0 + r * kHRows;
+#pragma unroll
+        for (int k = 0; k < PD; ++k) xs[r][k] = splat2(i < h.na ? __ldg(h.pa + (b * h.na + i) * PD + k) : 0.0f);
+    }
     const float4* rb = h.rb + b * (nbp / 2) * R4;
     const float2 kf = splat2(h.kfold), l2 = splat2(kLog2e);
-    float m = kNegBig, mL = fmaxf(m, -1.0e37f) * kLog2e;
-    float2 s2 = make_float2(0.0f, 0.0f);
-    for (int jp = j0; jp < j1; jp += kHU / 2) {
-        float2 t[kHU / 2];
+    float m[RL], mL[RL];
+    float2 s2[RL];
 #pragma unroll
-        for (int p = 0; p < kHU / 2; ++p) {
+    for (int r = 0; r < RL; ++r) {
+        m[r] = kNegBig;
+        mL[r] = fmaxf(m[r], -1.0e37f) * kLog2e;
+        s2[r] = make_float2(0.0f, 0.0f);
+    }
+    auto step = [&](const float4 (&q)[NP][R4]) {
+        float2 t[RL][NP];
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
             float rv[4 * R4];
 #pragma unroll
-            for (int r = 0; r < R4; ++r) {
-                const float4 f = __ldg(rb + (jp + p) * R4 + r);
-                rv[4 * r + 0] = f.x;
-                rv[4 * r + 1] = f.y;
-                rv[4 * r + 2] = f.z;
-                rv[4 * r + 3] = f.w;
+            for (int c = 0; c < R4; ++c) {
+                rv[4 * c + 0] = q[p][c].x;
+                rv[4 * c + 1] = q[p][c].y;
+                rv[4 * c + 2] = q[p][c].z;
+                rv[4 * c + 3] = q[p][c].w;
             }
-            float2 d = add2(xs[0], make_float2(rv[0], rv[1]));
-            float2 sq = mul2(d, d);
 #pragma unroll
-            for (int k = 1; k < PD; ++k) {
-                d = add2(xs[k], make_float2(rv[2 * k], rv[2 * k + 1]));
-                sq = fma2(d, d, sq);
+            for (int r = 0; r < RL; ++r) {
+                float2 d = add2(xs[r][0], make_float2(rv[0], rv[1]));
+                float2 sq = mul2(d, d);
+#pragma unroll
+                for (int k = 1; k < PD; ++k) {
+                    d = add2(xs[r][k], make_float2(rv[2 * k], rv[2 * k + 1]));
+                    sq = fma2(d, d, sq);
+                }
+                t[r][p] = fma2(sq, kf, make_float2(rv[2 * PD], rv[2 * PD + 1]));
             }
-            t[p] = fma2(sq, kf, make_float2(rv[2 * PD], rv[2 * PD + 1]));
         }
-        const float mx = max_of(t);
-        if (__any_sync(0xffffffffu, mx > m)) {   // some lane's maximum grew: rescale (factor 1 elsewhere)
-            const float mn = fmaxf(m, mx);
-            const float mLn = fmaxf(mn, -1.0e37f) * kLog2e;
-            const float f = ex2(mL - mLn);
-            s2 = mul2(s2, splat2(f));
-            m = mn;
-            mL = mLn;
-        }
-        const float2 nm = splat2(-mL);
+        float mx[RL];
+        bool grew = false;
 #pragma unroll
-        for (int p = 0; p < kHU / 2; ++p) {
-            const float2 a = fma2(t[p], l2, nm);
-            s2 = add2(s2, make_float2(ex2(a.x), ex2(a.y)));
+        for (int r = 0; r < RL; ++r) {
+            mx[r] = max_of(t[r]);
+            grew = grew || mx[r] > m[r];
         }
+        if (__any_sync(0xffffffffu, grew)) {   // some maximum grew: rescale (factor 1 elsewhere)
+#pragma unroll
+            for (int r = 0; r < RL; ++r) {
+                const float mn = fmaxf(m[r], mx[r]);
+                const float mLn = fmaxf(mn, -1.0e37f) * kLog2e;
+                s2[r] = mul2(s2[r], splat2(ex2(mL[r] - mLn)));
+                m[r] = mn;
+                mL[r] = mLn;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            const float2 nm = splat2(-mL[r]);
+#pragma unroll
+            for (int p = 0; p < NP; ++p) {
+                const float2 a = fma2(t[r][p], l2, nm);
+                s2[r] = add2(s2[r], make_float2(ex2(a.x), ex2(a.y)));
+            }
+        }
+    };
+    auto load = [&](float4 (&q)[NP][R4], int jp) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c = 0; c < R4; ++c) q[p][c] = __ldg(rb + (jp + p) * R4 + c);
+    };
+    for (int jp = j0; jp < j1; jp += NP) {
+        float4 q[NP][R4];
+        load(q, jp);
+        step(q);
     }
-    if (own) {
-        const float cr = fmaf(fmaxf(m, -1.0e37f), kLog2e, -mL);   // exact remainder of the rounded mL
-        h.part[(b * h.nchunk + chunk) * h.na + i] = make_float2(m, (s2.x + s2.y) * ex2(-cr));
+#pragma unroll
+    for (int r = 0; r < RL; ++r) {
+        const int64_t i = i0 + r * kHRows;
+        if (i < h.na) {
+            const float cr = fmaf(fmaxf(m[r], -1.0e37f), kLog2e, -mL[r]);   // exact remainder of the rounded mL
+            h.part[(b * h.nchunk + chunk) * h.na + i] = make_float2(m[r], (s2[r].x + s2[r].y) * ex2(-cr));
+        }
     }
 }
 
@@ -284,8 +328,12 @@ struct HalfPlan {
     int nchunk;
     int64_t ch;
 };
+// Points of side a per lane and side-b pairs per step of the half-step kernel.
+constexpr int kRL = 4;
+constexpr int kNP = 4;
+
 HalfPlan half_plan(int64_t B, int64_t na, int64_t nb) {
-    const int64_t base = ceil_div(na, kHRows) * B;
+    const int64_t base = ceil_div(na, kHRows * kRL) * B;
     int64_t chunks = ceil_div(int64_t(2 * 148 * 16), base);
     chunks = std::max<int64_t>(1, std::min<int64_t>(chunks, ceil_div(nb, 256)));
     HalfPlan hp;
@@ -314,9 +362,9 @@ PointsWs carve_points(Carve& c, int64_t B, int64_t n, int64_t m, int d, bool wan
 template <int PD>
 void launch_half(const HalfArgs& h, int64_t B, cudaStream_t st) {
     for (int64_t b0 = 0; b0 < B; b0 += kMaxGridZ) {
-        const dim3 grid(unsigned(ceil_div(h.na, kHRows)), unsigned(h.nchunk),
+        const dim3 grid(unsigned(ceil_div(h.na, kHRows * kRL)), unsigned(h.nchunk),
                         unsigned(std::min<int64_t>(kMaxGridZ, B - b0)));
-        skp_half_kernel<PD><<<grid, kHW * 32, 0, st>>>(h, b0);
+        skp_half_kernel<PD, kRL, kNP><<<grid, kHW * 32, 0, st>>>(h, b0);
     }
 }
 
