@@ -230,6 +230,9 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
     __shared__ int s_flag;
     __shared__ int s_nfix;
     __shared__ int s_fix[1024];
+    __shared__ unsigned s_rel[S];        // warps done with a stage (wrapping counter)
+    __shared__ int s_issued, s_kfail;    // blocks issued so far; first block whose wait expired
+    __shared__ volatile int s_abort;     // a bounded wait expired: stop waiting and copying
 
     pdl_launch_dependents();
     const FusedCommon& c = a.c;
@@ -251,7 +254,15 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
         }
         ring_prime(rg);
     }
-    if (tid == 0) s_nfix = 0;
+    if (tid == 0) {
+        s_nfix = 0;
+        s_abort = 0;
+        s_kfail = rg.g1;
+        s_issued = min(rg.g1, rg.g0 + S);   // ring_prime issued these
+#pragma unroll
+        for (int k = 0; k < S; ++k) s_rel[k] = 0u;
+    }
+    __syncthreads();
 
     auto live = [&](int p) -> bool { return FULL || (4 * lane + 128 * p) < m; };
     // packed two-lane arithmetic (pack.cuh) on element pairs (2k, 2k+1)
@@ -284,10 +295,12 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             const int i = wid + kFW * q;
             lar[q] = (a.la != nullptr && i < rj) ? __ldg(a.la + grow0 + i) : a.la_def;
         }
-        const bool ok = rg.wait(g, c.err);
-        if (!__syncthreads_and(ok)) {
-            ring_drain(rg, g, c.err);
-            return;
+        // warps run decoupled inside a problem segment: each waits for the
+        // stage itself, and the last warp done with it refills it (below)
+        const bool ok = __all_sync(0xffffffffu, !s_abort && rg.wait(g, c.err));
+        if (!ok && lane == 0) {
+            atomicMin(&s_kfail, g);
+            s_abort = 1;
         }
         const float* xs = rg.buf(g);
         auto do_row = [&](int q) {
@@ -342,16 +355,39 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
 #pragma unroll
             for (int k = 0; k < NC / 2; ++k) cS[k] = fma2(t[k], w, cS[k]);
         };
-        if (rj == R) {
+        if (!ok) {
+        } else if (rj == R) {
 #pragma unroll
             for (int q = 0; q < RPW; ++q) do_row(q);
         } else {
             for (int q = 0; q < RPW; ++q)
                 if (wid + kFW * q < rj) do_row(q);
         }
-        __syncthreads();   // stage buffer of block g is free again
 
-        if (g + 1 == rg.g1 || jb + 1 == c.s.nblk) {
+        if (g + 1 != rg.g1 && jb + 1 != c.s.nblk) {
+            // inside a segment: release the stage; the last warp to do so
+            // issues the copy of block g + S into it
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                const int st = (g - rg.g0) % S;
+                if (atomicInc(&s_rel[st], unsigned(kFW - 1)) == unsigned(kFW - 1)) {
+                    __threadfence_block();
+                    if (g + S < rg.g1 && !s_abort) {
+                        rg.issue(g + S);
+                        s_issued = g + S + 1;
+                    }
+                }
+            }
+        } else {
+            __syncthreads();   // every warp is done with the segment's rows (and with stage g)
+            if (__syncthreads_or(s_abort)) {   // results are void; keep the barrier sequence
+                if (++jb == c.s.nblk) {
+                    jb = 0;
+                    ++b;
+                }
+                continue;
+            }
             // ---- end of this CTA's part of problem b: publish its column partials ----
             const int kfirst = sched_owner(c.s, b * c.s.nblk);
             const int nseg = sched_owner(c.s, (b + 1) * c.s.nblk - 1) - kfirst + 1;
@@ -416,12 +452,21 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
             }
             fence_proxy_async_smem();   // merge-buffer writes before the stage is refilled by a bulk copy
             __syncthreads();
+            if (tid == 0 && g + S < rg.g1) {
+                rg.issue(g + S);
+                s_issued = g + S + 1;
+            }
         }
-        if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
         if (++jb == c.s.nblk) {
             jb = 0;
             ++b;
         }
+    }
+    __syncthreads();
+    if (s_abort) {   // copies still in flight after an expired wait
+        if (tid == 0)
+            for (int k = s_kfail; k < s_issued && k < s_kfail + S; ++k) rg.wait(k, nullptr);
+        __syncthreads();
     }
 
     if (tolmode) {
