@@ -204,35 +204,45 @@ __device__ __forceinline__ bool arrive_last(int32_t* cnt, int64_t b, int nseg, i
 }
 
 // The CTA's ring over its block range [g0, g1) (stage k at smem + k * kStage).
+// Positions p run g0 .. g1-1; the block at position p is p, or, for a ring
+// walked backwards (rev), g0 + g1 - 1 - p.  The second sweep of a direction
+// walks its range backwards: the first sweep gave every CTA the same range
+// and read it forwards, so its last blocks -- the first ones read again --
+// are the ones still in L2.
 struct Ring {
     const SweepArgs* a;
     unsigned char* smem;
     uint64_t* bar;
     int g0, g1;
+    bool rev;
 
-    __device__ unsigned char* stage(int g) const { return smem + size_t((g - g0) % kS) * kStage; }
-    __device__ uint64_t* barrier(int g) const { return bar + (g - g0) % kS; }
-    __device__ uint32_t parity(int g) const { return uint32_t(((g - g0) / kS) & 1); }
-    __device__ void issue(int g) const {   // one thread
+    __device__ int block(int p) const { return rev ? g0 + g1 - 1 - p : p; }
+    __device__ unsigned char* stage(int p) const { return smem + size_t((p - g0) % kS) * kStage; }
+    __device__ uint64_t* barrier(int p) const { return bar + (p - g0) % kS; }
+    __device__ uint32_t parity(int p) const { return uint32_t(((p - g0) / kS) & 1); }
+    __device__ void issue(int p) const {   // one thread
+        const int g = block(p);
         const int b = g / a->s.nblk, jb = g - b * a->s.nblk;
         const int64_t r0 = int64_t(jb) * a->R;
         const uint32_t rows = uint32_t(min(int64_t(a->R), a->L1 - r0));
         const int64_t row0 = int64_t(b) * a->L1 + r0;
         const uint32_t b0 = rows * uint32_t(a->L2) * uint32_t(a->esz);
         const uint32_t b1 = a->gout ? rows * uint32_t(a->L2) * 4u : 0u;
-        uint64_t* bb = barrier(g);
+        uint64_t* bb = barrier(p);
         mbar_arrive_expect_tx(bb, b0 + b1);
-        bulk_g2s(stage(g), a->sim + row0 * a->L2 * a->esz, b0, bb);
-        if (a->gout) bulk_g2s(stage(g) + a->gout_off, a->gout + row0 * a->L2, b1, bb);
+        bulk_g2s(stage(p), a->sim + row0 * a->L2 * a->esz, b0, bb);
+        if (a->gout) bulk_g2s(stage(p) + a->gout_off, a->gout + row0 * a->L2, b1, bb);
     }
-    __device__ bool wait(int g) const { return mbar_wait_sleep(barrier(g), parity(g), a->err); }
+    __device__ bool wait(int p) const { return mbar_wait_sleep(barrier(p), parity(p), a->err); }
 };
 
-__device__ __forceinline__ Ring ring_start(const SweepArgs& a, uint64_t* bars, unsigned char* smem) {
+__device__ __forceinline__ Ring ring_start(const SweepArgs& a, uint64_t* bars, unsigned char* smem,
+                                           bool rev = false) {
     Ring r;
     r.a = &a;
     r.smem = smem;
     r.bar = bars;
+    r.rev = rev;
     r.g0 = sched_q(a.s, blockIdx.x);
     r.g1 = sched_q(a.s, int(blockIdx.x) + 1);
     if (threadIdx.x == 0) {
@@ -443,13 +453,14 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
-    const Ring rg = ring_start(a, bars, smem);
+    const Ring rg = ring_start(a, bars, smem, true);
     pdl_wait();   // the first sweep's statistics / dots are complete and visible
     int64_t l1 = 0, l2 = 0;
-    int b = rg.g0 / a.s.nblk, jb = rg.g0 - b * a.s.nblk;
     int cur = -1;
 
-    for (int g = rg.g0; g < rg.g1; ++g) {
+    for (int pos = rg.g0; pos < rg.g1; ++pos) {
+        const int g = rg.block(pos);
+        const int b = g / a.s.nblk, jb = g - b * a.s.nblk;
         if (b != cur) {   // the barrier below orders these writes before their reads
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
@@ -459,12 +470,12 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
             }
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
-        const bool ok = rg.wait(g);
+        const bool ok = rg.wait(pos);
         if (!__syncthreads_and(ok)) {
-            ring_drain(rg, g);
+            ring_drain(rg, pos);
             return;
         }
-        const T* xs = reinterpret_cast<const T*>(rg.stage(g));
+        const T* xs = reinterpret_cast<const T*>(rg.stage(pos));
         for (int il = slot; il < rows; il += SLOTS) {
             const int64_t i = int64_t(jb) * a.R + il;
             const int64_t row = int64_t(b) * L1 + i;
@@ -501,11 +512,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
             }
         }
         __syncthreads();   // the stage is free
-        if (tid == 0 && g + kS < rg.g1) rg.issue(g + kS);
-        if (++jb == a.s.nblk) {
-            jb = 0;
-            ++b;
-        }
+        if (tid == 0 && pos + kS < rg.g1) rg.issue(pos + kS);
     }
 }
 
@@ -655,26 +662,27 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
-    const Ring rg = ring_start(a, bars, smem);
+    const Ring rg = ring_start(a, bars, smem, true);
     pdl_wait();   // the first sweep's statistics / dots are complete and visible
     int64_t l1 = 0, l2 = 0;
-    int b = rg.g0 / a.s.nblk, jb = rg.g0 - b * a.s.nblk;
     int cur = -1;
 
-    for (int g = rg.g0; g < rg.g1; ++g) {
+    for (int pos = rg.g0; pos < rg.g1; ++pos) {
+        const int g = rg.block(pos);
+        const int b = g / a.s.nblk, jb = g - b * a.s.nblk;
         if (b != cur) {   // the barrier below orders these writes before their reads
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
             for (int64_t col = tid; col < L2; col += kT) s_cs[col] = __ldg(a.cstat + int64_t(b) * L2 + col);
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
-        const bool ok = rg.wait(g);
+        const bool ok = rg.wait(pos);
         if (!__syncthreads_and(ok)) {
-            ring_drain(rg, g);
+            ring_drain(rg, pos);
             return;
         }
-        const T* xs = reinterpret_cast<const T*>(rg.stage(g));
-        const float* gs = reinterpret_cast<const float*>(rg.stage(g) + a.gout_off);
+        const T* xs = reinterpret_cast<const T*>(rg.stage(pos));
+        const float* gs = reinterpret_cast<const float*>(rg.stage(pos) + a.gout_off);
         const float* db = a.cdot + int64_t(b) * L2;
         for (int il = slot; il < rows; il += SLOTS) {
             const int64_t i = int64_t(jb) * a.R + il;
@@ -724,11 +732,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
             a.tau_row[int64_t(b) * L1 + int64_t(jb) * a.R + tid] = acc;
         }
         __syncthreads();   // s_tp is read before the next block writes it
-        if (tid == 0 && g + kS < rg.g1) rg.issue(g + kS);
-        if (++jb == a.s.nblk) {
-            jb = 0;
-            ++b;
-        }
+        if (tid == 0 && pos + kS < rg.g1) rg.issue(pos + kS);
     }
 }
 
