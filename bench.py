@@ -29,6 +29,8 @@ BASELINE configuration with its time per step, throughput, dominant-kernel
 roofline and CPU baseline; ``rowshard_cfg5`` -- configs[4] (32768 x 32768,
 reg 0.01) forward at 100 iterations, on one GPU at N=1 and rows sharded over
 the N GPUs (library-owned NCCL all-gather per iteration) at N>1;
+``rowshard_points_cfg5`` -- the same problem from its two point clouds
+(``sinkhorn_points_rowshard``: the cost built in the half-steps); and
 ``batchshard_cfg4`` -- configs[3] with its 4096 problems split over the N
 GPUs.  The last two are strong scaling and give the 1/2/4/8-GPU curve of the
 sharded configurations when the driver runs the bench at several N.
@@ -493,6 +495,40 @@ def measure_rowshard_cfg5(iters: int, rank: int, world: int, dev) -> dict:
     return out
 
 
+def measure_rowshard_points_cfg5(iters: int, rank: int, world: int, dev) -> dict:
+    """configs[4] (32768 x 32768 U[0,1)^3 clouds, reg 0.01) forward at
+    ``iters`` iterations from the two clouds, rows of x split over the ranks
+    (``sinkhorn_points_rowshard``: the half-steps on each rank's rows, one
+    NCCL all-gather of the column (max, sum) pairs per iteration); the cost
+    only (no plan)."""
+    import torch
+
+    from dot_b200.distributed import shard_range, sinkhorn_points_rowshard
+
+    cfg = CONFIGS["cfg5"]
+    g = torch.Generator(device="cpu")
+    g.manual_seed(1234)
+    x = torch.rand(1, cfg["n"], 3, generator=g)
+    y = torch.rand(1, cfg["m"], 3, generator=g).to(dev)
+    lo, hi = shard_range(cfg["n"], rank, world)
+    xl = x[:, lo:hi].contiguous().to(dev)
+
+    def step():
+        return sinkhorn_points_rowshard(xl, y, cfg["reg"], iters, n_total=cfg["n"], want_plan=False)["cost"]
+
+    steps = 3
+    ms, _ = time_device(step, steps, 2, world, dev, profile=False)
+    units = cfg["n"] * cfg["m"] * iters
+    it_s = ms / steps / 1e3
+    fp32_peak = 148 * 128 * 1965e6 * world
+    torch.cuda.empty_cache()
+    return {"n_gpus": world, "n_iters": iters, "ms_per_step": ms / steps, "ms_per_iter": ms / steps / iters,
+            "value": units / it_s, "unit": "cost-elem-iters/s", "scaling": "strong", "rows_per_gpu": hi - lo,
+            "roofline": {"bound": "fp32", "achieved": 18 * units / it_s / 1e12, "unit": "T FP32 lane-ops/s",
+                         "peak": fp32_peak / 1e12, "frac": 18 * units / it_s / fp32_peak,
+                         "peak_source": "nominal: 128 FP32 lanes per SM per clock x 148 SMs x 1965 MHz x n_gpus"}}
+
+
 def measure_batchshard_cfg4(rank: int, world: int, dev) -> dict:
     """configs[3] (B=4096, 128x128, 100 iterations, fwd+bwd) with the batch
     split over the ranks by ``sinkhorn_batchshard`` (strong scaling; the
@@ -632,9 +668,11 @@ def run_ours(args, cfg: dict) -> None:
             line["points_cfg5"] = pts
     if not args.no_scaling and cfg["name"] != "cfg5":
         rs = measure_rowshard_cfg5(100, rank, world, dev)
+        rsp = measure_rowshard_points_cfg5(100, rank, world, dev)
         bsd = measure_batchshard_cfg4(rank, world, dev)
         if line is not None:
             line["rowshard_cfg5"] = rs
+            line["rowshard_points_cfg5"] = rsp
             line["batchshard_cfg4"] = bsd
     if line is not None:
         print(json.dumps(line), flush=True)

@@ -55,6 +55,9 @@ _SIGS = {
     "dot_sinkhorn_points_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i, _i, _f, _i, _i]),
     "dot_sinkhorn_points_fwd": (_i, [_vp, _vp, _i64, _i64, _i64, _i, _f, _vp, _vp, _f, _i, _f, _vp, _vp, _vp, _vp,
                                      _vp, _vp, _sz, _vp]),
+    "dot_sinkhorn_points_fwd_rowshard_workspace_bytes": (_sz, [_i64, _i64, _i64, _i, _i]),
+    "dot_sinkhorn_points_fwd_rowshard": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i64, _f, _f, _i, _vp, _vp,
+                                              _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dot_nccl_unique_id": (_i, [_vp]),
     "dot_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _i, _vp, _i]),
     "dot_nccl_comm_destroy": (_i, [_vp]),

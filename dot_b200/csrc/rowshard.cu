@@ -212,4 +212,74 @@ int dot_sinkhorn_fwd_rowshard(const float* X, float score_sign, const float* log
     return check_launch("sinkhorn row-sharded forward");
 }
 
+size_t dot_sinkhorn_points_fwd_rowshard_workspace_bytes(int64_t B, int64_t n, int64_t m, int d, int nranks) {
+    if (B <= 0 || n < 0 || m <= 0 || d < 1 || d > 4 || nranks < 1) return 0;
+    Carve c(nullptr);
+    c.take<float2>(size_t(nranks) * size_t(B * m));
+    c.take<char>(skp_shard_ws(B, n, m, d));
+    return c.size();
+}
+
+int dot_sinkhorn_points_fwd_rowshard(const float* x, const float* y, const float* log_a, const float* log_b,
+                                     int64_t B, int64_t n, int64_t m, int d, int64_t n_total, float cost_scale,
+                                     float tau, int n_iters, void* nccl_comm, float* plan, float* cost,
+                                     float* pot_u, float* pot_v, int32_t* status, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (B < 0 || n < 0 || m < 0) return fail(DOT_ERR_INVALID, "negative dimension");
+    if (d < 1) return fail(DOT_ERR_INVALID, "point dimension must be >= 1");
+    if (d > 4) return fail(DOT_ERR_UNSUPPORTED, "row-sharded point clouds take up to 4 coordinates");
+    if (!(tau > 0.0f) || !std::isfinite(tau)) return fail(DOT_ERR_INVALID, "tau must be > 0");
+    if (!std::isfinite(cost_scale)) return fail(DOT_ERR_INVALID, "cost_scale must be finite");
+    if (n_iters < 0) return fail(DOT_ERR_INVALID, "n_iters must be >= 0");
+    if (n_total < n || n_total < 1) return fail(DOT_ERR_INVALID, "n_total must be >= the shard's row count and >= 1");
+    int nranks = 1, rank = 0;
+    const Nccl* nc = nullptr;
+    if (nccl_comm != nullptr) {
+        nc = &nccl();
+        if (!nc->ok) return fail(DOT_ERR_UNSUPPORTED, nc->why);
+        ncclResult_t r = nc->comm_count(static_cast<ncclComm_t>(nccl_comm), &nranks);
+        if (r == ncclSuccess) r = nc->comm_user_rank(static_cast<ncclComm_t>(nccl_comm), &rank);
+        if (r != ncclSuccess) return nccl_fail(*nc, r, "ncclCommCount/UserRank");
+    }
+    if (B == 0 || m == 0) return DOT_OK;
+    if (!y || !pot_v || !status || (n > 0 && (!x || !pot_u))) return fail(DOT_ERR_INVALID, "null tensor pointer");
+    const size_t need = dot_sinkhorn_points_fwd_rowshard_workspace_bytes(B, n, m, d, nranks);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(DOT_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    Carve c(workspace);
+    float2* gathered = c.take<float2>(size_t(nranks) * size_t(B * m));
+    void* sws = c.take<char>(skp_shard_ws(B, n, m, d));
+    float2* mine = gathered + size_t(rank) * size_t(B * m);
+    const float kinv = -(1.0f / tau);
+    const float la_def = -logf(float(n_total)), lb_def = -logf(float(m));   // uniform marginals of the whole problem
+
+    cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    int rc = skp_shard_begin(x, y, B, n, m, d, pot_u, pot_v, sws, st);
+    for (int it = 0; it < n_iters && rc == DOT_OK; ++it) {
+        rc = skp_shard_rows_pairs(x, y, log_a, la_def, B, n, m, d, cost_scale * kinv, pot_u, mine, sws, st);
+        if (rc != DOT_OK) break;
+        if (nranks > 1) {
+            // in place: this rank's pairs already sit in its slot of the gather buffer
+            ProfScope ps(DOT_K_SK_EXCHANGE, st);
+            const ncclResult_t r = nc->all_gather(mine, gathered, size_t(B * m) * 2, ncclFloat32,
+                                                  static_cast<ncclComm_t>(nccl_comm), st);
+            if (r != ncclSuccess) return nccl_fail(*nc, r, "ncclAllGather (column pairs)");
+        }
+        rc = skp_shard_col_merge(gathered, nranks, log_b, lb_def, B, n, m, d, pot_v, sws, st);
+    }
+    if (rc != DOT_OK) return rc;
+    if (plan != nullptr || cost != nullptr) {
+        rc = skp_shard_plan(x, y, B, n, m, d, cost_scale, kinv, pot_u, pot_v, plan, cost, sws, st);
+        if (rc != DOT_OK) return rc;
+        if (cost != nullptr && nranks > 1) {
+            const ncclResult_t r =
+                nc->all_reduce(cost, cost, size_t(B), ncclFloat32, ncclSum, static_cast<ncclComm_t>(nccl_comm), st);
+            if (r != ncclSuccess) return nccl_fail(*nc, r, "ncclAllReduce (cost)");
+        }
+    }
+    return check_launch("point-cloud row-sharded forward");
+}
+
 }  // extern "C"

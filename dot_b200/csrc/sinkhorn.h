@@ -90,6 +90,25 @@ int sk_wide_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);
 int sk_wide_rows_pairs(const float* X, float kinv, const float* la, float la_def, int64_t B, int64_t n, int64_t m,
                        const float* v2, float* u2, float2* pairs, int32_t* err, void* ws, cudaStream_t st);
 
+// Row shards of the point-cloud solver (sinkhorn_points.cu): this rank holds
+// the points x [B,n,d] of its rows (n may be 0) and all of y [B,m,d], d <= 4.
+// begin packs both clouds and zeroes the potentials; rows_pairs runs the row
+// half-step (u of the shard's rows from v) and the column half-step over the
+// shard's rows, leaving one (max, sum) pair per column in pairs [B,m];
+// col_merge merges the gathered pairs [nranks][B][m] in rank order into v;
+// plan writes the shard's plan rows (plan may be null) and cost sums over
+// its rows.  All share one workspace of skp_shard_ws bytes.
+size_t skp_shard_ws(int64_t B, int64_t n, int64_t m, int d);
+int skp_shard_begin(const float* x, const float* y, int64_t B, int64_t n, int64_t m, int d, float* pot_u,
+                    float* pot_v, void* ws, cudaStream_t st);
+int skp_shard_rows_pairs(const float* x, const float* y, const float* la, float la_def, int64_t B, int64_t n,
+                         int64_t m, int d, float kfold, float* pot_u, float2* pairs, void* ws, cudaStream_t st);
+int skp_shard_col_merge(const float2* gathered, int nranks, const float* lb, float lb_def, int64_t B, int64_t n,
+                        int64_t m, int d, float* pot_v, void* ws, cudaStream_t st);
+int skp_shard_plan(const float* x, const float* y, int64_t B, int64_t n, int64_t m, int d, float cost_scale,
+                   float kinv, const float* pot_u, const float* pot_v, float* plan, float* cost, void* ws,
+                   cudaStream_t st);
+
 // Unrolled backward through a recorded forward (sinkhorn_unrolled.cu):
 // a.bwd_iters = the number of recorded iterations to differentiate through.
 size_t sk_unrolled_bwd_ws(int64_t B, int64_t n, int64_t m);

@@ -227,6 +227,51 @@ __global__ void skp_merge_kernel(const float2* __restrict__ part, int nchunk, in
     rec_a[((b * (padded_points(na) / 2) + (i >> 1)) * rec_f4(d)) * 4 + 2 * d + (i & 1)] = v;
 }
 
+// Row shards: each column's chunk partials over this shard's rows merged
+// into one (max, sum) pair (the column half-step's skp_merge_kernel without
+// the log), for the cross-shard exchange.
+__global__ void skp_pairs_kernel(const float2* __restrict__ part, int nchunk, int64_t B, int64_t m,
+                                 float2* __restrict__ pairs) {
+    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= B * m) return;
+    const int64_t b = idx / m, j = idx - b * m;
+    const float2* pc = part + b * nchunk * m + j;
+    float mm = kNegBig;
+    for (int c = 0; c < nchunk; ++c) mm = fmaxf(mm, pc[int64_t(c) * m].x);
+    float ss = 0.0f;
+    for (int c = 0; c < nchunk; ++c) {
+        const float2 q = pc[int64_t(c) * m];
+        ss = fmaf(q.y, exp_shift(q.x - mm), ss);
+    }
+    pairs[idx] = make_float2(mm, ss);
+}
+
+// v from the gathered pairs [nranks][B][m], merged in rank order (max pass,
+// then the rescaled sums), written to pot_v and to y's records; every rank
+// computes the same v.
+__global__ void skp_rank_merge_kernel(const float2* __restrict__ pairs, int nranks, int64_t B, int64_t m, int d,
+                                      const float* __restrict__ lb, float lb_def, float* __restrict__ pot_v,
+                                      float* __restrict__ rec_y) {
+    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= B * m) return;
+    const int64_t b = idx / m, j = idx - b * m;
+    float mm = kNegBig;
+    for (int r = 0; r < nranks; ++r) mm = fmaxf(mm, pairs[int64_t(r) * B * m + idx].x);
+    float ss = 0.0f;
+    for (int r = 0; r < nranks; ++r) {
+        const float2 q = pairs[int64_t(r) * B * m + idx];
+        ss = fmaf(q.y, exp_shift(q.x - mm), ss);
+    }
+    const float v = (lb ? lb[idx] : lb_def) - lse_finish(mm, ss);
+    pot_v[idx] = v;
+    rec_y[((b * (padded_points(m) / 2) + (j >> 1)) * rec_f4(d)) * 4 + 2 * d + (j & 1)] = v;
+}
+
+__global__ void skp_empty_pairs_kernel(float2* pairs, int64_t count) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < count) pairs[i] = make_float2(kNegBig, 0.0f);
+}
+
 // Plan P = safe_exp((K + u_i) + v_j) with K = C * kinv, C built from the
 // points (out may be null: cost only), and per-row cost partials
 // sum_j P_ij C_ij -- the arithmetic of the matrix epilogue (sk_plan_kernel)
@@ -386,7 +431,91 @@ void half_step(const float* pa, float* rec_a, const float* rec_b, int64_t B, int
 
 bool bad_float(float v) { return !std::isfinite(v); }
 
+// Row-shard workspace: the records of the shard's x (n rows) and of y, the
+// partials of the larger half-step, the cost rows.
+PointsWs carve_shard(Carve& c, int64_t B, int64_t n, int64_t m, int d) {
+    return carve_points(c, B, n > 0 ? n : 1, m, d, true);
+}
+
 }  // namespace
+
+size_t skp_shard_ws(int64_t B, int64_t n, int64_t m, int d) {
+    Carve c(nullptr);
+    carve_shard(c, B, n, m, d);
+    return c.size();
+}
+
+int skp_shard_begin(const float* x, const float* y, int64_t B, int64_t n, int64_t m, int d, float* pot_u,
+                    float* pot_v, void* ws, cudaStream_t st) {
+    Carve c(ws);
+    const PointsWs w = carve_shard(c, B, n, m, d);
+    if (n > 0) cudaMemsetAsync(pot_u, 0, sizeof(float) * size_t(B * n), st);
+    cudaMemsetAsync(pot_v, 0, sizeof(float) * size_t(B * m), st);
+    ProfScope ps(DOT_K_SK_FWD_EPI, st);
+    if (n > 0)
+        skp_pack_kernel<<<unsigned(ceil_div(B * padded_points(n) / 2, 256)), 256, 0, st>>>(x, B, n, d, w.recx);
+    skp_pack_kernel<<<unsigned(ceil_div(B * padded_points(m) / 2, 256)), 256, 0, st>>>(y, B, m, d, w.recy);
+    return check_launch("point-cloud row shard set-up");
+}
+
+int skp_shard_rows_pairs(const float* x, const float* y, const float* la, float la_def, int64_t B, int64_t n,
+                         int64_t m, int d, float kfold, float* pot_u, float2* pairs, void* ws, cudaStream_t st) {
+    Carve c(ws);
+    const PointsWs w = carve_shard(c, B, n, m, d);
+    if (n == 0) {
+        ProfScope ps(DOT_K_SK_EXCHANGE, st);
+        skp_empty_pairs_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(pairs, B * m);
+        return check_launch("point-cloud row shard (no rows)");
+    }
+    {
+        ProfScope ps(DOT_K_SK_FWD_ITER, st, 2 * int(ceil_div(B, kMaxGridZ) + 1));
+        half_step(x, w.recx, w.recy, B, n, m, d, kfold, w.part, la, la_def, pot_u, st);   // u of the shard's rows
+        // column partials over the shard's rows with the new u: side a = y, side b = x
+        const HalfPlan hp = half_plan(B, m, n);
+        HalfArgs h{y, reinterpret_cast<const float4*>(w.recx), m, n, hp.ch, hp.nchunk, kfold, w.part};
+        switch (d) {
+            case 1: launch_half<1>(h, B, st); break;
+            case 2: launch_half<2>(h, B, st); break;
+            case 3: launch_half<3>(h, B, st); break;
+            default: launch_half<4>(h, B, st); break;
+        }
+        skp_pairs_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(w.part, hp.nchunk, B, m, pairs);
+    }
+    return check_launch("point-cloud row shard half-steps");
+}
+
+int skp_shard_col_merge(const float2* gathered, int nranks, const float* lb, float lb_def, int64_t B, int64_t n,
+                        int64_t m, int d, float* pot_v, void* ws, cudaStream_t st) {
+    Carve c(ws);
+    const PointsWs w = carve_shard(c, B, n, m, d);
+    ProfScope ps(DOT_K_SK_EXCHANGE, st);
+    skp_rank_merge_kernel<<<unsigned(ceil_div(B * m, 256)), 256, 0, st>>>(gathered, nranks, B, m, d, lb, lb_def,
+                                                                          pot_v, w.recy);
+    return check_launch("point-cloud column merge");
+}
+
+int skp_shard_plan(const float* x, const float* y, int64_t B, int64_t n, int64_t m, int d, float cost_scale,
+                   float kinv, const float* pot_u, const float* pot_v, float* plan, float* cost, void* ws,
+                   cudaStream_t st) {
+    Carve c(ws);
+    const PointsWs w = carve_shard(c, B, n, m, d);
+    ProfScope ps(DOT_K_SK_FWD_EPI, st);
+    if (n == 0) {
+        if (cost != nullptr) cudaMemsetAsync(cost, 0, sizeof(float) * size_t(B), st);
+        return check_launch("point-cloud row shard plan");
+    }
+    const int64_t rows = B * n;
+    float* crow = cost != nullptr ? w.cost_row : nullptr;
+    switch (d) {
+        case 1: launch_plan<1>(x, y, cost_scale, kinv, pot_u, pot_v, plan, crow, rows, n, m, st); break;
+        case 2: launch_plan<2>(x, y, cost_scale, kinv, pot_u, pot_v, plan, crow, rows, n, m, st); break;
+        case 3: launch_plan<3>(x, y, cost_scale, kinv, pot_u, pot_v, plan, crow, rows, n, m, st); break;
+        default: launch_plan<4>(x, y, cost_scale, kinv, pot_u, pot_v, plan, crow, rows, n, m, st); break;
+    }
+    if (cost != nullptr) skp_cost_sum_kernel<<<unsigned(ceil_div(B, 8)), 256, 0, st>>>(w.cost_row, cost, B, n);
+    return check_launch("point-cloud row shard plan");
+}
+
 }  // namespace dotb
 
 using namespace dotb;

@@ -149,6 +149,52 @@ def sinkhorn_rowshard(C_local: torch.Tensor, reg: float, n_iters: int, n_total: 
     return {"u": u, "v": v, "P": P if want_plan else None, "cost": cost}
 
 
+def sinkhorn_points_rowshard(x_local: torch.Tensor, y: torch.Tensor, reg: float, n_iters: int, n_total: int,
+                             log_a_local: Optional[torch.Tensor] = None, log_b: Optional[torch.Tensor] = None,
+                             cost_scale: float = 1.0, want_plan: bool = False, want_cost: bool = True,
+                             group=None) -> dict:
+    """Row-sharded Sinkhorn forward on point clouds (the cost
+    ``cost_scale * |x_i - y_j|^2`` built in the half-steps, fixed ``n_iters``,
+    1 <= d <= 4).
+
+    ``x_local`` [B, n_local, d] holds this rank's points of the n_total rows,
+    ``y`` [B, m, d] all column points; ``log_a_local`` / ``log_b`` as for
+    :func:`sinkhorn_rowshard`.  Per iteration the library runs the row and
+    column half-steps on this rank's rows and all-gathers one (max, sum) pair
+    per column over NCCL.  Returns ``{"P": plan rows or None, "cost": [B] or
+    None, "u": [B, n_local], "v": [B, m]}``; ``v`` and ``cost`` are the same on
+    every rank.  Every rank must call it with the same arguments apart from
+    its rows.
+    """
+    if not (x_local.is_cuda and y.is_cuda):
+        raise RuntimeError("dot_b200: x_local and y must be CUDA tensors")
+    x = x_local.to(torch.float32).contiguous()
+    yy = y.to(device=x.device, dtype=torch.float32).contiguous()
+    if x.dim() != 3 or yy.dim() != 3 or x.size(0) != yy.size(0) or x.size(2) != yy.size(2):
+        raise ValueError("x_local and y must be [B, n_local, d] and [B, m, d]")
+    B, n, d = x.shape
+    m = yy.size(1)
+    dev = x.device
+    lib = _lib.load()
+    _, world = _world(group)
+    comm = nccl_communicator(group, dev)
+    la = None if log_a_local is None else log_a_local.to(device=dev, dtype=torch.float32).contiguous()
+    lb = None if log_b is None else log_b.to(device=dev, dtype=torch.float32).contiguous()
+    u = torch.empty((B, n), dtype=torch.float32, device=dev)
+    v = torch.empty((B, m), dtype=torch.float32, device=dev)
+    status = torch.zeros((1,), dtype=torch.int32, device=dev)
+    P = torch.empty((B, n, m), dtype=torch.float32, device=dev) if want_plan else None
+    cost = torch.empty((B,), dtype=torch.float32, device=dev) if want_cost else None
+    nb = lib.dot_sinkhorn_points_fwd_rowshard_workspace_bytes(B, n, m, d, world)
+    ws = _lib.workspace(nb, dev)
+    _lib.check(lib.dot_sinkhorn_points_fwd_rowshard(_lib.ptr(x), _lib.ptr(yy), _lib.ptr(la), _lib.ptr(lb), B, n, m, d,
+                                                    int(n_total), float(cost_scale), float(reg), int(n_iters), comm,
+                                                    _lib.ptr(P), _lib.ptr(cost), _lib.ptr(u), _lib.ptr(v),
+                                                    _lib.ptr(status), _lib.ptr(ws), nb, _lib.stream_of(x)),
+               "dot_sinkhorn_points_fwd_rowshard")
+    return {"u": u, "v": v, "P": P, "cost": cost}
+
+
 # ---------------------------------------------------------------------------
 # batch sharding
 # ---------------------------------------------------------------------------

@@ -280,6 +280,33 @@ DOT_API int dot_sinkhorn_points_fwd(const float* x, const float* y, int64_t B, i
                                     float* pot_u, float* pot_v, int32_t* status, void* workspace,
                                     size_t workspace_bytes, void* stream);
 
+/* Bytes of workspace dot_sinkhorn_points_fwd_rowshard needs on a rank holding
+ * n of the rows (0 for d > 4, which it does not take). */
+DOT_API size_t dot_sinkhorn_points_fwd_rowshard_workspace_bytes(int64_t B, int64_t n, int64_t m, int d,
+                                                                int nranks);
+
+/*
+ * dot_sinkhorn_points_fwd for one problem batch whose rows are split over the
+ * ranks of nccl_comm (NULL: one rank): this rank holds the points x [B,n,d]
+ * of its n of the n_total rows (n may be 0; which rows does not matter to the
+ * arithmetic) and their log_a [B,n] (or NULL: uniform -log n_total), and all
+ * of y [B,m,d] and log_b [B,m].  Each iteration runs the row half-step on the shard's points,
+ * the column half-step over the shard's rows -- one (max, sum) pair per
+ * column -- and one in-place NCCL all-gather of the pairs, merged in rank
+ * order, so every rank ends with the same v.  plan [B,n,m] (this rank's rows)
+ * and cost [B] (all-reduced over the ranks) may be NULL.  1 <= d <= 4
+ * (DOT_ERR_UNSUPPORTED otherwise).  status is one device int32 word, 0.
+ * Collective: every rank calls it with the same B, m, d, tau, n_iters and
+ * the same requests for cost.  Extension with no counterpart in the
+ * reference (it has no multi-GPU path).
+ */
+DOT_API int dot_sinkhorn_points_fwd_rowshard(const float* x, const float* y, const float* log_a,
+                                             const float* log_b, int64_t B, int64_t n, int64_t m, int d,
+                                             int64_t n_total, float cost_scale, float tau, int n_iters,
+                                             void* nccl_comm, float* plan, float* cost, float* pot_u,
+                                             float* pot_v, int32_t* status, void* workspace,
+                                             size_t workspace_bytes, void* stream);
+
 /*
  * NCCL communicator for dot_sinkhorn_fwd_rowshard, for callers that have
  * none: rank 0 creates a 128-byte id, the caller hands it to every rank (any

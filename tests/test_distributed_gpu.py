@@ -127,3 +127,85 @@ def test_rowshard_wide_rows_one_rank_matches_forward(shape, reg, cube):
     assert dP < 1e-5, dP
     assert dv < 1e-4, dv
     assert dc < 1e-5, dc
+
+
+# ---------------------------------------------------------------------------
+# point clouds (dot_sinkhorn_points_fwd_rowshard): rows of x split over ranks
+# ---------------------------------------------------------------------------
+
+def _clouds(B, n, m, d, seed=7):
+    g = torch.Generator().manual_seed(seed)
+    return torch.rand(B, n, d, generator=g), torch.rand(B, m, d, generator=g)
+
+
+def _points_worker(rank, world, port, out, shape, reg, T):
+    import datetime
+
+    import torch.distributed as dist
+
+    from dot_b200 import ops
+    from dot_b200.distributed import release_communicators, shard_range, sinkhorn_points_rowshard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        B, n, m, d = shape
+        x, y = _clouds(B, n, m, d)
+        lo, hi = shard_range(n, rank, world)
+        res = sinkhorn_points_rowshard(x[:, lo:hi].cuda(), y.cuda(), reg, T, n_total=n, want_plan=True)
+        P_ref, cost_ref, _, v_ref, _ = ops.sinkhorn_points_forward_raw(x.cuda(), y.cuda(), 1.0, reg, T)
+        torch.cuda.synchronize()
+        dP = (res["P"] - P_ref[:, lo:hi]).abs().amax().item() / P_ref.abs().amax().item()
+        dv = (res["v"] - v_ref).abs().amax().item()
+        dc = ((res["cost"] - cost_ref).abs() / cost_ref.abs()).amax().item()
+        out[rank] = (dP, dv, dc)
+        dist.barrier()
+    finally:
+        release_communicators()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("shape,reg,T", [((2, 1030, 2000, 3), 0.05, 30), ((1, 1200, 32768, 3), 0.01, 20)],
+                         ids=["2x1030x2000", "cfg5-regime"])
+def test_points_rowshard_two_gpus_matches_single_gpu(shape, reg, T):
+    """The row-sharded point-cloud solver on 2 GPUs against the single-GPU
+    point-cloud solver on the whole problem (plan rows, v, cost)."""
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_points_worker, args=(world, _free_port(), out, shape, reg, T), nprocs=world, join=True,
+                       start_method="spawn")
+    assert len(out) == world
+    for rank, (dP, dv, dc) in out.items():
+        assert dP < 1e-5, (rank, dP)
+        assert dv < 1e-4, (rank, dv)
+        assert dc < 1e-5, (rank, dc)
+
+
+@pytest.mark.parametrize("shape,reg", [((3, 700, 900, 2), 0.05), ((1, 300, 32768, 3), 0.01), ((2, 5, 64, 4), 0.1)],
+                         ids=["3x700x900", "32768-cube", "tiny"])
+def test_points_rowshard_one_rank_matches_forward(shape, reg):
+    """Without a process group the point-cloud row-shard solver runs the
+    whole problem as one shard: half-steps, column pairs, rank merge of one
+    part; it matches the single-GPU point-cloud forward within rounding (the
+    column merge takes two levels, chunks then ranks)."""
+    from dot_b200 import ops
+    from dot_b200.distributed import sinkhorn_points_rowshard
+
+    B, n, m, d = shape
+    T = 20
+    x, y = _clouds(B, n, m, d)
+    res = sinkhorn_points_rowshard(x.cuda(), y.cuda(), reg, T, n_total=n, want_plan=True)
+    P_ref, cost_ref, u_ref, v_ref, _ = ops.sinkhorn_points_forward_raw(x.cuda(), y.cuda(), 1.0, reg, T)
+    torch.cuda.synchronize()
+    dP = (res["P"] - P_ref).abs().amax().item() / P_ref.abs().amax().item()
+    dv = (res["v"] - v_ref).abs().amax().item()
+    dc = ((res["cost"] - cost_ref).abs() / cost_ref.abs()).amax().item()
+    assert dP < 1e-5, dP
+    assert dv < 1e-4, dv
+    assert dc < 1e-5, dc
