@@ -69,3 +69,21 @@ def test_points_abi_checks_and_workspace():
         assert rc == -1, bad
     assert lib.dot_sq_dist(None, None, 1, 2, 2, 0, 1.0, None, None) == -1
     assert lib.dot_sq_dist(None, None, 0, 2, 2, 3, 1.0, None, None) == 0
+
+
+def test_points_rowshard_abi_checks():
+    lib = _lib.load()
+    # workspace: the gather buffer for every rank plus the shard's records and partials
+    one = lib.dot_sinkhorn_points_fwd_rowshard_workspace_bytes(1, 4096, 32768, 3, 1)
+    eight = lib.dot_sinkhorn_points_fwd_rowshard_workspace_bytes(1, 4096, 32768, 3, 8)
+    assert eight - one >= 7 * 32768 * 8
+    assert lib.dot_sinkhorn_points_fwd_rowshard_workspace_bytes(1, 4096, 32768, 5, 1) == 0
+    assert lib.dot_sinkhorn_points_fwd_rowshard_workspace_bytes(1, 0, 64, 3, 2) > 0   # a shard without rows
+
+    def call(d=3, tau=0.1, iters=5, n=4, n_total=8, scale=1.0):
+        return lib.dot_sinkhorn_points_fwd_rowshard(None, None, None, None, 1, n, 4, d, n_total, scale, tau, iters,
+                                                    None, None, None, None, None, None, None, 0, None)
+
+    assert call(d=5) == -4            # DOT_ERR_UNSUPPORTED
+    for bad in (dict(d=0), dict(tau=0.0), dict(iters=-1), dict(n_total=3), dict(scale=float("nan"))):
+        assert call(**bad) == -1, bad
