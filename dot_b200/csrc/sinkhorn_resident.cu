@@ -135,7 +135,9 @@ __device__ __forceinline__ bool load_tile(float* tile, const float* src, int64_t
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
-template <typename C>
+// FULL: every row slot holds rows (n % ROWS_PER_SLOT == 0) and the lanes'
+// columns are the row (m == CW), so the sweep needs no row or column checks.
+template <typename C, bool FULL>
 __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
     constexpr int LPR = C::LPR, VPL = C::VPL, W = C::W, G = C::G, NC = C::NC;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -178,12 +180,12 @@ __global__ void __launch_bounds__(C::T, C::MINB) skr_fwd_kernel(SkFwdArgs a) {
         float A = kNegBig;
         for (int sl = 0; sl < nslots; ++sl) {
             const int64_t i = int64_t(sl) * C::ROWS_PER_SLOT + wid * G + grp;
-            const bool rok = i < n;
+            const bool rok = FULL || i < n;
             float2 t[NC / 2];
 #pragma unroll
             for (int p = 0; p < VPL; ++p) {
                 const int col = colof(p);
-                if (rok && col < m) {
+                if (FULL || (rok && col < m)) {
                     const float4 k4 = *reinterpret_cast<const float4*>(S.tile + i * m + col);
                     t[2 * p] = add2(make_float2(k4.x, k4.y), vr[2 * p]);
                     t[2 * p + 1] = add2(make_float2(k4.z, k4.w), vr[2 * p + 1]);
@@ -533,9 +535,14 @@ RKind pick(int64_t n, int64_t m) {
 template <typename C>
 int launch_fwd(const SkFwdArgs& a, cudaStream_t st) {
     const size_t sm = RSmem<C>::bytes(a.n, a.m);
-    cudaFuncSetAttribute(skr_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     ProfScope ps(DOT_K_SK_RESIDENT, st);
-    skr_fwd_kernel<C><<<unsigned(a.B), C::T, sm, st>>>(a);
+    if (a.n % C::ROWS_PER_SLOT == 0 && a.m == C::CW) {
+        cudaFuncSetAttribute(skr_fwd_kernel<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+        skr_fwd_kernel<C, true><<<unsigned(a.B), C::T, sm, st>>>(a);
+    } else {
+        cudaFuncSetAttribute(skr_fwd_kernel<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+        skr_fwd_kernel<C, false><<<unsigned(a.B), C::T, sm, st>>>(a);
+    }
     return check_launch("sinkhorn forward (resident)");
 }
 

@@ -195,3 +195,14 @@ def test_points_cfg5_full_size_cost_only():
     # potentials are O(1/reg) = O(100) in magnitude; rounding differences of
     # the two kernel configurations stay at the fp32 level of that scale
     assert (u1 - u2).abs().max().item() <= 1e-3 and (v1 - v2).abs().max().item() <= 1e-3
+
+
+def test_points_batch_beyond_grid_limit():
+    """More problems than one launch's grid.z holds (65535): the half-steps
+    run in batch slices."""
+    B, n, m, d = 70000, 6, 10, 2
+    x, y = cube(B, n, d, 1300), cube(B, m, d, 1301)
+    P, cost, _, _, _ = ops.sinkhorn_points_forward_raw(x.to(DEV), y.to(DEV), 1.0, 0.2, 10)
+    ref = O.sinkhorn_points_api(x.numpy(), y.numpy(), 0.2, 10, with_grad=False)
+    U.assert_normwise(P, ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_rel(cost, ref["cost"], U.COST_RTOL, "cost")
