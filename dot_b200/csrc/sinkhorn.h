@@ -60,7 +60,9 @@ struct FusedPlan {
 };
 bool sk_fused_shape_ok(int64_t B, int64_t n, int64_t m);
 bool sk_fused_supported(int64_t B, int64_t n, int64_t m, const void* data);
-FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m);
+// fwd: the plan of the forward iterations (their full-width kernel holds
+// fewer CTAs per SM than the adjoint's)
+FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m, bool fwd = false);
 // first: launched without programmatic dependency (the previous stream work
 // writes what the kernel reads before its dependency wait); last: plain
 // copies (earlier iterations copy with L2 evict_first).

@@ -221,7 +221,7 @@ __device__ __forceinline__ float exact_column(const float* X, const float* u2, f
 }
 
 template <int VPL, bool FULL, int S>
-__global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fwd_iter_kernel(FwdIter a) {
+__global__ void __launch_bounds__(kFT, (FULL || VPL >= 8 || S >= 3) ? 2 : 3) skf_fwd_iter_kernel(FwdIter a) {
     using Cfg = FCfg<VPL>;
     constexpr int R = Cfg::R, RPW = Cfg::RPW, NC = Cfg::NC;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -355,7 +355,69 @@ __global__ void __launch_bounds__(kFT, (VPL >= 8 ? 2 : (S >= 3 ? 2 : 3))) skf_fw
 #pragma unroll
             for (int k = 0; k < NC / 2; ++k) cS[k] = fma2(t[k], w, cS[k]);
         };
+        // all of the warp's rows of a full block at once: the RPW rows' chains
+        // (loads, maxima, exponentials, sums and their warp reductions)
+        // interleave; the column updates then follow in row order, as in do_row
+        auto do_rows = [&]() {
+            float2 t[RPW][NC / 2];
+            const float2 k2 = splat2(a.kinv), l2 = splat2(kLog2e);
+#pragma unroll
+            for (int q = 0; q < RPW; ++q) {
+                const int i = wid + kFW * q;
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    const float4 x = *reinterpret_cast<const float4*>(xs + i * int(m) + 4 * lane + 128 * p);
+                    t[q][2 * p] = add2(mul2(make_float2(x.x, x.y), k2), vr[2 * p]);
+                    t[q][2 * p + 1] = add2(mul2(make_float2(x.z, x.w), k2), vr[2 * p + 1]);
+                }
+            }
+            float mx[RPW], cr[RPW], sl[RPW];
+#pragma unroll
+            for (int q = 0; q < RPW; ++q) mx[q] = max_of(t[q]);
+#pragma unroll
+            for (int q = 0; q < RPW; ++q) mx[q] = warp_max<32>(mx[q]);
+#pragma unroll
+            for (int q = 0; q < RPW; ++q) {
+                const float mxc = fmaxf(mx[q], -1.0e37f);
+                const float mL = mxc * kLog2e;
+                cr[q] = fmaf(mxc, kLog2e, -mL);
+                const float2 nm = splat2(-mL);
+#pragma unroll
+                for (int k = 0; k < NC / 2; ++k) {
+                    const float2 e = fma2(t[q][k], l2, nm);
+                    t[q][k] = make_float2(ex2(e.x), ex2(e.y));
+                }
+                const float2 s2 = tree_sum2(t[q]);
+                sl[q] = s2.x + s2.y;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+                for (int q = 0; q < RPW; ++q) sl[q] += __shfl_xor_sync(0xffffffffu, sl[q], off);
+            }
+#pragma unroll
+            for (int q = 0; q < RPW; ++q) {
+                const int64_t grow = grow0 + wid + kFW * q;
+                const float unew = lar[q] - (mx[q] + (fast_log(fmaxf(sl[q], kSumFloor)) - cr[q] * kLn2));
+                if (lane == 0) {
+                    if (tolmode) dmax = fmaxf(dmax, fabsf(unew - __ldcg(a.u2 + grow)));
+                    a.u2[grow] = unew;
+                }
+                const float ai = mx[q] + unew;
+                if (ai > A + kRaise) {            // warp-uniform
+                    const float2 sc = splat2(exp_shift(A - ai));
+#pragma unroll
+                    for (int k = 0; k < NC / 2; ++k) cS[k] = mul2(cS[k], sc);
+                    A = ai;
+                }
+                const float2 w = splat2(ex2(fmaf(ai - A, kLog2e, -cr[q])));   // exp(ai - A) / 2^cr
+#pragma unroll
+                for (int k = 0; k < NC / 2; ++k) cS[k] = fma2(t[q][k], w, cS[k]);
+            }
+        };
         if (!ok) {
+        } else if (FULL && rj == R) {
+            do_rows();
         } else if (rj == R) {
 #pragma unroll
             for (int q = 0; q < RPW; ++q) do_row(q);
@@ -802,15 +864,15 @@ void ensure_attrs() {
     if (dev >= 0 && dev < kMaxDev) done[dev] = true;
 }
 
-template <int S>
+template <int S, bool FULL>
 int per_sm_for(int vpl) {
     const int sm = S * kTileFloats * int(sizeof(float));
     int nb = 0;
     switch (vpl) {
-        case 1: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<1, false, S>, kFT, sm); break;
-        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<2, false, S>, kFT, sm); break;
-        case 4: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<4, false, S>, kFT, sm); break;
-        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<8, false, S>, kFT, sm); break;
+        case 1: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<1, FULL, S>, kFT, sm); break;
+        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<2, FULL, S>, kFT, sm); break;
+        case 4: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<4, FULL, S>, kFT, sm); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, skf_fwd_iter_kernel<8, FULL, S>, kFT, sm); break;
     }
     return nb > 0 ? nb : 1;
 }
@@ -882,12 +944,14 @@ bool sk_fused_supported(int64_t B, int64_t n, int64_t m, const void* data) {
     return sk_fused_shape_ok(B, n, m) && (reinterpret_cast<uintptr_t>(data) & 15u) == 0;
 }
 
-FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m) {
+FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m, bool fwd) {
     FusedPlan p;
     ensure_attrs();
     const int R = rows_per_block(m);
     p.stages = kStages;
-    const int per_sm = p.stages == 3 ? per_sm_for<3>(vpl_for(m)) : per_sm_for<2>(vpl_for(m));
+    const bool full = fwd && m == 128 * vpl_for(m);   // the forward's full-width kernel holds fewer CTAs
+    const int per_sm = full ? (p.stages == 3 ? per_sm_for<3, true>(vpl_for(m)) : per_sm_for<2, true>(vpl_for(m)))
+                            : (p.stages == 3 ? per_sm_for<3, false>(vpl_for(m)) : per_sm_for<2, false>(vpl_for(m)));
     p.nblk = (n + R - 1) / R;
     p.total_blocks = B * p.nblk;
     const int64_t slots = int64_t(sm_count()) * per_sm;

@@ -586,7 +586,7 @@ static SkFwdWs carve_fwd(Carve& c, int64_t B, int64_t n, int64_t m, int n_iters,
                          bool want_cost) {
     SkFwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
-    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m).nseg : 1;
+    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m, true).nseg : 1;
     const int64_t parts = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
     w.part = parts > 0 ? c.take<float2>(size_t(B * parts * m)) : nullptr;
     w.delta = tol > 0.0f ? c.take<float>(size_t(n_iters > 0 ? n_iters : 1)) : nullptr;
@@ -622,7 +622,7 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     const bool fused = sk_fused_supported(a.B, a.n, a.m, a.X);
     FusedPlan plan;
     if (fused) {
-        plan = sk_fused_plan(a.B, a.n, a.m);
+        plan = sk_fused_plan(a.B, a.n, a.m, true);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
     }
     const bool wide = !fused && a.tol == 0.0f && w.wide != nullptr && sk_wide_supported(a.B, a.n, a.m, a.X);
