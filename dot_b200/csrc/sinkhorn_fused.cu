@@ -833,6 +833,9 @@ int sm_count() {
 // Pipeline depth: 2 stages (3 CTAs per SM); 3 stages (2 CTAs per SM)
 // measured 64 vs 60 us per cfg2 forward iteration.
 constexpr int kStages = 2;
+// The forward's full-width kernel runs 2 CTAs per SM (registers), which
+// leaves room for a third stage of the ring.
+constexpr int kStagesFullFwd = 3;
 
 template <int VPL, bool FULL, int S>
 void set_attr_one() {
@@ -948,8 +951,8 @@ FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m, bool fwd) {
     FusedPlan p;
     ensure_attrs();
     const int R = rows_per_block(m);
-    p.stages = kStages;
     const bool full = fwd && m == 128 * vpl_for(m);   // the forward's full-width kernel holds fewer CTAs
+    p.stages = full ? kStagesFullFwd : kStages;
     const int per_sm = full ? (p.stages == 3 ? per_sm_for<3, true>(vpl_for(m)) : per_sm_for<2, true>(vpl_for(m)))
                             : (p.stages == 3 ? per_sm_for<3, false>(vpl_for(m)) : per_sm_for<2, false>(vpl_for(m)));
     p.nblk = (n + R - 1) / R;
