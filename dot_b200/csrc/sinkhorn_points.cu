@@ -367,8 +367,8 @@ void launch_plan(const float* x, const float* y, float scale, float kinv, const 
 bool points_fused(int64_t d, float tol) { return tol == 0.0f && d >= 1 && d <= 4; }
 
 // Chunks of side b for a half-step over na points of side a: enough CTAs for
-// about two full waves of 16 resident CTAs per SM on 148 SMs, chunks of at
-// least 256 points, a multiple of kHU points each.
+// about two full waves of 16 resident CTAs per SM, chunks of at least 256
+// points, a multiple of kHU points each.
 struct HalfPlan {
     int nchunk;
     int64_t ch;
@@ -377,9 +377,23 @@ struct HalfPlan {
 constexpr int kRL = 4;
 constexpr int kNP = 4;
 
+int sm_count_cached() {
+    static int cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 148;
+    }
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return n;
+}
+
 HalfPlan half_plan(int64_t B, int64_t na, int64_t nb) {
     const int64_t base = ceil_div(na, kHRows * kRL) * B;
-    int64_t chunks = ceil_div(int64_t(2 * 148 * 16), base);
+    int64_t chunks = ceil_div(int64_t(2 * 16) * sm_count_cached(), base);
     chunks = std::max<int64_t>(1, std::min<int64_t>(chunks, ceil_div(nb, 256)));
     HalfPlan hp;
     hp.ch = ceil_div(ceil_div(nb, chunks), kHU) * kHU;
