@@ -544,6 +544,251 @@ __global__ void __launch_bounds__(kFT, (FULL || VPL >= 8 || S >= 3) ? 2 : 3) skf
 }
 
 // ---------------------------------------------------------------------------
+// forward iteration for mid-width rows (1024 < m <= 8192)
+// ---------------------------------------------------------------------------
+// A row is too wide for one warp's registers, so the whole CTA shares every
+// row: thread t owns columns 4t + 1024p (p < VPL) of every row (its v and
+// column partials stay in registers), a block holds R = 8 / VPL rows, and
+// each row's max and sum are reduced over the CTA with one barrier each,
+// for all R rows of the block at once.  The stage is free after the first
+// barrier, so its refill is issued there and overlaps the rest of the block.
+// The arithmetic per element and the column partials against a CTA-wide
+// reference A are those of skf_fwd_iter_kernel (row values are the same in
+// every thread here, so A needs no warp agreement); a thread owns its
+// columns for the whole CTA, so a segment's partials are published without
+// an intra-CTA merge.
+constexpr int kMidFix = 1024;   // exactly recomputed columns per merge (cap)
+// A block holds 8 / VPL rows (at most 8192 floats, one stage): its rows are
+// held in registers at once (32 floats per thread), beside v and the
+// partials.
+
+// VS: v in shared memory (after the S stages) instead of registers, for the
+// widest rows (VPL 8), where t, v and the partials would not all fit.
+template <int VPL, int S, bool VS>
+__global__ void __launch_bounds__(kFT, 2) skm_fwd_iter_kernel(FwdIter a) {
+    constexpr int NC = 4 * VPL;
+    constexpr int RMAX = 8 / VPL;   // rows per block (rows_mid): RMAX * NC = 32 floats of t per thread
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[S];
+    __shared__ float s_pm[RMAX][kFW];   // per-warp row maxima
+    __shared__ float s_ps[RMAX][kFW];   // per-warp row sums
+    __shared__ float s_dmax;
+    __shared__ int s_flag, s_nfix;
+    __shared__ int s_fix[kMidFix];
+
+    pdl_launch_dependents();
+    const FusedCommon& c = a.c;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int64_t m = c.m, n = c.n;
+    const int R = c.R;
+    Ring<S> rg = ring_init<S>(c, bars, smem);
+    const bool tolmode = a.delta != nullptr;
+    if (!tolmode) ring_prime(rg);   // the matrix is read-only across launches
+    pdl_wait();
+    if (tolmode) {   // device-side early stop (as skf_fwd_iter_kernel)
+        if (*reinterpret_cast<volatile int32_t*>(a.status + 2) != 0) return;
+        if (a.iter > 0 && __ldcg(a.delta + a.iter - 1) < a.tol) {
+            if (blockIdx.x == 0 && tid == 0) {
+                a.status[0] = a.iter;
+                a.status[1] = 1;
+                a.status[2] = 1;
+            }
+            return;
+        }
+        ring_prime(rg);
+    }
+    if (tid == 0) {
+        s_nfix = 0;
+        s_dmax = 0.0f;
+    }
+
+    auto live = [&](int p) -> bool { return (4 * tid + 1024 * p) < m; };
+    constexpr int NV = VS ? 1 : NC / 2;
+    float2 vr[NV], cS[NC / 2];
+    float* s_v = reinterpret_cast<float*>(smem + size_t(S) * kTileFloats * sizeof(float));   // VS: [m]
+    // v of column pair h of this thread's float4 p
+    auto vpair = [&](int p, int h) -> float2 {
+        if constexpr (VS) {
+            return *reinterpret_cast<const float2*>(s_v + 4 * tid + 1024 * p + 2 * h);
+        } else {
+            return vr[2 * p + h];
+        }
+    };
+    float A = kNegBig;   // CTA-wide column reference
+    int cur = -1;
+
+    int b = rg.g0 / c.s.nblk, jb = rg.g0 - b * c.s.nblk;
+    for (int g = rg.g0; g < rg.g1; ++g) {
+        if (b != cur) {   // first block of a problem in this range (the barrier below orders s_v)
+            cur = b;
+            if constexpr (VS) {
+                for (int64_t q = tid; q < (m >> 2); q += kFT)
+                    reinterpret_cast<float4*>(s_v)[q] = __ldcg(reinterpret_cast<const float4*>(a.v2 + b * m) + q);
+            } else {
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    const int64_t col = 4 * tid + 1024 * p;
+                    const float4 v4 = live(p) ? __ldcg(reinterpret_cast<const float4*>(a.v2 + b * m + col))
+                                              : make_float4(0, 0, 0, 0);
+                    vr[2 * p] = make_float2(v4.x, v4.y);
+                    vr[2 * p + 1] = make_float2(v4.z, v4.w);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < NC / 2; ++k) cS[k] = make_float2(0.0f, 0.0f);
+            A = kNegBig;
+        }
+        const int rj = int(min(int64_t(R), n - int64_t(jb) * R));
+        const int64_t grow0 = int64_t(b) * n + int64_t(jb) * R;
+        const bool ok = rg.wait(g, c.err);
+        if (!__syncthreads_and(ok)) {
+            ring_drain(rg, g, c.err);
+            return;
+        }
+        const float* xs = rg.buf(g);
+        float2 t[RMAX][NC / 2];
+        const float2 k2 = splat2(a.kinv), l2 = splat2(kLog2e);
+        // t = K + v and the thread's maxima (ptxas contracts the packed
+        // multiply and add into one FMA, as in skf_fwd_iter_kernel)
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r < rj) {
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    if (live(p)) {
+                        const float4 x = *reinterpret_cast<const float4*>(xs + r * int(m) + 4 * tid + 1024 * p);
+                        t[r][2 * p] = add2(mul2(make_float2(x.x, x.y), k2), vpair(p, 0));
+                        t[r][2 * p + 1] = add2(mul2(make_float2(x.z, x.w), k2), vpair(p, 1));
+                    } else {
+                        t[r][2 * p] = t[r][2 * p + 1] = make_float2(-INFINITY, -INFINITY);
+                    }
+                }
+                const float pm = warp_max<32>(max_of(t[r]));
+                if (lane == 0) s_pm[r][wid] = pm;
+            }
+        }
+        __syncthreads();   // row maxima complete; every thread is done with the stage
+        if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
+        float mx[RMAX], cr[RMAX];
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r < rj) {
+                float mm = s_pm[r][0];
+#pragma unroll
+                for (int w = 1; w < kFW; ++w) mm = fmaxf(mm, s_pm[r][w]);
+                mx[r] = mm;
+                const float mxc = fmaxf(mm, -1.0e37f);
+                const float mL = mxc * kLog2e;
+                cr[r] = fmaf(mxc, kLog2e, -mL);
+                const float2 nm = splat2(-mL);
+#pragma unroll
+                for (int k = 0; k < NC / 2; ++k) {
+                    const float2 e = fma2(t[r][k], l2, nm);
+                    t[r][k] = make_float2(ex2(e.x), ex2(e.y));
+                }
+                const float2 s2 = tree_sum2(t[r]);
+                const float ps = warp_sum<32>(s2.x + s2.y);
+                if (lane == 0) s_ps[r][wid] = ps;
+            }
+        }
+        __syncthreads();   // row sums complete
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r < rj) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kFW; ++w) ss += s_ps[r][w];
+                const int64_t grow = grow0 + r;
+                const float la = a.la != nullptr ? __ldg(a.la + grow) : a.la_def;
+                const float unew = la - (mx[r] + (fast_log(fmaxf(ss, kSumFloor)) - cr[r] * kLn2));
+                if (tid == 0) {
+                    if (tolmode) s_dmax = fmaxf(s_dmax, fabsf(unew - __ldcg(a.u2 + grow)));
+                    a.u2[grow] = unew;
+                }
+                const float ai = mx[r] + unew;   // the same in every thread
+                if (ai > A + kRaise) {
+                    const float2 sc = splat2(exp_shift(A - ai));
+#pragma unroll
+                    for (int k = 0; k < NC / 2; ++k) cS[k] = mul2(cS[k], sc);
+                    A = ai;
+                }
+                const float2 w = splat2(ex2(fmaf(ai - A, kLog2e, -cr[r])));   // exp(ai - A) / 2^cr
+#pragma unroll
+                for (int k = 0; k < NC / 2; ++k) cS[k] = fma2(t[r][k], w, cS[k]);
+            }
+        }
+
+        if (g + 1 == rg.g1 || jb + 1 == c.s.nblk) {
+            // ---- end of this CTA's part of problem b: publish its column partials ----
+            const int kfirst = sched_owner(c.s, b * c.s.nblk);
+            const int nseg = sched_owner(c.s, (b + 1) * c.s.nblk - 1) - kfirst + 1;
+            const int seg = int(blockIdx.x) - kfirst;
+            auto finish = [&](int64_t col, float mm, float ss) {
+                const float l = a.lb ? a.lb[b * m + col] : a.lb_def;
+                if (ss < kTinySum) {
+                    const int k = atomicAdd(&s_nfix, 1);
+                    if (k < kMidFix) s_fix[k] = int(col);
+                    else a.v2[b * m + col] = l - lse_finish(mm, ss);
+                } else {
+                    a.v2[b * m + col] = l - lse_finish(mm, ss);
+                }
+            };
+            float2* mypart = a.part + (b * c.s.maxseg + seg) * m;
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                if (live(p)) {
+                    const int64_t col = 4 * tid + 1024 * p;
+                    const float2 v0 = vpair(p, 0), v1 = vpair(p, 1);
+                    const float2 q[4] = {make_float2(A - v0.x, cS[2 * p].x), make_float2(A - v0.y, cS[2 * p].y),
+                                         make_float2(A - v1.x, cS[2 * p + 1].x),
+                                         make_float2(A - v1.y, cS[2 * p + 1].y)};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (nseg == 1) finish(col + e, q[e].x, q[e].y);
+                        else mypart[col + e] = q[e];
+                    }
+                }
+            }
+            bool merged = nseg == 1;
+            if (nseg > 1 && arrive_last(c.cnt, b, nseg, &s_flag)) {
+                merged = true;
+                for (int64_t col = tid; col < m; col += kFT) {
+                    float mm = kNegBig, ss = 0.0f;
+                    for (int sg = 0; sg < nseg; ++sg) {
+                        const float2 pp = __ldcg(a.part + (b * c.s.maxseg + sg) * m + col);
+                        lse_merge(mm, ss, pp.x, pp.y);
+                    }
+                    finish(col, mm, ss);
+                }
+                if (tid == 0) c.cnt[b] = 0;
+            }
+            if (merged) {
+                if (nseg == 1) __threadfence();   // this CTA's u rows are read back by exact_column
+                __syncthreads();
+                const int nfix = min(s_nfix, kMidFix);
+                for (int k = wid; k < nfix; k += kFW) {
+                    const int64_t col = s_fix[k];
+                    const float lse = exact_column(c.data, a.u2, a.kinv, b, n, m, col);
+                    if (lane == 0) a.v2[b * m + col] = (a.lb ? a.lb[b * m + col] : a.lb_def) - lse;
+                }
+                __syncthreads();
+                if (tid == 0) s_nfix = 0;
+            }
+            __syncthreads();
+        }
+        if (++jb == c.s.nblk) {
+            jb = 0;
+            ++b;
+        }
+    }
+
+    if (tolmode) {
+        __syncthreads();
+        if (tid == 0) atomic_max_nonneg(a.delta + a.iter, s_dmax);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // backward (adjoint) iteration
 // ---------------------------------------------------------------------------
 template <int VPL, bool FULL, int S>
@@ -856,6 +1101,22 @@ void set_attrs_s() {
     set_attr_one<8, true, S>();
 }
 
+// Mid-width rows, 2 CTAs per SM (registers: all of a block's rows are held
+// at once): 3 stages, or 2 stages and v in shared memory for VPL 8.
+int vpl_mid(int64_t m) { return m <= 2048 ? 2 : m <= 4096 ? 4 : 8; }
+int rows_mid(int64_t m) { return 8 / vpl_mid(m); }
+constexpr size_t kMidSmem3 = size_t(3) * kTileFloats * sizeof(float);
+constexpr size_t kMidSmem8 = size_t(2) * kTileFloats * sizeof(float) + 8192 * sizeof(float);
+#define SKM2 skm_fwd_iter_kernel<2, 3, false>
+#define SKM4 skm_fwd_iter_kernel<4, 3, false>
+#define SKM8 skm_fwd_iter_kernel<8, 2, true>
+
+void set_attrs_mid() {
+    cudaFuncSetAttribute(SKM2, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem3));
+    cudaFuncSetAttribute(SKM4, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem3));
+    cudaFuncSetAttribute(SKM8, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem8));
+}
+
 void ensure_attrs() {
     constexpr int kMaxDev = 64;
     static bool done[kMaxDev] = {};
@@ -864,6 +1125,7 @@ void ensure_attrs() {
     if (dev >= 0 && dev < kMaxDev && done[dev]) return;
     set_attrs_s<2>();
     set_attrs_s<3>();
+    set_attrs_mid();
     if (dev >= 0 && dev < kMaxDev) done[dev] = true;
 }
 
@@ -881,11 +1143,11 @@ int per_sm_for(int vpl) {
 }
 
 template <typename Args, typename K>
-void launch(K kernel, const Args& a, int G, int S, bool pdl, cudaStream_t st) {
+void launch(K kernel, const Args& a, int G, int S, bool pdl, cudaStream_t st, size_t smem_bytes = 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(G));
     cfg.blockDim = dim3(kFT);
-    cfg.dynamicSmemBytes = size_t(S) * kTileFloats * sizeof(float);
+    cfg.dynamicSmemBytes = smem_bytes ? smem_bytes : size_t(S) * kTileFloats * sizeof(float);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -968,6 +1230,76 @@ FusedPlan sk_fused_plan(int64_t B, int64_t n, int64_t m, bool fwd) {
     p.maxseg = maxseg;
     p.nseg = maxseg;
     return p;
+}
+
+bool sk_mid_shape_ok(int64_t B, int64_t n, int64_t m) {
+    if (B < 1 || n < 1 || m <= 1024 || m > 8192 || (m % 4) != 0) return false;
+    const int64_t R = rows_mid(m);
+    return B * ((n + R - 1) / R) < (int64_t(1) << 31);   // block indices are 32-bit
+}
+
+bool sk_mid_supported(int64_t B, int64_t n, int64_t m, const void* data) {
+    return sk_mid_shape_ok(B, n, m) && (reinterpret_cast<uintptr_t>(data) & 15u) == 0;
+}
+
+FusedPlan sk_mid_plan(int64_t B, int64_t n, int64_t m) {
+    FusedPlan p;
+    ensure_attrs();
+    const int R = rows_mid(m);
+    p.stages = vpl_mid(m) == 8 ? 2 : 3;
+    int nb = 0;
+    switch (vpl_mid(m)) {
+        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, SKM2, kFT, kMidSmem3); break;
+        case 4: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, SKM4, kFT, kMidSmem3); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, SKM8, kFT, kMidSmem8); break;
+    }
+    if (nb < 1) {
+        cudaGetLastError();
+        nb = 1;
+    }
+    p.nblk = (n + R - 1) / R;
+    p.total_blocks = B * p.nblk;
+    p.G = int(std::min<int64_t>(p.total_blocks, int64_t(sm_count()) * nb));
+    Sched s = sched_of(p);
+    int maxseg = 1;
+    for (int b = 0; b < int(B); ++b) {
+        const int k0 = sched_owner(s, b * s.nblk), k1 = sched_owner(s, (b + 1) * s.nblk - 1);
+        maxseg = std::max(maxseg, k1 - k0 + 1);
+    }
+    p.maxseg = maxseg;
+    p.nseg = maxseg;
+    return p;
+}
+
+int sk_mid_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta, int iter,
+                    bool first, bool last, cudaStream_t st) {
+    FwdIter f{};
+    f.c.data = a.X;
+    f.c.n = a.n;
+    f.c.m = a.m;
+    f.c.R = rows_mid(a.m);
+    f.c.s = sched_of(p);
+    f.c.s.hint = last ? 0 : 1;
+    f.c.cnt = cnt;
+    f.c.err = a.status + 3;
+    f.kinv = a.kinv;
+    f.la = a.la;
+    f.la_def = a.la_def;
+    f.lb = a.lb;
+    f.lb_def = a.lb_def;
+    f.u2 = a.u2;
+    f.v2 = a.v2;
+    f.part = part;
+    f.delta = delta;
+    f.status = a.status;
+    f.tol = a.tol;
+    f.iter = iter;
+    switch (vpl_mid(a.m)) {
+        case 2: launch(SKM2, f, p.G, 3, !first, st); break;
+        case 4: launch(SKM4, f, p.G, 3, !first, st); break;
+        default: launch(SKM8, f, p.G, 2, !first, st, kMidSmem8); break;
+    }
+    return DOT_OK;
 }
 
 int sk_fused_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta,

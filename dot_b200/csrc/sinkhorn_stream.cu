@@ -586,7 +586,8 @@ static SkFwdWs carve_fwd(Carve& c, int64_t B, int64_t n, int64_t m, int n_iters,
                          bool want_cost) {
     SkFwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
-    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m, true).nseg : 1;
+    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m, true).nseg
+                         : sk_mid_shape_ok(B, n, m) ? sk_mid_plan(B, n, m).nseg : 1;
     const int64_t parts = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
     w.part = parts > 0 ? c.take<float2>(size_t(B * parts * m)) : nullptr;
     w.delta = tol > 0.0f ? c.take<float>(size_t(n_iters > 0 ? n_iters : 1)) : nullptr;
@@ -619,13 +620,17 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     if (w.delta) cudaMemsetAsync(w.delta, 0, sizeof(float) * size_t(a.n_iters > 0 ? a.n_iters : 1), st);
 
     SkCtl ctl{w.delta, a.status, a.tol, 0};
-    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.X);
+    // the single-pass kernels read v (and write u) in 16-byte vectors
+    const bool pots16 = ((reinterpret_cast<uintptr_t>(a.v2) | reinterpret_cast<uintptr_t>(a.u2)) & 15u) == 0;
+    const bool fused = pots16 && sk_fused_supported(a.B, a.n, a.m, a.X);
+    const bool mid = pots16 && !fused && sk_mid_supported(a.B, a.n, a.m, a.X);
     FusedPlan plan;
-    if (fused) {
-        plan = sk_fused_plan(a.B, a.n, a.m, true);
+    if (fused || mid) {
+        plan = fused ? sk_fused_plan(a.B, a.n, a.m, true) : sk_mid_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
     }
-    const bool wide = !fused && a.tol == 0.0f && w.wide != nullptr && sk_wide_supported(a.B, a.n, a.m, a.X);
+    const bool wide =
+        pots16 && !fused && !mid && a.tol == 0.0f && w.wide != nullptr && sk_wide_supported(a.B, a.n, a.m, a.X);
     if (wide) {
         int rc = sk_wide_fwd(a, w.wide, st);
         if (rc != DOT_OK) return rc;
@@ -638,15 +643,16 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
         cudaMemcpyAsync(a.v_hist + int64_t(it) * a.B * a.m, a.v2, sizeof(float) * size_t(a.B * a.m),
                         cudaMemcpyDeviceToDevice, st);
     };
-    if (fused && a.n_iters > 0) {
+    if ((fused || mid) && a.n_iters > 0) {
         ProfScope ps(DOT_K_SK_FWD_ITER, st, a.n_iters);
         for (int it = 0; it < a.n_iters; ++it) {
             // a copy between two iterations ends the programmatic dependency chain
-            sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, it == 0 || hist, it == a.n_iters - 1, st);
+            if (fused) sk_fused_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, it == 0 || hist, it == a.n_iters - 1, st);
+            else sk_mid_fwd_iter(a, plan, w.part, w.cnt, w.delta, it, it == 0 || hist, it == a.n_iters - 1, st);
             record(it);
         }
     }
-    for (int it = 0; it < (fused || wide ? 0 : a.n_iters); ++it) {
+    for (int it = 0; it < (fused || mid || wide ? 0 : a.n_iters); ++it) {
         if (it > 0) record(it - 1);
         ctl.iter = it;
         {
@@ -668,7 +674,7 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
                                                             chunks, ctl, nullptr);
         }
     }
-    if (!fused && !wide && a.n_iters > 0) record(a.n_iters - 1);
+    if (!fused && !mid && !wide && a.n_iters > 0) record(a.n_iters - 1);
     {
         ProfScope ps(DOT_K_SK_FWD_EPI, st);
         sk_status_kernel<<<1, 32, 0, st>>>(w.delta, a.status, a.n_iters, a.tol);
