@@ -81,9 +81,11 @@ int sk_fused_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv
 // and partial buffers are as for sk_fused_*.
 bool sk_mid_shape_ok(int64_t B, int64_t n, int64_t m);
 bool sk_mid_supported(int64_t B, int64_t n, int64_t m, const void* data);
-FusedPlan sk_mid_plan(int64_t B, int64_t n, int64_t m);
+FusedPlan sk_mid_plan(int64_t B, int64_t n, int64_t m, bool fwd);
 int sk_mid_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_t* cnt, float* delta, int iter,
                     bool first, bool last, cudaStream_t st);
+int sk_mid_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv, const float2* cinv, float* lam,
+                    float* mu, float* part, int32_t* cnt, int32_t* err, bool first, bool last, cudaStream_t st);
 
 size_t sk_stream_fwd_ws(int64_t B, int64_t n, int64_t m, int n_iters, float tol, bool want_cost);
 int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st);

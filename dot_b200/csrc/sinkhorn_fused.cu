@@ -788,6 +788,152 @@ __global__ void __launch_bounds__(kFT, 2) skm_fwd_iter_kernel(FwdIter a) {
     }
 }
 
+// Adjoint sweep for mid-width rows (1024 < m <= 8192), laid out as
+// skm_fwd_iter_kernel: thread t owns columns 4t + 1024p, a block holds
+// 8 / VPL rows, each row's dot product with mu is reduced over the CTA with
+// one barrier for the block's rows together (the stage is refilled there),
+// then lambda_i and the column sums sum_i P_ik lambda_i in registers; the
+// arithmetic is skf_bwd_iter_kernel's.  VS: mu in shared memory.
+template <int VPL, int S, bool VS>
+__global__ void __launch_bounds__(kFT, 2) skm_bwd_iter_kernel(BwdIter a) {
+    constexpr int NC = 4 * VPL;
+    constexpr int RMAX = 8 / VPL;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[S];
+    __shared__ float s_pd[RMAX][kFW];   // per-warp row dot products
+    __shared__ int s_flag;
+
+    pdl_launch_dependents();
+    const FusedCommon& c = a.c;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int64_t m = c.m, n = c.n;
+    Ring<S> rg = ring_init<S>(c, bars, smem);
+    ring_prime(rg);   // the plan is read-only across launches
+    pdl_wait();
+
+    auto live = [&](int p) -> bool { return (4 * tid + 1024 * p) < m; };
+    constexpr int NM = VS ? 1 : NC;
+    float mr[NM], acc[NC];
+    float* s_mu = reinterpret_cast<float*>(smem + size_t(S) * kTileFloats * sizeof(float));   // VS: [m]
+    auto mu4 = [&](int p) -> float4 {
+        if constexpr (VS) {
+            return *reinterpret_cast<const float4*>(s_mu + 4 * tid + 1024 * p);
+        } else {
+            return make_float4(mr[4 * p], mr[4 * p + 1], mr[4 * p + 2], mr[4 * p + 3]);
+        }
+    };
+    int cur = -1;
+
+    int b = rg.g0 / c.s.nblk, jb = rg.g0 - b * c.s.nblk;
+    for (int g = rg.g0; g < rg.g1; ++g) {
+        if (b != cur) {   // the barrier below orders the s_mu writes before their reads
+            cur = b;
+            if constexpr (VS) {
+                for (int64_t q = tid; q < (m >> 2); q += kFT)
+                    reinterpret_cast<float4*>(s_mu)[q] = __ldcg(reinterpret_cast<const float4*>(a.mu + b * m) + q);
+            } else {
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    const int64_t col = 4 * tid + 1024 * p;
+                    const float4 u4 = live(p) ? __ldcg(reinterpret_cast<const float4*>(a.mu + b * m + col))
+                                              : make_float4(0, 0, 0, 0);
+                    mr[4 * p + 0] = u4.x;
+                    mr[4 * p + 1] = u4.y;
+                    mr[4 * p + 2] = u4.z;
+                    mr[4 * p + 3] = u4.w;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < NC; ++e) acc[e] = 0.0f;
+        }
+        const int rj = int(min(int64_t(RMAX), n - int64_t(jb) * RMAX));
+        const int64_t grow0 = int64_t(b) * n + int64_t(jb) * RMAX;
+        float2 ri[RMAX];   // row invariants, loaded before waiting on the block
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) ri[r] = r < rj ? __ldg(a.rinv + grow0 + r) : make_float2(0.0f, 1.0f);
+        const bool ok = rg.wait(g, c.err);
+        if (!__syncthreads_and(ok)) {
+            ring_drain(rg, g, c.err);
+            return;
+        }
+        const float* ps = rg.buf(g);
+        float pv[RMAX][NC];
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r < rj) {
+                float sd = 0.0f;
+#pragma unroll
+                for (int p = 0; p < VPL; ++p) {
+                    if (live(p)) {
+                        const float4 x = *reinterpret_cast<const float4*>(ps + r * int(m) + 4 * tid + 1024 * p);
+                        const float4 u = mu4(p);
+                        pv[r][4 * p + 0] = x.x;
+                        pv[r][4 * p + 1] = x.y;
+                        pv[r][4 * p + 2] = x.z;
+                        pv[r][4 * p + 3] = x.w;
+                        sd += x.x * u.x + x.y * u.y + x.z * u.z + x.w * u.w;
+                    } else {
+                        pv[r][4 * p + 0] = pv[r][4 * p + 1] = pv[r][4 * p + 2] = pv[r][4 * p + 3] = 0.0f;
+                    }
+                }
+                sd = warp_sum<32>(sd);
+                if (lane == 0) s_pd[r][wid] = sd;
+            }
+        }
+        __syncthreads();   // row dots complete; every thread is done with the stage
+        if (tid == 0 && g + S < rg.g1) rg.issue(g + S);
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r < rj) {
+                float sd = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kFW; ++w) sd += s_pd[r][w];
+                const float l = (ri[r].x - sd) / fmaxf(ri[r].y, kSumFloor);
+                if (tid == 0) a.lam[grow0 + r] = l;
+#pragma unroll
+                for (int e = 0; e < NC; ++e) acc[e] += pv[r][e] * l;
+            }
+        }
+        __syncthreads();   // s_pd is read before the next block writes it
+
+        if (g + 1 == rg.g1 || jb + 1 == c.s.nblk) {
+            const int kfirst = sched_owner(c.s, b * c.s.nblk);
+            const int nseg = sched_owner(c.s, (b + 1) * c.s.nblk - 1) - kfirst + 1;
+            const int seg = int(blockIdx.x) - kfirst;
+            float* mypart = a.part + (b * c.s.maxseg + seg) * m;
+#pragma unroll
+            for (int p = 0; p < VPL; ++p) {
+                if (live(p)) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int64_t col = 4 * tid + 1024 * p + e;
+                        if (nseg == 1) {
+                            const float2 ci = a.cinv[b * m + col];
+                            a.mu[b * m + col] = (ci.x - acc[4 * p + e]) / fmaxf(ci.y, kSumFloor);
+                        } else {
+                            mypart[col] = acc[4 * p + e];
+                        }
+                    }
+                }
+            }
+            if (nseg > 1 && arrive_last(c.cnt, b, nseg, &s_flag)) {
+                for (int64_t col = tid; col < m; col += kFT) {
+                    float sum = 0.0f;
+                    for (int sg = 0; sg < nseg; ++sg) sum += __ldcg(a.part + (b * c.s.maxseg + sg) * m + col);
+                    const float2 ci = a.cinv[b * m + col];
+                    a.mu[b * m + col] = (ci.x - sum) / fmaxf(ci.y, kSumFloor);
+                }
+                if (tid == 0) c.cnt[b] = 0;
+            }
+            __syncthreads();
+        }
+        if (++jb == c.s.nblk) {
+            jb = 0;
+            ++b;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // backward (adjoint) iteration
 // ---------------------------------------------------------------------------
@@ -1110,11 +1256,17 @@ constexpr size_t kMidSmem8 = size_t(2) * kTileFloats * sizeof(float) + 8192 * si
 #define SKM2 skm_fwd_iter_kernel<2, 3, false>
 #define SKM4 skm_fwd_iter_kernel<4, 3, false>
 #define SKM8 skm_fwd_iter_kernel<8, 2, true>
+#define SKMB2 skm_bwd_iter_kernel<2, 3, false>
+#define SKMB4 skm_bwd_iter_kernel<4, 3, false>
+#define SKMB8 skm_bwd_iter_kernel<8, 2, true>
 
 void set_attrs_mid() {
     cudaFuncSetAttribute(SKM2, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem3));
     cudaFuncSetAttribute(SKM4, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem3));
     cudaFuncSetAttribute(SKM8, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem8));
+    cudaFuncSetAttribute(SKMB2, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem3));
+    cudaFuncSetAttribute(SKMB4, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem3));
+    cudaFuncSetAttribute(SKMB8, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmem8));
 }
 
 void ensure_attrs() {
@@ -1242,17 +1394,18 @@ bool sk_mid_supported(int64_t B, int64_t n, int64_t m, const void* data) {
     return sk_mid_shape_ok(B, n, m) && (reinterpret_cast<uintptr_t>(data) & 15u) == 0;
 }
 
-FusedPlan sk_mid_plan(int64_t B, int64_t n, int64_t m) {
+FusedPlan sk_mid_plan(int64_t B, int64_t n, int64_t m, bool fwd) {
     FusedPlan p;
     ensure_attrs();
     const int R = rows_mid(m);
     p.stages = vpl_mid(m) == 8 ? 2 : 3;
     int nb = 0;
-    switch (vpl_mid(m)) {
-        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, SKM2, kFT, kMidSmem3); break;
-        case 4: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, SKM4, kFT, kMidSmem3); break;
-        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, SKM8, kFT, kMidSmem8); break;
-    }
+    const int v = vpl_mid(m);
+    const size_t sm = v == 8 ? kMidSmem8 : kMidSmem3;
+    cudaError_t e;
+    if (fwd) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, v == 2 ? SKM2 : v == 4 ? SKM4 : SKM8, kFT, sm);
+    else e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, v == 2 ? SKMB2 : v == 4 ? SKMB4 : SKMB8, kFT, sm);
+    if (e != cudaSuccess) nb = 0;
     if (nb < 1) {
         cudaGetLastError();
         nb = 1;
@@ -1298,6 +1451,30 @@ int sk_mid_fwd_iter(const SkFwdArgs& a, const FusedPlan& p, float2* part, int32_
         case 2: launch(SKM2, f, p.G, 3, !first, st); break;
         case 4: launch(SKM4, f, p.G, 3, !first, st); break;
         default: launch(SKM8, f, p.G, 2, !first, st, kMidSmem8); break;
+    }
+    return DOT_OK;
+}
+
+int sk_mid_bwd_iter(const SkBwdArgs& a, const FusedPlan& p, const float2* rinv, const float2* cinv, float* lam,
+                    float* mu, float* part, int32_t* cnt, int32_t* err, bool first, bool last, cudaStream_t st) {
+    BwdIter f{};
+    f.c.data = a.P;
+    f.c.n = a.n;
+    f.c.m = a.m;
+    f.c.R = rows_mid(a.m);
+    f.c.s = sched_of(p);
+    f.c.s.hint = last ? 0 : 1;
+    f.c.cnt = cnt;
+    f.c.err = err;
+    f.rinv = rinv;
+    f.cinv = cinv;
+    f.lam = lam;
+    f.mu = mu;
+    f.part = part;
+    switch (vpl_mid(a.m)) {
+        case 2: launch(SKMB2, f, p.G, 3, !first, st); break;
+        case 4: launch(SKMB4, f, p.G, 3, !first, st); break;
+        default: launch(SKMB8, f, p.G, 2, !first, st, kMidSmem8); break;
     }
     return DOT_OK;
 }

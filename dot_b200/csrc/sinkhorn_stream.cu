@@ -587,7 +587,7 @@ static SkFwdWs carve_fwd(Carve& c, int64_t B, int64_t n, int64_t m, int n_iters,
     SkFwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
     const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m, true).nseg
-                         : sk_mid_shape_ok(B, n, m) ? sk_mid_plan(B, n, m).nseg : 1;
+                         : sk_mid_shape_ok(B, n, m) ? sk_mid_plan(B, n, m, true).nseg : 1;
     const int64_t parts = std::max(chunks > 1 ? chunks : int64_t(0), fseg > 1 ? fseg : int64_t(0));
     w.part = parts > 0 ? c.take<float2>(size_t(B * parts * m)) : nullptr;
     w.delta = tol > 0.0f ? c.take<float>(size_t(n_iters > 0 ? n_iters : 1)) : nullptr;
@@ -626,7 +626,7 @@ int sk_stream_fwd(const SkFwdArgs& a, void* ws, cudaStream_t st) {
     const bool mid = pots16 && !fused && sk_mid_supported(a.B, a.n, a.m, a.X);
     FusedPlan plan;
     if (fused || mid) {
-        plan = fused ? sk_fused_plan(a.B, a.n, a.m, true) : sk_mid_plan(a.B, a.n, a.m);
+        plan = fused ? sk_fused_plan(a.B, a.n, a.m, true) : sk_mid_plan(a.B, a.n, a.m, true);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B), st);
     }
     const bool wide =
@@ -705,7 +705,8 @@ struct SkBwdWs {
 static SkBwdWs carve_bwd(Carve& c, int64_t B, int64_t n, int64_t m) {
     SkBwdWs w{};
     const int64_t chunks = ceil_div(n, col_rows_per_chunk(n));
-    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m).nseg : 1;
+    const int64_t fseg = sk_fused_shape_ok(B, n, m) ? sk_fused_plan(B, n, m).nseg
+                         : sk_mid_shape_ok(B, n, m) ? sk_mid_plan(B, n, m, false).nseg : 1;
     w.rinv = c.take<float2>(size_t(B * n));
     w.cinv = c.take<float2>(size_t(B * m));
     w.lam = c.take<float>(size_t(B * n));
@@ -739,9 +740,16 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
 
     cudaMemsetAsync(w.mu, 0, sizeof(float) * size_t(a.B * a.m), st);
     cudaMemsetAsync(w.lam, 0, sizeof(float) * size_t(rows), st);
-    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.P) && aligned16_host(a.X) &&
-                       (a.gP == nullptr || aligned16_host(a.gP));
+    const bool vec16 = aligned16_host(a.X) && (a.gP == nullptr || aligned16_host(a.gP));
+    const bool fused = sk_fused_supported(a.B, a.n, a.m, a.P) && vec16;
+    // mid-width rows: single-pass adjoint sweeps; the invariants below come
+    // from the two-sweep set-up (once per call)
+    const bool mid = !fused && vec16 && sk_mid_supported(a.B, a.n, a.m, a.P);
     FusedPlan plan;
+    if (mid) {
+        plan = sk_mid_plan(a.B, a.n, a.m, false);
+        cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B + 1), st);
+    }
     if (fused) {
         plan = sk_fused_plan(a.B, a.n, a.m);
         cudaMemsetAsync(w.cnt, 0, sizeof(int32_t) * size_t(a.B + 1), st);
@@ -766,13 +774,18 @@ int sk_stream_bwd(const SkBwdArgs& a, void* ws, cudaStream_t st) {
             skb_col_prep_merge_kernel<<<merge_grid, 256, 0, st>>>(w.part2, w.cinv, a.B, a.m, chunks);
         }
     }
-    if (fused && a.bwd_iters > 0) {
+    if ((fused || mid) && a.bwd_iters > 0) {
         ProfScope ps(DOT_K_SK_BWD_ITER, st, a.bwd_iters);
-        for (int it = 0; it < a.bwd_iters; ++it)
-            sk_fused_bwd_iter(a, plan, w.rinv, w.cinv, w.lam, w.mu, w.part1, w.cnt, w.cnt + a.B, it == 0,
-                              it == a.bwd_iters - 1, st);
+        for (int it = 0; it < a.bwd_iters; ++it) {
+            if (fused)
+                sk_fused_bwd_iter(a, plan, w.rinv, w.cinv, w.lam, w.mu, w.part1, w.cnt, w.cnt + a.B, it == 0,
+                                  it == a.bwd_iters - 1, st);
+            else
+                sk_mid_bwd_iter(a, plan, w.rinv, w.cinv, w.lam, w.mu, w.part1, w.cnt, w.cnt + a.B, it == 0,
+                                it == a.bwd_iters - 1, st);
+        }
     }
-    for (int it = 0; it < (fused ? 0 : a.bwd_iters); ++it) {
+    for (int it = 0; it < (fused || mid ? 0 : a.bwd_iters); ++it) {
         {
             ProfScope ps(DOT_K_SK_BWD_ITER, st);
             skb_row_iter_kernel<<<row_grid, kRowThreads, 0, st>>>(a.P, w.rinv, w.mu, w.lam, rows, a.n, a.m);

@@ -814,3 +814,30 @@ def test_mid_width_fwd_bwd_and_tol():
     res = dot.sinkhorn(Cg, reg=0.1, n_iters=200, tol=1e-4)
     u, v, n_used, conv = O.sinkhorn_dual(-C.numpy(), 0.1, 200, tol=1e-4)
     assert abs(res.n_iters_used - n_used) <= 1 and res.converged == bool(conv)
+
+
+@pytest.mark.parametrize("B,n,m,reg,T", [(2, 300, 1100, 0.1, 15), (1, 200, 4096, 0.05, 20), (2, 129, 6000, 0.1, 12)],
+                         ids=["1100", "4096", "6000"])
+def test_mid_width_implicit_backward_matches_oracle(B, n, m, reg, T):
+    """The adjoint sweeps of mid-width rows (single pass, the CTA sharing
+    each row) for a loss on both the plan and the cost."""
+    from dot_b200 import _lib
+
+    g = U.gen(15000 + m)
+    C = torch.rand(B, n, m, generator=g)
+    W = torch.randn(B, n, m, generator=g)
+    cw = torch.randn(B, generator=g)
+    ref = O.sinkhorn_api(C.numpy(), reg, T, g_cost=cw.numpy(), grad_P=W.numpy(), bwd_tol=0.0)
+    _lib.prof_begin(time_events=False)
+    r = run_api(C, reg, T, cost_weight=cw, plan_weight=W, reg_tensor=True)
+    torch.cuda.synchronize()
+    prof = _lib.prof_end()
+    assert prof["sk_fwd_iter"]["launches"] == T and prof["sk_bwd_iter"]["launches"] == T, prof
+    U.assert_normwise(r["P"], ref["P"], U.PLAN_RTOL, "plan")
+    U.assert_normwise(r["dC"], ref["dC"], U.GRAD_RTOL, "dC")
+    Cn = C.numpy()
+    G = cw.numpy()[:, None, None].astype(np.float64) * Cn + W.numpy()
+    _, gtau64 = O.sinkhorn_implicit_fp64(-Cn, O.sinkhorn_dual_fp64(-Cn, reg, T), G, reg, T)
+    dreg64 = float(gtau64.sum())
+    own = abs(float(ref["dreg"]) - dreg64)
+    assert abs(r["dreg"] - float(ref["dreg"])) <= own + U.GRAD_RTOL * abs(dreg64) + 1e-6
