@@ -660,7 +660,9 @@ def run_ours(args, cfg: dict) -> None:
     if world == 1 and not args.no_configs and cfg["name"] == "cfg2":
         confs = {}
         for name in SECONDARY:
-            confs[name] = measure_config(name, 3, 3, rank, world, dev, args.cpu_seconds / 2,
+            # configs[0] is a ~0.3 ms step dominated by launch overhead: more steps steady it
+            steps_c = 20 if name == "cfg1" else 3
+            confs[name] = measure_config(name, steps_c, 3, rank, world, dev, args.cpu_seconds / 2,
                                          with_cpu=not args.no_cpu_baseline)
         pts = measure_points_cfg5(dev)
         if line is not None:
