@@ -964,6 +964,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=None, help="override the config's iteration count (profiling)")
     ap.add_argument("--rows", type=int, default=None, help="override the config's row count n (profiling)")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch size B (profiling)")
+    ap.add_argument("--cols", type=int, default=None, help="override the config's row length m (profiling)")
     ap.add_argument("--points", action="store_true",
                     help="configs[4] from its two point clouds through dot_b200.sinkhorn_points (1 GPU)")
     args = ap.parse_args()
@@ -978,6 +979,9 @@ def main() -> None:
     if args.batch is not None:
         cfg["B"] = args.batch
         cfg["desc"] += f" (run with batch {args.batch})"
+    if args.cols is not None:
+        cfg["m"] = args.cols
+        cfg["desc"] += f" (run with {args.cols} columns)"
     if args.impl == "reference":
         run_reference(args, cfg)
     elif args.points:

@@ -27,7 +27,7 @@ from typing import Optional
 import torch
 
 from . import ops
-from .sinkhorn import SinkhornResult, _check_cuda, _prepare_marginal, _tau_value
+from .sinkhorn import SinkhornResult, _check_cuda, _prepare_marginals, _tau_value
 
 
 class _SinkhornPointsFn(torch.autograd.Function):
@@ -115,8 +115,7 @@ def sinkhorn_points(
         raise ValueError("x and y must be (B, n, d) and (B, m, d)")
     B, n, _ = xb.shape
     m = yb.size(1)
-    a = _prepare_marginal(a, B, n, "a", xb.device, torch.float32)
-    b = _prepare_marginal(b, B, m, "b", xb.device, torch.float32)
+    a, b = _prepare_marginals([(a, B, n, "a"), (b, B, m, "b")], xb.device, torch.float32)
     log_a = torch.log(a) if a is not None else None
     log_b = torch.log(b) if b is not None else None
     tau = _tau_value(reg)

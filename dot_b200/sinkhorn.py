@@ -149,19 +149,45 @@ class _SinkhornUnrolledFn(torch.autograd.Function):
 
 def _prepare_marginal(marginal, batch: int, size: int, name: str, device, dtype):
     """Validate a marginal and broadcast it to [batch, size] (``dot/sinkhorn.py:1259-1281``)."""
-    if marginal is None:
-        return None
-    if marginal.dim() == 1:
-        marginal = marginal.unsqueeze(0).expand(batch, -1)
-    if marginal.shape != (batch, size):
-        raise ValueError(f"{name} must have shape ({batch}, {size}) or ({size},)")
-    if torch.any(marginal <= 0):
-        raise ValueError(f"{name} must be strictly positive")
-    marginal = marginal.to(device=device, dtype=dtype)
-    sums = marginal.sum(dim=-1)
-    if not torch.allclose(sums, torch.ones_like(sums), atol=1e-4, rtol=1e-4):
-        raise ValueError(f"{name} must sum to 1 along the last dimension")
-    return marginal
+    return _prepare_marginals([(marginal, batch, size, name)], device, dtype)[0]
+
+
+def _prepare_marginals(specs, device, dtype):
+    """``_prepare_marginal`` for several marginals ``(marginal, batch, size,
+    name)`` with one host synchronisation: the reference's checks (shape,
+    strictly positive, rows summing to 1 within atol = rtol = 1e-4, in that
+    order per marginal, marginals in the order given) evaluated on the device
+    and read back together.  Same results and errors as checking each in turn."""
+    out, flags, names = [], [], []
+
+    def raise_pending():   # the value errors of the marginals checked so far, in order
+        if not flags:
+            return
+        for name, (nonpos, offsum) in zip(names, torch.stack(flags).tolist()):
+            if nonpos:
+                raise ValueError(f"{name} must be strictly positive")
+            if offsum:
+                raise ValueError(f"{name} must sum to 1 along the last dimension")
+
+    for marginal, batch, size, name in specs:
+        if marginal is None:
+            out.append(None)
+            continue
+        if marginal.dim() == 1:
+            marginal = marginal.unsqueeze(0).expand(batch, -1)
+        if marginal.shape != (batch, size):
+            raise_pending()
+            raise ValueError(f"{name} must have shape ({batch}, {size}) or ({size},)")
+        nonpos = (marginal <= 0).any().to(device)
+        marginal = marginal.to(device=device, dtype=dtype)
+        sums = marginal.sum(dim=-1)
+        # torch.allclose(sums, 1, atol=1e-4, rtol=1e-4): |sums - 1| <= 1e-4 + 1e-4 * 1 (NaN fails)
+        offsum = ~((sums - 1).abs() <= 2e-4).all()
+        flags.append(torch.stack([nonpos, offsum]))
+        names.append(name)
+        out.append(marginal)
+    raise_pending()
+    return out
 
 
 def _resolve_iters(n_iters, max_iter):
@@ -248,8 +274,7 @@ def sinkhorn(
     if C.dim() != 3:
         raise ValueError("cost_matrix must be (B, n, m) or (n, m)")
     B, n, m = C.shape
-    a = _prepare_marginal(a, B, n, "a", C.device, C.dtype)
-    b = _prepare_marginal(b, B, m, "b", C.device, C.dtype)
+    a, b = _prepare_marginals([(a, B, n, "a"), (b, B, m, "b")], C.device, C.dtype)
     log_a = torch.log(a) if a is not None else None
     log_b = torch.log(b) if b is not None else None
     tau = _tau_value(reg)
@@ -309,8 +334,7 @@ def sinkhorn_from_scores(
     unbatched = log_alpha.dim() == 2
     L = log_alpha.unsqueeze(0) if unbatched else log_alpha
     B, n, m = L.shape
-    a = _prepare_marginal(a, B, n, "a", L.device, L.dtype)
-    b = _prepare_marginal(b, B, m, "b", L.device, L.dtype)
+    a, b = _prepare_marginals([(a, B, n, "a"), (b, B, m, "b")], L.device, L.dtype)
     log_a = torch.log(a) if a is not None else None
     log_b = torch.log(b) if b is not None else None
     if backward_iters is None:

@@ -90,3 +90,28 @@ def test_unrolled_op_rejects_cpu_tensors():
         dot._ops.sinkhorn_with_grads_unrolled(torch.rand(1, 4, 4), torch.rand(1, 4, 4), 1.0, 5)
     with pytest.raises(RuntimeError, match="CUDA"):
         dot.sinkhorn(torch.rand(1, 4, 4), reg=0.5, n_iters=5, backward_mode="unrolled")
+
+
+def test_prepare_marginals_error_order():
+    """Both marginals validated with one read-back, errors in the reference's
+    order (a's checks before b's, shape before values per marginal)."""
+    import pytest
+    import torch
+
+    from dot_b200.sinkhorn import _prepare_marginals
+
+    good = torch.full((2, 3), 1 / 3)
+    bad_sum = torch.full((2, 3), 0.5)
+    neg = torch.tensor([[0.5, 0.6, -0.1]] * 2)
+    dev, dt = torch.device("cpu"), torch.float32
+    a, b = _prepare_marginals([(good, 2, 3, "a"), (good[:, :2] * 1.5, 2, 2, "b")], dev, dt)
+    assert a.shape == (2, 3) and b.shape == (2, 2)
+    with pytest.raises(ValueError, match="a must sum to 1"):
+        _prepare_marginals([(bad_sum, 2, 3, "a"), (torch.ones(5), 2, 4, "b")], dev, dt)   # a before b's shape
+    with pytest.raises(ValueError, match="b must have shape"):
+        _prepare_marginals([(good, 2, 3, "a"), (torch.ones(5), 2, 4, "b")], dev, dt)
+    with pytest.raises(ValueError, match="a must be strictly positive"):
+        _prepare_marginals([(neg, 2, 3, "a"), (neg, 2, 3, "b")], dev, dt)
+    with pytest.raises(ValueError, match="b must be strictly positive"):
+        _prepare_marginals([(good, 2, 3, "a"), (neg, 2, 3, "b")], dev, dt)
+    assert _prepare_marginals([(None, 2, 3, "a"), (None, 2, 3, "b")], dev, dt) == [None, None]
