@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(kFT, 2) skm_fwd_iter_kernel(FwdIter a) {
 
     auto live = [&](int p) -> bool { return (4 * tid + 1024 * p) < m; };
     constexpr int NV = VS ? 1 : NC / 2;
-    float2 vr[NV], cS[NC / 2];
+    float2 vr[NV] = {}, cS[NC / 2];   // vr is loaded at each problem's first block, before any use
     float* s_v = reinterpret_cast<float*>(smem + size_t(S) * kTileFloats * sizeof(float));   // VS: [m]
     // v of column pair h of this thread's float4 p
     auto vpair = [&](int p, int h) -> float2 {
@@ -813,7 +813,7 @@ __global__ void __launch_bounds__(kFT, 2) skm_bwd_iter_kernel(BwdIter a) {
 
     auto live = [&](int p) -> bool { return (4 * tid + 1024 * p) < m; };
     constexpr int NM = VS ? 1 : NC;
-    float mr[NM], acc[NC];
+    float mr[NM] = {}, acc[NC];   // mr is loaded at each problem's first block, before any use
     float* s_mu = reinterpret_cast<float*>(smem + size_t(S) * kTileFloats * sizeof(float));   // VS: [m]
     auto mu4 = [&](int p) -> float4 {
         if constexpr (VS) {
