@@ -28,10 +28,10 @@
 //           of sum grad * sim / T for the temperature gradient.
 // The statistics are (max, 1/sum); every sweep recomputes its values from
 // sim.  The output and dot sweeps need only row * col, which they take from
-// one exponential, exp(2v - rmax - cmax), with the same expression, so the dot
-// sweep sees the forward's out bit for bit; the gradient sweep needs row and
-// col apart and forms row * col from them (within a few ulp of the other
-// form).  Each sweep reads its inputs once (the output sweeps re-read sim:
+// one exponential, exp(2v - rmax - cmax), with the same expression; the
+// gradient sweep needs row and col apart and forms row * col from them
+// (within a few ulp of the other form).  Element pairs go through the packed
+// f32x2 instructions (half the issue slots of scalar FP32 code).  Each sweep reads its inputs once (the output sweeps re-read sim:
 // 1.5x / 1.67x the compulsory bytes of the two directions) and runs at
 // streaming bandwidth instead of holding whole problems in flight.  The
 // second sweep of a direction is a programmatic dependent launch: it sets up
@@ -44,6 +44,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "pack.cuh"
 #include "tma.cuh"
 
 namespace dotb {
@@ -67,6 +68,7 @@ struct WL {
     static constexpr int WPR = VPL >= 8 ? 2 : 1;
     static constexpr int VPLW = VPL / WPR;
     static constexpr int NC = 4 * VPLW;
+    static constexpr int NP = NC / 2;   // value pairs per lane
     static constexpr int SLOTS = kW / WPR;
 };
 
@@ -98,14 +100,15 @@ __device__ __forceinline__ void st4g(__nv_bfloat16* p, const float (&v)[4]) {
     x.y = *reinterpret_cast<const uint32_t*>(&b);
     __stcs(reinterpret_cast<uint2*>(p), x);
 }
-// four consecutive column statistics (16-byte aligned)
-__device__ __forceinline__ void ld_cs4(const float2* p, float2 (&c)[4]) {
+// four consecutive column statistics (16-byte aligned) as pairs: first
+// components (c0, c1), (c2, c3) in f, second components in g
+__device__ __forceinline__ void cs4_pairs(const float2* p, float2 (&f)[2], float2 (&g)[2]) {
     const float4 a = *reinterpret_cast<const float4*>(p);
     const float4 b = *reinterpret_cast<const float4*>(p + 2);
-    c[0] = make_float2(a.x, a.y);
-    c[1] = make_float2(a.z, a.w);
-    c[2] = make_float2(b.x, b.y);
-    c[3] = make_float2(b.z, b.w);
+    f[0] = make_float2(a.x, a.z);
+    g[0] = make_float2(a.y, a.w);
+    f[1] = make_float2(b.x, b.z);
+    g[1] = make_float2(b.y, b.w);
 }
 __device__ __forceinline__ float rsqrt_approx(float x) {
     float y;
@@ -119,29 +122,16 @@ __device__ __forceinline__ void window(const int32_t* lengths, int64_t b, int64_
     l2 = min(max(int64_t(__ldg(lengths + 2 * b + 1)), int64_t(0)), L2);
 }
 
-// Per-element values from the statistics (the gradient sweep):
-//   row = exp(v - rmax) * rinv, col = exp(v - cmax) * cinv, rc = row * col,
-//   out = min(sqrt(1e-9 + rc), 1), iout = 1 / out.
-// sqrt and 1/sqrt come from one rsqrt (SFU, ~2^-22 relative).  The column
-// value's numerator exp(v - A) and its share of the column sum (accumulated
-// as E*w) can differ by an ulp, so rc may exceed 1 by rounding where one
+// Per-element values (the output, dot and gradient sweeps) come from the
+// statistics: row = exp(v - rmax) * rinv, col = exp(v - cmax) * cinv,
+// out = min(sqrt(1e-9 + row * col), 1), 1/out = max(rsqrt(1e-9 + row * col), 1).
+// sqrt and rsqrt run on the SFU (~2^-22 relative).  The column value's
+// numerator exp(v - A) and its share of the column sum (accumulated as E*w)
+// can differ by an ulp, so row * col may exceed 1 by rounding where one
 // element dominates its row and column; out is capped at 1, its
 // exact-arithmetic bound.  out >= sqrt(1e-9) > 1e-9, so the reference's guard
-// dp = 0 for out <= 1e-9 never applies.
-struct BsVals {
-    float row, col, rc, out, iout;
-};
-__device__ __forceinline__ BsVals bs_vals(float v, float2 rs, float2 cs) {
-    BsVals q;
-    q.row = exp_shift(v - rs.x) * rs.y;
-    q.col = exp_shift(v - cs.x) * cs.y;
-    q.rc = q.row * q.col;
-    const float x = 1e-9f + q.rc;
-    const float r = rsqrt_approx(x);
-    q.out = fminf(x * r, 1.0f);
-    q.iout = fmaxf(r, 1.0f);
-    return q;
-}
+// dp = 0 for out <= 1e-9 never applies.  Pairs of elements go through the
+// packed f32x2 instructions.
 
 // Exact column softmax statistics (max, 1/sum) over rows [0, l1) -- one warp.
 template <typename T>
@@ -154,6 +144,47 @@ __device__ float2 exact_col_stats(const T* sb, int64_t L2, int64_t l1, int64_t c
     for (int64_t i = lane; i < l1; i += 32) s += exp_shift(__fmul_rn(float(sb[i * L2 + col]), invT) - mx);
     s = warp_sum<32>(s);
     return make_float2(mx, s > 0.0f ? 1.0f / s : 0.0f);
+}
+
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float y;
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float2 ex2x2(float2 x) { return make_float2(ex2(x.x), ex2(x.y)); }
+
+// This lane's values of a row, scaled by 1/T (rounded), as pairs; -inf
+// outside [0, l2).  FULL: the row is l2 == L2 == 128 * VPLW * WPR columns.
+template <typename T, int VPLW, bool FULL>
+__device__ __forceinline__ void load_scaled(const T* xr, int cbase, int lane, int64_t L2, int64_t l2, float invT,
+                                            float2 (&t)[2 * VPLW]) {
+#pragma unroll
+    for (int p = 0; p < VPLW; ++p) {
+        const int col = cbase + 4 * lane + 128 * p;
+        if (FULL || col < L2) {
+            float v[4];
+            ld4s(xr + col, v);
+            t[2 * p] = mul2(make_float2(v[0], v[1]), splat2(invT));
+            t[2 * p + 1] = mul2(make_float2(v[2], v[3]), splat2(invT));
+            if (!FULL && col + 3 >= l2) {
+                if (col + 0 >= l2) t[2 * p].x = -INFINITY;
+                if (col + 1 >= l2) t[2 * p].y = -INFINITY;
+                if (col + 2 >= l2) t[2 * p + 1].x = -INFINITY;
+                t[2 * p + 1].y = -INFINITY;
+            }
+        } else {
+            t[2 * p] = t[2 * p + 1] = make_float2(-INFINITY, -INFINITY);
+        }
+    }
+}
+
+// row * col for a pair of elements from one exponential:
+// 2^((2v - rmax - cmax) log2 e) * rinv * cinv, the exponent formed as
+// fma(v, 2 log2 e, -rmL) - cmL (rmL, cmL: the maxima times log2 e, rounded;
+// nrmL = -rmL).  The output and dot sweeps use this same expression.
+__device__ __forceinline__ float2 rowcol2(float2 val, float2 nrmL, float2 rinv, float2 cmL, float2 cinv) {
+    const float2 d = sub2(fma2(val, splat2(2.0f * kLog2e), nrmL), cmL);
+    return mul2(mul2(ex2x2(d), rinv), cinv);
 }
 
 // ---------------------------------------------------------------------------
@@ -269,7 +300,7 @@ __device__ __forceinline__ void ring_drain(const Ring& r, int g) {
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
     using W = WL<VPL>;
-    constexpr int WPR = W::WPR, VPLW = W::VPLW, NC = W::NC, SLOTS = W::SLOTS;
+    constexpr int WPR = W::WPR, VPLW = W::VPLW, NP = W::NP, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
     __shared__ float2 s_rp[kMaxR][WPR];   // per-row (max, sum) of the row's warps
@@ -285,8 +316,9 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
     const Ring rg = ring_start(a, bars, smem);
     const T* simT = reinterpret_cast<const T*>(a.sim);
 
-    float Sc[NC];
+    float2 Sc[NP];   // column sums of exp(v - A), this lane's columns in pairs
     float A = kNegBig;
+    const bool wide = L2 == 128 * VPL;
     int64_t l1 = 0, l2 = 0;
     int b = rg.g0 / a.s.nblk, jb = rg.g0 - b * a.s.nblk;   // advanced per block, no division
     int cur = -1;
@@ -306,7 +338,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
 #pragma unroll
-            for (int e = 0; e < NC; ++e) Sc[e] = 0.0f;
+            for (int k = 0; k < NP; ++k) Sc[k] = make_float2(0.0f, 0.0f);
             A = kNegBig;
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
@@ -322,25 +354,10 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
                 if (lane == 0) s_rp[il][cpart] = make_float2(kNegBig, 0.0f);
                 continue;
             }
-            float t[NC];
-#pragma unroll
-            for (int p = 0; p < VPLW; ++p) {
-                const int64_t col = cbase + 4 * lane + 128 * p;
-                float v[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                if (col < L2) {
-                    ld4s(xs + il * L2 + col, v);
-                    if (col + 3 < l2) {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) v[e] = __fmul_rn(v[e], a.invT);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) v[e] = (col + e < l2) ? __fmul_rn(v[e], a.invT) : -INFINITY;
-                    }
-                }
-#pragma unroll
-                for (int e = 0; e < 4; ++e) t[4 * p + e] = v[e];
-            }
-            const float mx = warp_max<32>(tree_max(t));
+            float2 t[NP];
+            if (wide && l2 == L2) load_scaled<T, VPLW, true>(xs + il * L2, cbase, lane, L2, l2, a.invT, t);
+            else load_scaled<T, VPLW, false>(xs + il * L2, cbase, lane, L2, l2, a.invT, t);
+            const float mx = warp_max<32>(max_of(t));
             float s = 0.0f;
             if (mx != -INFINITY) {   // warp-uniform; else every column of this warp's part is masked
                 // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e rounded;
@@ -349,17 +366,18 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
                 const float mL = mx * kLog2e;
                 const float cr = fmaf(mx, kLog2e, -mL);
 #pragma unroll
-                for (int e = 0; e < NC; ++e) t[e] = ex2(fmaf(t[e], kLog2e, -mL));
-                s = warp_sum<32>(tree_sum(t)) * ex2(-cr);
+                for (int k = 0; k < NP; ++k) t[k] = ex2x2(fma2(t[k], splat2(kLog2e), splat2(-mL)));
+                const float2 s2 = tree_sum2(t);
+                s = warp_sum<32>(s2.x + s2.y) * ex2(-cr);
                 if (mx > A + kRaiseB) {
                     const float sc = exp_shift(A - mx);
 #pragma unroll
-                    for (int e = 0; e < NC; ++e) Sc[e] *= sc;
+                    for (int k = 0; k < NP; ++k) Sc[k] = mul2(Sc[k], splat2(sc));
                     A = mx;
                 }
                 const float w = ex2(fmaf(mx - A, kLog2e, -cr));   // exp(mx - A) / 2^cr
 #pragma unroll
-                for (int e = 0; e < NC; ++e) Sc[e] = fmaf(t[e], w, Sc[e]);
+                for (int k = 0; k < NP; ++k) Sc[k] = fma2(t[k], splat2(w), Sc[k]);
             }
             if (lane == 0) s_rp[il][cpart] = make_float2(mx == -INFINITY ? kNegBig : mx, s);
         }
@@ -387,7 +405,10 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
                 const int64_t col = cbase + 4 * lane + 128 * p;
                 if (col < L2) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) mb[slot * L2 + col + e] = make_float2(A, Sc[4 * p + e]);
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 pr = Sc[2 * p + (e >> 1)];
+                        mb[slot * L2 + col + e] = make_float2(A, (e & 1) ? pr.y : pr.x);
+                    }
                 }
             }
             __syncthreads();
@@ -453,6 +474,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
+    const bool wide = L2 == 128 * VPL;
     const Ring rg = ring_start(a, bars, smem, true);
     pdl_wait();   // the first sweep's statistics / dots are complete and visible
     int64_t l1 = 0, l2 = 0;
@@ -482,33 +504,32 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
             float* orow = a.out + row * L2;
             const bool live = i < l1;
             const float2 rs = live ? __ldg(a.rstat + row) : make_float2(0.0f, 0.0f);
-            const float rmL = rs.x * kLog2e;
+            const float2 nrmL = splat2(-(rs.x * kLog2e)), rinv = splat2(rs.y);
+            const bool full = wide && l2 == L2;
 #pragma unroll
             for (int p = 0; p < VPLW; ++p) {
-                const int64_t col = cbase + 4 * lane + 128 * p;
-                if (col < L2) {
-                    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if (live && col < l2) {
-                        float v[4];
-                        float2 cs[4];
-                        ld4s(xs + il * L2 + col, v);
-                        ld_cs4(s_cs + col, cs);
-                        const bool whole = col + 3 < l2;
+                const int col = cbase + 4 * lane + 128 * p;
+                if (!full && col >= L2) continue;
+                float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (live && (full || col < l2)) {
+                    float v[4];
+                    float2 cm[2], ci[2];
+                    ld4s(xs + il * L2 + col, v);
+                    cs4_pairs(s_cs + col, cm, ci);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (whole || col + e < l2) {
-                                // row * col = exp(2v - rmax - cmax) * rinv * cinv: one
-                                // exponential (the gradient sweep needs row and col
-                                // apart and keeps bs_vals)
-                                const float val = __fmul_rn(v[e], a.invT);
-                                const float rc = ex2(fmaf(val, 2.0f * kLog2e, -rmL) - cs[e].x) * rs.y * cs[e].y;
-                                const float x = 1e-9f + rc;
-                                o[e] = fminf(x * rsqrt_approx(x), 1.0f);
-                            }
-                        }
+                    for (int h = 0; h < 2; ++h) {
+                        const float2 val = mul2(make_float2(v[2 * h], v[2 * h + 1]), splat2(a.invT));
+                        const float2 x = add2(rowcol2(val, nrmL, rinv, cm[h], ci[h]), splat2(1e-9f));
+                        o[2 * h] = fminf(sqrt_approx(x.x), 1.0f);
+                        o[2 * h + 1] = fminf(sqrt_approx(x.y), 1.0f);
                     }
-                    st4g(orow + col, o);
+                    if (!full && col + 3 >= l2) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (col + e >= l2) o[e] = 0.0f;
+                    }
                 }
+                st4g(orow + col, o);
             }
         }
         __syncthreads();   // the stage is free
@@ -522,7 +543,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     using W = WL<VPL>;
-    constexpr int WPR = W::WPR, VPLW = W::VPLW, NC = W::NC, SLOTS = W::SLOTS;
+    constexpr int WPR = W::WPR, VPLW = W::VPLW, NP = W::NP, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
     __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's columns: (cmax * log2 e, 1/sum)
@@ -536,7 +557,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     pdl_launch_dependents();   // the second sweep may start its copies of the read-only input
     const Ring rg = ring_start(a, bars, smem);
 
-    float Sd[NC];
+    float2 Sd[NP];   // column sums of q, this lane's columns in pairs
+    const bool wide = L2 == 128 * VPL;
     int64_t l1 = 0, l2 = 0;
     int b = rg.g0 / a.s.nblk, jb = rg.g0 - b * a.s.nblk;
     int cur = -1;
@@ -550,7 +572,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
                 s_cs[col] = make_float2(c.x * kLog2e, c.y);
             }
 #pragma unroll
-            for (int e = 0; e < NC; ++e) Sd[e] = 0.0f;
+            for (int k = 0; k < NP; ++k) Sd[k] = make_float2(0.0f, 0.0f);
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
         const bool ok = rg.wait(g);
@@ -565,33 +587,36 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
             float rd = 0.0f;
             if (i < l1) {   // warp-uniform
                 const float2 rs = __ldg(a.rstat + int64_t(b) * L1 + i);
-                const float rmL = rs.x * kLog2e;
+                const float2 nrmL = splat2(-(rs.x * kLog2e)), rinv = splat2(rs.y);
+                const bool full = wide && l2 == L2;
+                float2 rd2 = make_float2(0.0f, 0.0f);
 #pragma unroll
                 for (int p = 0; p < VPLW; ++p) {
-                    const int64_t col = cbase + 4 * lane + 128 * p;
-                    if (col < l2) {
+                    const int col = cbase + 4 * lane + 128 * p;
+                    if (full || col < l2) {
                         float v[4], gv[4];
-                        float2 cs[4];
+                        float2 cm[2], ci[2];
                         ld4s(xs + il * L2 + col, v);
                         ld4s(gs + il * L2 + col, gv);
-                        ld_cs4(s_cs + col, cs);
-                        const bool whole = col + 3 < l2;
+                        cs4_pairs(s_cs + col, cm, ci);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (whole || col + e < l2) {
-                                // q needs row * col only: exp(2v - rmax - cmax) *
-                                // rinv * cinv, one exponential
-                                const float val = __fmul_rn(v[e], a.invT);
-                                const float rc =
-                                    ex2(fmaf(val, 2.0f * kLog2e, -rmL) - cs[e].x) * rs.y * cs[e].y;
-                                const float iout = fmaxf(rsqrt_approx(1e-9f + rc), 1.0f);
-                                const float qq = (gv[e] * 0.5f) * iout * rc;
-                                rd += qq;
-                                Sd[4 * p + e] += qq;
+                        for (int h = 0; h < 2; ++h) {
+                            // q needs row * col only: the output sweep's expression
+                            const float2 val = mul2(make_float2(v[2 * h], v[2 * h + 1]), splat2(a.invT));
+                            const float2 rc = rowcol2(val, nrmL, rinv, cm[h], ci[h]);
+                            const float2 x = add2(rc, splat2(1e-9f));
+                            const float2 iout = make_float2(fmaxf(rsqrt_approx(x.x), 1.0f), fmaxf(rsqrt_approx(x.y), 1.0f));
+                            float2 q = mul2(mul2(mul2(make_float2(gv[2 * h], gv[2 * h + 1]), splat2(0.5f)), iout), rc);
+                            if (!full && col + 3 >= l2) {
+                                if (col + 2 * h >= l2) q.x = 0.0f;
+                                if (col + 2 * h + 1 >= l2) q.y = 0.0f;
                             }
+                            rd2 = add2(rd2, q);
+                            Sd[2 * p + h] = add2(Sd[2 * p + h], q);
                         }
                     }
                 }
+                rd = rd2.x + rd2.y;
                 rd = warp_sum<32>(rd);
             }
             if (lane == 0) s_rd[il][cpart] = rd;
@@ -614,7 +639,10 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
                 const int64_t col = cbase + 4 * lane + 128 * p;
                 if (col < L2) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) mb[slot * L2 + col + e] = Sd[4 * p + e];
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 pr = Sd[2 * p + (e >> 1)];
+                        mb[slot * L2 + col + e] = (e & 1) ? pr.y : pr.x;
+                    }
                 }
             }
             __syncthreads();
@@ -662,6 +690,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
+    const bool wide = L2 == 128 * VPL;
     const Ring rg = ring_start(a, bars, smem, true);
     pdl_wait();   // the first sweep's statistics / dots are complete and visible
     int64_t l1 = 0, l2 = 0;
@@ -690,35 +719,48 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
             G* grow = gsim + row * L2;
             const bool live = i < l1;
             const float2 rs = live ? __ldg(a.rstat + row) : make_float2(0.0f, 0.0f);
-            const float rd = live ? __ldg(a.rdot + row) : 0.0f;
-            float acc = 0.0f;
+            const float2 rmax = splat2(rs.x), rinv = splat2(rs.y);
+            const float2 nrd = splat2(live ? -__ldg(a.rdot + row) : 0.0f);
+            const float2 it = splat2(a.invT), lg = splat2(kLog2e);
+            const bool full = wide && l2 == L2;
+            float2 acc2 = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int p = 0; p < VPLW; ++p) {
-                const int64_t col = cbase + 4 * lane + 128 * p;
-                if (col < L2) {
-                    float gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if (live && col < l2) {
-                        float v[4], gv[4];
-                        float2 cs[4];
-                        ld4s(xs + il * L2 + col, v);
-                        ld4s(gs + il * L2 + col, gv);
-                        ld_cs4(s_cs + col, cs);
-                        const float4 d4 = __ldg(reinterpret_cast<const float4*>(db + col));
-                        const float cd[4] = {d4.x, d4.y, d4.z, d4.w};
-                        const bool whole = col + 3 < l2;
+                const int col = cbase + 4 * lane + 128 * p;
+                if (!full && col >= L2) continue;
+                float gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (live && (full || col < l2)) {
+                    float v[4], gv[4];
+                    float2 cm[2], ci[2];
+                    ld4s(xs + il * L2 + col, v);
+                    ld4s(gs + il * L2 + col, gv);
+                    cs4_pairs(s_cs + col, cm, ci);
+                    const float4 d4 = __ldg(reinterpret_cast<const float4*>(db + col));
+                    const float2 cd[2] = {make_float2(d4.x, d4.y), make_float2(d4.z, d4.w)};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (whole || col + e < l2) {
-                                const BsVals q = bs_vals(__fmul_rn(v[e], a.invT), rs, cs[e]);
-                                const float qq = (gv[e] * 0.5f) * q.iout * q.rc;
-                                gr[e] = (2.0f * qq - rd * q.row - cd[e] * q.col) * a.invT;
-                                acc = fmaf(gr[e], v[e] * a.invT, acc);
-                            }
+                    for (int h = 0; h < 2; ++h) {
+                        // row = exp(v - rmax) rinv, col = exp(v - cmax) cinv, out from
+                        // one rsqrt of 1e-9 + row * col; 2q = g * (1/out) * row * col
+                        const float2 val = mul2(make_float2(v[2 * h], v[2 * h + 1]), it);
+                        const float2 rw = mul2(ex2x2(mul2(sub2(val, rmax), lg)), rinv);
+                        const float2 cl = mul2(ex2x2(mul2(sub2(val, cm[h]), lg)), ci[h]);
+                        const float2 rc = mul2(rw, cl);
+                        const float2 x = add2(rc, splat2(1e-9f));
+                        const float2 iout = make_float2(fmaxf(rsqrt_approx(x.x), 1.0f), fmaxf(rsqrt_approx(x.y), 1.0f));
+                        const float2 q2 = mul2(mul2(make_float2(gv[2 * h], gv[2 * h + 1]), iout), rc);
+                        float2 g2 = mul2(sub2(fma2(nrd, rw, q2), mul2(cd[h], cl)), it);
+                        if (!full && col + 3 >= l2) {
+                            if (col + 2 * h >= l2) g2.x = 0.0f;
+                            if (col + 2 * h + 1 >= l2) g2.y = 0.0f;
                         }
+                        acc2 = fma2(g2, val, acc2);
+                        gr[2 * h] = g2.x;
+                        gr[2 * h + 1] = g2.y;
                     }
-                    st4g(grow + col, gr);
                 }
+                st4g(grow + col, gr);
             }
+            float acc = acc2.x + acc2.y;
             if (a.tau_row != nullptr) {
                 acc = warp_sum<32>(acc);
                 if (lane == 0) s_tp[il][cpart] = acc;

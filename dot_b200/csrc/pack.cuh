@@ -1,4 +1,4 @@
-// Packed two-lane fp32 arithmetic for sm_100a (PTX add/mul/fma .rn.f32x2):
+// Packed two-lane fp32 arithmetic for sm_100a (PTX add/sub/mul/fma .rn.f32x2):
 // one instruction performs the same IEEE round-to-nearest operation on both
 // halves of a 64-bit register pair -- each instruction on its own is
 // bit-identical per half to the scalar __fadd_rn / __fmul_rn / fmaf (measured
@@ -30,6 +30,12 @@ __device__ __forceinline__ float2 f2_of(unsigned long long r) {
 __device__ __forceinline__ float2 add2(float2 a, float2 b) {
     unsigned long long r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_of(r);
+}
+// a - b
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
     return f2_of(r);
 }
 // a * b
