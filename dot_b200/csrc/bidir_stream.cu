@@ -100,15 +100,15 @@ __device__ __forceinline__ void st4g(__nv_bfloat16* p, const float (&v)[4]) {
     x.y = *reinterpret_cast<const uint32_t*>(&b);
     __stcs(reinterpret_cast<uint2*>(p), x);
 }
-// four consecutive column statistics (16-byte aligned) as pairs: first
-// components (c0, c1), (c2, c3) in f, second components in g
-__device__ __forceinline__ void cs4_pairs(const float2* p, float2 (&f)[2], float2 (&g)[2]) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 2);
-    f[0] = make_float2(a.x, a.z);
-    g[0] = make_float2(a.y, a.w);
-    f[1] = make_float2(b.x, b.z);
-    g[1] = make_float2(b.y, b.w);
+// four consecutive columns' statistics (shared memory, 16-byte aligned) as
+// pairs (c0, c1), (c2, c3): f from pf, g from pg
+__device__ __forceinline__ void cs4_pairs(const float* pf, const float* pg, float2 (&f)[2], float2 (&g)[2]) {
+    const float4 a = *reinterpret_cast<const float4*>(pf);
+    const float4 b = *reinterpret_cast<const float4*>(pg);
+    f[0] = make_float2(a.x, a.y);
+    f[1] = make_float2(a.z, a.w);
+    g[0] = make_float2(b.x, b.y);
+    g[1] = make_float2(b.z, b.w);
 }
 __device__ __forceinline__ float rsqrt_approx(float x) {
     float y;
@@ -124,14 +124,15 @@ __device__ __forceinline__ void window(const int32_t* lengths, int64_t b, int64_
 
 // Per-element values (the output, dot and gradient sweeps) come from the
 // statistics: row = exp(v - rmax) * rinv, col = exp(v - cmax) * cinv,
-// out = min(sqrt(1e-9 + row * col), 1), 1/out = max(rsqrt(1e-9 + row * col), 1).
+// out = min(sqrt(1e-9 + row * col), 1), 1/out = rsqrt(1e-9 + row * col).
 // sqrt and rsqrt run on the SFU (~2^-22 relative).  The column value's
 // numerator exp(v - A) and its share of the column sum (accumulated as E*w)
 // can differ by an ulp, so row * col may exceed 1 by rounding where one
 // element dominates its row and column; out is capped at 1, its
-// exact-arithmetic bound.  out >= sqrt(1e-9) > 1e-9, so the reference's guard
-// dp = 0 for out <= 1e-9 never applies.  Pairs of elements go through the
-// packed f32x2 instructions.
+// exact-arithmetic bound (1/out then differs from 1 by those few ulp).
+// out >= sqrt(1e-9) > 1e-9, so the reference's guard dp = 0 for out <= 1e-9
+// never applies.  Pairs of elements go through the packed f32x2
+// instructions.
 
 // Exact column softmax statistics (max, 1/sum) over rows [0, l1) -- one warp.
 template <typename T>
@@ -348,37 +349,77 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
             return;
         }
         const T* xs = reinterpret_cast<const T*>(rg.stage(g));
-        for (int il = slot; il < rows; il += SLOTS) {
+        const bool fullw = wide && l2 == L2;
+        // The row's exponentials, sums and column weights: a row whose warp
+        // part is all masked (max -inf) contributes nothing.  Rows enter the
+        // column sums in the order il, il + SLOTS, ...
+        // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e rounded;
+        // every term carries 2^cr, cr = mx*log2e - mL exactly (FMA remainder),
+        // taken out of the row sum and the column weight.  A row whose warp
+        // part is all masked (mx = -inf; warp-uniform) gets mL = 0: its terms
+        // are exp(-inf) = 0.
+        auto exps = [&](float2 (&t)[NP], float mx, float& cr) {
+            const float mL = mx == -INFINITY ? 0.0f : mx * kLog2e;
+            cr = mx == -INFINITY ? 0.0f : fmaf(mx, kLog2e, -mL);
+#pragma unroll
+            for (int k = 0; k < NP; ++k) t[k] = ex2x2(fma2(t[k], splat2(kLog2e), splat2(-mL)));
+        };
+        auto accumulate = [&](float2 (&t)[NP], float mx, float cr) {
+            if (mx == -INFINITY) return;
+            if (mx > A + kRaiseB) {
+                const float sc = exp_shift(A - mx);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) Sc[k] = mul2(Sc[k], splat2(sc));
+                A = mx;
+            }
+            const float w = ex2(fmaf(mx - A, kLog2e, -cr));   // exp(mx - A) / 2^cr
+#pragma unroll
+            for (int k = 0; k < NP; ++k) Sc[k] = fma2(t[k], splat2(w), Sc[k]);
+        };
+        int il = slot;
+        if (fullw) {
+            // two live full-width rows per pass: their loads, maxima and sums
+            // overlap (same results as one at a time)
+            for (; il + SLOTS < rows && int64_t(jb) * a.R + il + SLOTS < l1; il += 2 * SLOTS) {
+                float2 t0[NP], t1[NP];
+                load_scaled<T, VPLW, true>(xs + il * L2, cbase, lane, L2, l2, a.invT, t0);
+                load_scaled<T, VPLW, true>(xs + (il + SLOTS) * L2, cbase, lane, L2, l2, a.invT, t1);
+                const float m0 = warp_max<32>(max_of(t0)), m1 = warp_max<32>(max_of(t1));
+                float cr0, cr1;
+                exps(t0, m0, cr0);
+                exps(t1, m1, cr1);
+                const float2 u0 = tree_sum2(t0), u1 = tree_sum2(t1);
+                float s0 = u0.x + u0.y, s1 = u1.x + u1.y;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+                    s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+                }
+                s0 = m0 == -INFINITY ? 0.0f : s0 * ex2(-cr0);
+                s1 = m1 == -INFINITY ? 0.0f : s1 * ex2(-cr1);
+                accumulate(t0, m0, cr0);
+                accumulate(t1, m1, cr1);
+                if (lane == 0) {
+                    s_rp[il][cpart] = make_float2(m0 == -INFINITY ? kNegBig : m0, s0);
+                    s_rp[il + SLOTS][cpart] = make_float2(m1 == -INFINITY ? kNegBig : m1, s1);
+                }
+            }
+        }
+        for (; il < rows; il += SLOTS) {
             const int64_t i = int64_t(jb) * a.R + il;
             if (i >= l1 || l2 == 0) {
                 if (lane == 0) s_rp[il][cpart] = make_float2(kNegBig, 0.0f);
                 continue;
             }
             float2 t[NP];
-            if (wide && l2 == L2) load_scaled<T, VPLW, true>(xs + il * L2, cbase, lane, L2, l2, a.invT, t);
+            if (fullw) load_scaled<T, VPLW, true>(xs + il * L2, cbase, lane, L2, l2, a.invT, t);
             else load_scaled<T, VPLW, false>(xs + il * L2, cbase, lane, L2, l2, a.invT, t);
             const float mx = warp_max<32>(max_of(t));
-            float s = 0.0f;
-            if (mx != -INFINITY) {   // warp-uniform; else every column of this warp's part is masked
-                // exp(t - mx) as 2^(t*log2e - mL) in one FFMA, mL = mx*log2e rounded;
-                // every term carries 2^cr, cr = mx*log2e - mL exactly (FMA
-                // remainder), taken out of the row sum and the column weight
-                const float mL = mx * kLog2e;
-                const float cr = fmaf(mx, kLog2e, -mL);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) t[k] = ex2x2(fma2(t[k], splat2(kLog2e), splat2(-mL)));
-                const float2 s2 = tree_sum2(t);
-                s = warp_sum<32>(s2.x + s2.y) * ex2(-cr);
-                if (mx > A + kRaiseB) {
-                    const float sc = exp_shift(A - mx);
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) Sc[k] = mul2(Sc[k], splat2(sc));
-                    A = mx;
-                }
-                const float w = ex2(fmaf(mx - A, kLog2e, -cr));   // exp(mx - A) / 2^cr
-#pragma unroll
-                for (int k = 0; k < NP; ++k) Sc[k] = fma2(t[k], splat2(w), Sc[k]);
-            }
+            float cr;
+            exps(t, mx, cr);
+            const float2 u = tree_sum2(t);
+            const float s = mx == -INFINITY ? 0.0f : warp_sum<32>(u.x + u.y) * ex2(-cr);
+            accumulate(t, mx, cr);
             if (lane == 0) s_rp[il][cpart] = make_float2(mx == -INFINITY ? kNegBig : mx, s);
         }
         __syncthreads();   // the stage is free; s_rp is complete
@@ -468,7 +509,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
     constexpr int WPR = W::WPR, VPLW = W::VPLW, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's columns: (cmax * log2 e, 1/sum)
+    __shared__ __align__(16) float s_cm[kMaxL2];   // the problem's columns: cmax * log2 e
+    __shared__ __align__(16) float s_ci[kMaxL2];   // and 1/sum
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int slot = wid / WPR, cpart = wid % WPR;
@@ -488,7 +530,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
             window(a.lengths, b, L1, L2, l1, l2);
             for (int64_t col = tid; col < L2; col += kT) {
                 const float2 c = __ldg(a.cstat + int64_t(b) * L2 + col);
-                s_cs[col] = make_float2(c.x * kLog2e, c.y);
+                s_cm[col] = c.x * kLog2e;
+                s_ci[col] = c.y;
             }
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
@@ -515,7 +558,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_out_kernel(SweepArgs a) {
                     float v[4];
                     float2 cm[2], ci[2];
                     ld4s(xs + il * L2 + col, v);
-                    cs4_pairs(s_cs + col, cm, ci);
+                    cs4_pairs(s_cm + col, s_ci + col, cm, ci);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const float2 val = mul2(make_float2(v[2 * h], v[2 * h + 1]), splat2(a.invT));
@@ -546,7 +589,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     constexpr int WPR = W::WPR, VPLW = W::VPLW, NP = W::NP, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's columns: (cmax * log2 e, 1/sum)
+    __shared__ __align__(16) float s_cm[kMaxL2];   // the problem's columns: cmax * log2 e
+    __shared__ __align__(16) float s_ci[kMaxL2];   // and 1/sum
     __shared__ float s_rd[kMaxR][WPR];               // per-row q sums of the row's warps
     __shared__ int s_flag;
 
@@ -569,7 +613,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
             window(a.lengths, b, L1, L2, l1, l2);
             for (int64_t col = tid; col < L2; col += kT) {
                 const float2 c = __ldg(a.cstat + int64_t(b) * L2 + col);
-                s_cs[col] = make_float2(c.x * kLog2e, c.y);
+                s_cm[col] = c.x * kLog2e;
+                s_ci[col] = c.y;
             }
 #pragma unroll
             for (int k = 0; k < NP; ++k) Sd[k] = make_float2(0.0f, 0.0f);
@@ -598,14 +643,14 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
                         float2 cm[2], ci[2];
                         ld4s(xs + il * L2 + col, v);
                         ld4s(gs + il * L2 + col, gv);
-                        cs4_pairs(s_cs + col, cm, ci);
+                        cs4_pairs(s_cm + col, s_ci + col, cm, ci);
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             // q needs row * col only: the output sweep's expression
                             const float2 val = mul2(make_float2(v[2 * h], v[2 * h + 1]), splat2(a.invT));
                             const float2 rc = rowcol2(val, nrmL, rinv, cm[h], ci[h]);
                             const float2 x = add2(rc, splat2(1e-9f));
-                            const float2 iout = make_float2(fmaxf(rsqrt_approx(x.x), 1.0f), fmaxf(rsqrt_approx(x.y), 1.0f));
+                            const float2 iout = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
                             float2 q = mul2(mul2(mul2(make_float2(gv[2 * h], gv[2 * h + 1]), splat2(0.5f)), iout), rc);
                             if (!full && col + 3 >= l2) {
                                 if (col + 2 * h >= l2) q.x = 0.0f;
@@ -683,7 +728,8 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
     constexpr int WPR = W::WPR, VPLW = W::VPLW, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ __align__(16) float2 s_cs[kMaxL2];   // the problem's column statistics
+    __shared__ __align__(16) float s_cm[kMaxL2];   // the problem's columns: cmax
+    __shared__ __align__(16) float s_ci[kMaxL2];   // and 1/sum
     __shared__ float s_tp[kMaxR][WPR];               // per-row tau partials of the row's warps
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -702,7 +748,11 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
         if (b != cur) {   // the barrier below orders these writes before their reads
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
-            for (int64_t col = tid; col < L2; col += kT) s_cs[col] = __ldg(a.cstat + int64_t(b) * L2 + col);
+            for (int64_t col = tid; col < L2; col += kT) {
+                const float2 c = __ldg(a.cstat + int64_t(b) * L2 + col);
+                s_cm[col] = c.x;
+                s_ci[col] = c.y;
+            }
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
         const bool ok = rg.wait(pos);
@@ -734,7 +784,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
                     float2 cm[2], ci[2];
                     ld4s(xs + il * L2 + col, v);
                     ld4s(gs + il * L2 + col, gv);
-                    cs4_pairs(s_cs + col, cm, ci);
+                    cs4_pairs(s_cm + col, s_ci + col, cm, ci);
                     const float4 d4 = __ldg(reinterpret_cast<const float4*>(db + col));
                     const float2 cd[2] = {make_float2(d4.x, d4.y), make_float2(d4.z, d4.w)};
 #pragma unroll
@@ -746,7 +796,7 @@ __global__ void __launch_bounds__(kT, 3) bs2_grad_kernel(SweepArgs a, G* __restr
                         const float2 cl = mul2(ex2x2(mul2(sub2(val, cm[h]), lg)), ci[h]);
                         const float2 rc = mul2(rw, cl);
                         const float2 x = add2(rc, splat2(1e-9f));
-                        const float2 iout = make_float2(fmaxf(rsqrt_approx(x.x), 1.0f), fmaxf(rsqrt_approx(x.y), 1.0f));
+                        const float2 iout = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
                         const float2 q2 = mul2(mul2(make_float2(gv[2 * h], gv[2 * h + 1]), iout), rc);
                         float2 g2 = mul2(sub2(fma2(nrd, rw, q2), mul2(cd[h], cl)), it);
                         if (!full && col + 3 >= l2) {
