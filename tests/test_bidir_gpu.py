@@ -74,6 +74,12 @@ CASES = [
     (5, 3, 64, 0.5, None),
     (4, 37, 256, 0.2, [[37, 256], [30, 200], [1, 8], [0, 0]]),
     (300, 16, 96, 0.3, None),
+    # full-width rows without per-element masks at each row width the sweeps
+    # specialise (128, 512 columns: one warp per row; 1024: two), odd row
+    # counts so blocks end part-filled
+    (2, 50, 128, 0.5, None),
+    (3, 41, 512, 0.2, None),
+    (2, 23, 1024, 0.05, [[23, 1024], [22, 1024]]),
 ]
 
 
