@@ -31,11 +31,13 @@
 // one exponential, exp(2v - rmax - cmax), with the same expression; the
 // gradient sweep needs row and col apart and forms row * col from them
 // (within a few ulp of the other form).  Element pairs go through the packed
-// f32x2 instructions (half the issue slots of scalar FP32 code).  Each sweep reads its inputs once (the output sweeps re-read sim:
-// 1.5x / 1.67x the compulsory bytes of the two directions) and runs at
-// streaming bandwidth instead of holding whole problems in flight.  The
-// second sweep of a direction is a programmatic dependent launch: it sets up
-// and starts copying sim while the first finishes.
+// f32x2 instructions (half the issue slots of scalar FP32 code); full-width
+// rows (l2 == L2 == 128 * VPL) take a path without per-element masks.  Each
+// sweep reads its inputs once (the second sweep of a direction re-reads sim,
+// and grad_out: 1.5x / 1.67x the compulsory bytes of the two directions) and
+// runs at streaming bandwidth instead of holding whole problems in flight.
+// The second sweep of a direction is a programmatic dependent launch: it sets
+// up and starts copying sim while the first finishes.
 #include <cuda_bf16.h>
 
 #include <algorithm>
