@@ -290,6 +290,14 @@ __device__ __forceinline__ Ring ring_start(const SweepArgs& a, uint64_t* bars, u
     return r;
 }
 
+// Wait (bounded) for the copies of positions [k0, k1) (clipped to the range),
+// then the CTA may return.
+__device__ __forceinline__ void ring_drain_span(const Ring& r, int k0, int k1) {
+    if (threadIdx.x == 0)
+        for (int k = k0; k < r.g1 && k < k1; ++k) r.wait(k);
+    __syncthreads();
+}
+
 // After a failed wait at block g: wait (bounded) for the copies still in flight.
 __device__ __forceinline__ void ring_drain(const Ring& r, int g) {
     if (threadIdx.x == 0)
@@ -306,18 +314,39 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
     constexpr int WPR = W::WPR, VPLW = W::VPLW, NP = W::NP, SLOTS = W::SLOTS;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kS];
-    __shared__ float2 s_rp[kMaxR][WPR];   // per-row (max, sum) of the row's warps
-    __shared__ int s_flag, s_nfix;
+    __shared__ float2 s_rp[2][kMaxR][WPR];   // per-row (max, sum) of the row's warps, two blocks
+    __shared__ int s_flag, s_nfix, s_abort;
     __shared__ int s_fix[kMaxL2];
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
-    if (tid == 0) s_nfix = 0;
+    if (tid == 0) {
+        s_nfix = 0;
+        s_abort = 0;
+    }
     pdl_launch_dependents();   // the second sweep may start its copies of the read-only input
     const Ring rg = ring_start(a, bars, smem);
     const T* simT = reinterpret_cast<const T*>(a.sim);
+    // row statistics of a block from its warps' partials (threads < rows)
+    auto write_rstat = [&](int buf, int bb, int jbb, int rws, int64_t ll1, int64_t ll2) {
+        if (tid < rws) {
+            const int64_t i = int64_t(jbb) * a.R + tid;
+            float2 st = make_float2(0.0f, 0.0f);
+            if (i < ll1 && ll2 > 0) {
+                float mm = kNegBig, ss = 0.0f;
+#pragma unroll
+                for (int c = 0; c < WPR; ++c) lse_merge(mm, ss, s_rp[buf][tid][c].x, s_rp[buf][tid][c].y);
+                st = make_float2(mm, ss > 0.0f ? 1.0f / ss : 0.0f);
+            }
+            a.rstat[int64_t(bb) * L1 + i] = st;
+        }
+    };
+    // the previous block's row statistics are written after the next
+    // barrier; such a block is never a problem's last, so it is the full
+    // block jb - 1 of the current problem
+    bool pend = false;
 
     float2 Sc[NP];   // column sums of exp(v - A), this lane's columns in pairs
     float A = kNegBig;
@@ -345,11 +374,21 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
             A = kNegBig;
         }
         const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
-        const bool ok = rg.wait(g);
-        if (!__syncthreads_and(ok)) {
-            ring_drain(rg, g);
+        const int pb = (g - rg.g0) & 1;
+        // One barrier per block: the previous block's rows are done, so its
+        // stage is refilled and its row statistics written here; a failed
+        // copy wait (recorded in s_abort, the rows below then read stale
+        // but in-bounds shared memory) ends the CTA at the next barrier.
+        __syncthreads();
+        if (s_abort) {
+            ring_drain_span(rg, g - 1, g - 1 + kS);
             return;
         }
+        if (g > rg.g0) {
+            if (tid == 0 && g - 1 + kS < rg.g1) rg.issue(g - 1 + kS);
+            if (pend) write_rstat(pb ^ 1, b, jb - 1, a.R, l1, l2);
+        }
+        if (!rg.wait(g)) s_abort = 1;
         const T* xs = reinterpret_cast<const T*>(rg.stage(g));
         const bool fullw = wide && l2 == L2;
         // The row's exponentials, sums and column weights: a row whose warp
@@ -402,15 +441,15 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
                 accumulate(t0, m0, cr0);
                 accumulate(t1, m1, cr1);
                 if (lane == 0) {
-                    s_rp[il][cpart] = make_float2(m0 == -INFINITY ? kNegBig : m0, s0);
-                    s_rp[il + SLOTS][cpart] = make_float2(m1 == -INFINITY ? kNegBig : m1, s1);
+                    s_rp[pb][il][cpart] = make_float2(m0 == -INFINITY ? kNegBig : m0, s0);
+                    s_rp[pb][il + SLOTS][cpart] = make_float2(m1 == -INFINITY ? kNegBig : m1, s1);
                 }
             }
         }
         for (; il < rows; il += SLOTS) {
             const int64_t i = int64_t(jb) * a.R + il;
             if (i >= l1 || l2 == 0) {
-                if (lane == 0) s_rp[il][cpart] = make_float2(kNegBig, 0.0f);
+                if (lane == 0) s_rp[pb][il][cpart] = make_float2(kNegBig, 0.0f);
                 continue;
             }
             float2 t[NP];
@@ -422,23 +461,14 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
             const float2 u = tree_sum2(t);
             const float s = mx == -INFINITY ? 0.0f : warp_sum<32>(u.x + u.y) * ex2(-cr);
             accumulate(t, mx, cr);
-            if (lane == 0) s_rp[il][cpart] = make_float2(mx == -INFINITY ? kNegBig : mx, s);
+            if (lane == 0) s_rp[pb][il][cpart] = make_float2(mx == -INFINITY ? kNegBig : mx, s);
         }
-        __syncthreads();   // the stage is free; s_rp is complete
-        if (tid < rows) {
-            const int64_t i = int64_t(jb) * a.R + tid;
-            float2 st = make_float2(0.0f, 0.0f);
-            if (i < l1 && l2 > 0) {
-                float mm = kNegBig, ss = 0.0f;
-#pragma unroll
-                for (int c = 0; c < WPR; ++c) lse_merge(mm, ss, s_rp[tid][c].x, s_rp[tid][c].y);
-                st = make_float2(mm, ss > 0.0f ? 1.0f / ss : 0.0f);
-            }
-            a.rstat[int64_t(b) * L1 + i] = st;
-        }
-
-        if (g + 1 == rg.g1 || jb + 1 == a.s.nblk) {
-            // ---- end of this CTA's part of problem b: publish its column partials ----
+        pend = !(g + 1 == rg.g1 || jb + 1 == a.s.nblk);
+        if (!pend) {
+            // ---- end of this CTA's part of problem b: publish its column partials
+            // (the next block's barrier orders the merge buffer before the refill) ----
+            __syncthreads();   // the stage is free; s_rp is complete
+            write_rstat(pb, b, jb, rows, l1, l2);
             const int kfirst = sched_owner(a.s, b * a.s.nblk);
             const int nseg = sched_owner(a.s, (b + 1) * a.s.nblk - 1) - kfirst + 1;
             const int seg = int(blockIdx.x) - kfirst;
@@ -492,14 +522,16 @@ __global__ void __launch_bounds__(kT, 3) bs2_stats_kernel(SweepArgs a) {
                 if (tid == 0) s_nfix = 0;
             }
             fence_proxy_async_smem();   // merge-buffer writes before the stage is refilled by a bulk copy
-            __syncthreads();
         }
-        if (tid == 0 && g + kS < rg.g1) rg.issue(g + kS);
         if (++jb == a.s.nblk) {
             jb = 0;
             ++b;
         }
     }
+    // the range always ends with a problem end (nothing pending); a failed
+    // wait in the last block leaves its copy to be drained
+    __syncthreads();
+    if (s_abort) ring_drain_span(rg, rg.g1 - 1, rg.g1);
 }
 
 // ---------------------------------------------------------------------------
@@ -593,15 +625,26 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     __shared__ __align__(8) uint64_t bars[kS];
     __shared__ __align__(16) float s_cm[kMaxL2];   // the problem's columns: cmax * log2 e
     __shared__ __align__(16) float s_ci[kMaxL2];   // and 1/sum
-    __shared__ float s_rd[kMaxR][WPR];               // per-row q sums of the row's warps
-    __shared__ int s_flag;
+    __shared__ float s_rd[2][kMaxR][WPR];            // per-row q sums of the row's warps, two blocks
+    __shared__ int s_flag, s_abort;
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int slot = wid / WPR, cpart = wid % WPR;
     const int cbase = cpart * 128 * VPLW;
     const int64_t L1 = a.L1, L2 = a.L2;
+    if (tid == 0) s_abort = 0;
     pdl_launch_dependents();   // the second sweep may start its copies of the read-only input
     const Ring rg = ring_start(a, bars, smem);
+    // rdot of a block's rows from its warps' partials (threads < rows)
+    auto write_rdot = [&](int buf, int bb, int jbb, int rws) {
+        if (tid < rws) {
+            float rd = 0.0f;
+#pragma unroll
+            for (int c = 0; c < WPR; ++c) rd += s_rd[buf][tid][c];
+            a.rdot[int64_t(bb) * L1 + int64_t(jbb) * a.R + tid] = rd;
+        }
+    };
+    bool pend = false;   // the previous (full, same-problem) block's rdot, written after the next barrier
 
     float2 Sd[NP];   // column sums of q, this lane's columns in pairs
     const bool wide = L2 == 128 * VPL;
@@ -610,7 +653,19 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
     int cur = -1;
 
     for (int g = rg.g0; g < rg.g1; ++g) {
-        if (b != cur) {   // the barrier below orders these writes before their reads
+        const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
+        const int pb = (g - rg.g0) & 1;
+        // One barrier per block, as in the statistics sweep.
+        __syncthreads();
+        if (s_abort) {
+            ring_drain_span(rg, g - 1, g - 1 + kS);
+            return;
+        }
+        if (g > rg.g0) {
+            if (tid == 0 && g - 1 + kS < rg.g1) rg.issue(g - 1 + kS);
+            if (pend) write_rdot(pb ^ 1, b, jb - 1, a.R);
+        }
+        if (b != cur) {   // no warp reads s_cm / s_ci between the barriers around these writes
             cur = b;
             window(a.lengths, b, L1, L2, l1, l2);
             for (int64_t col = tid; col < L2; col += kT) {
@@ -620,13 +675,9 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
             }
 #pragma unroll
             for (int k = 0; k < NP; ++k) Sd[k] = make_float2(0.0f, 0.0f);
+            __syncthreads();
         }
-        const int rows = int(min(int64_t(a.R), L1 - int64_t(jb) * a.R));
-        const bool ok = rg.wait(g);
-        if (!__syncthreads_and(ok)) {
-            ring_drain(rg, g);
-            return;
-        }
+        if (!rg.wait(g)) s_abort = 1;
         const T* xs = reinterpret_cast<const T*>(rg.stage(g));
         const float* gs = reinterpret_cast<const float*>(rg.stage(g) + a.gout_off);
         for (int il = slot; il < rows; il += SLOTS) {
@@ -666,17 +717,12 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
                 rd = rd2.x + rd2.y;
                 rd = warp_sum<32>(rd);
             }
-            if (lane == 0) s_rd[il][cpart] = rd;
+            if (lane == 0) s_rd[pb][il][cpart] = rd;
         }
-        __syncthreads();   // the stage is free; s_rd is complete
-        if (tid < rows) {
-            float rd = 0.0f;
-#pragma unroll
-            for (int c = 0; c < WPR; ++c) rd += s_rd[tid][c];
-            a.rdot[int64_t(b) * L1 + int64_t(jb) * a.R + tid] = rd;
-        }
-
-        if (g + 1 == rg.g1 || jb + 1 == a.s.nblk) {
+        pend = !(g + 1 == rg.g1 || jb + 1 == a.s.nblk);
+        if (!pend) {
+            __syncthreads();   // the stage is free; s_rd is complete
+            write_rdot(pb, b, jb, rows);
             const int kfirst = sched_owner(a.s, b * a.s.nblk);
             const int nseg = sched_owner(a.s, (b + 1) * a.s.nblk - 1) - kfirst + 1;
             const int seg = int(blockIdx.x) - kfirst;
@@ -710,15 +756,15 @@ __global__ void __launch_bounds__(kT, 3) bs2_dots_kernel(SweepArgs a) {
                 }
                 if (tid == 0) a.cnt[b] = 0;
             }
-            fence_proxy_async_smem();
-            __syncthreads();
+            fence_proxy_async_smem();   // merge-buffer writes before the next barrier and the refill
         }
-        if (tid == 0 && g + kS < rg.g1) rg.issue(g + kS);
         if (++jb == a.s.nblk) {
             jb = 0;
             ++b;
         }
     }
+    __syncthreads();
+    if (s_abort) ring_drain_span(rg, rg.g1 - 1, rg.g1);
 }
 
 // ---------------------------------------------------------------------------
